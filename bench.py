@@ -1,0 +1,482 @@
+#!/usr/bin/env python
+"""Benchmark of the Qwen3 GQA attention block on B200.
+
+Headline workload: full-depth decode attention for
+one new token, 36 layers x (32 q heads, 8 KV heads, head_dim 128), KV length
+8192 (new token at position 8191), fp32 cache.  One step = the 36 layer calls
+of q3a_attn_layer (QK-norm + RoPE + KV append + attention, one kernel each).
+`value` is HBM GB/s of algorithmic bytes with everything resident in HBM;
+`us_per_layer` is the same measurement as time per layer.  `e2e` is the same
+metric through the host-pointer C-ABI (q, k, v, norm gains copied in from
+pinned memory and xb, q, k copied out, every layer, synchronously).
+
+Extra keys: `bf16` (the bf16-cache variant), `prefill` (configs[2]: causal
+prefill of 2048 tokens, TFLOP/s of the dense contraction).
+
+--impl reference times the reference's own CPU code (oracle/_ref, compiled
+from the reference sources: launch_attn with OpenMP over heads, plus its
+rmsnorm_head / rope / kv write) on the same metric, or the oracle port when
+the reference library is absent.
+
+Multi-GPU: one process per GPU (torchrun); every rank decodes its own
+sequence (weak scaling, no data-path collective), value = all ranks' bytes /
+max-over-ranks time.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "qwen3.c_b200"))
+
+HQ, HKV, HD = 32, 8, 128
+KV_DIM = HKV * HD
+N_LAYERS = 36
+L_CTX = 8192
+POS = L_CTX - 1
+METRIC = "decode attn µs/layer + HBM GB/s (KV 8K); prefill attn TFLOP/s (2K tok)"
+PREFILL_S = 2048
+
+
+def algo_bytes_per_layer(esize: int) -> int:
+    """Bytes the block must move per layer: K and V rows 0..L-2 read from the
+    cache, the new K/V row written, and the fp32 vectors (q in/out, xb out,
+    k in/out, v in, two norm gains)."""
+    cache = 2 * (L_CTX - 1) * KV_DIM * esize + 2 * KV_DIM * esize
+    vecs = 3 * HQ * HD * 4 + 3 * KV_DIM * 4 + 2 * HD * 4
+    return cache + vecs
+
+
+def prefill_flops(S: int = PREFILL_S) -> float:
+    return 4.0 * HD * HQ * S * (S + 1) / 2.0
+
+
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return d.get("hbm_gbs", 6650.0), d.get("bf16_tflops", 1590.0), \
+            d.get("bf16_tflops_sustained", 1400.0), "measured"
+    return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+def profile_traffic(name: str):
+    """Per-launch DRAM bytes of a kernel from a committed ncu summary."""
+    p = os.path.join(ROOT, "profiles", "traffic.json")
+    if not os.path.exists(p):
+        return None
+    with open(p) as f:
+        return json.load(f).get(name)
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
+               0x2: "applications_clocks_setting", 0x1: "gpu_idle"}
+
+    def __init__(self, torch_dev: int, period_s: float = 0.005):
+        self.samples = []
+        self.reasons = set()
+        self.max_mhz = None
+        self.period = period_s
+        self._stop = threading.Event()
+        self.h = None
+        try:
+            import pynvml
+            import torch
+            pynvml.nvmlInit()
+            uuid = str(torch.cuda.get_device_properties(torch_dev).uuid)
+            if not uuid.startswith("GPU-"):
+                uuid = "GPU-" + uuid
+            self.h = pynvml.nvmlDeviceGetHandleByUUID(uuid)
+            self.nv = pynvml
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+        except Exception as e:  # clocks are reported as unavailable
+            self.err = repr(e)
+
+    def _run(self):
+        nv = self.nv
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
+                r = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                for bit, name in self.REASONS.items():
+                    if r & bit:
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self.h is not None:
+            self.t = threading.Thread(target=self._run, daemon=True)
+            self.t.start()
+        return self
+
+    def __exit__(self, *a):
+        if self.h is not None:
+            self._stop.set()
+            self.t.join()
+
+    def report(self):
+        if self.h is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "note": "nvml unavailable"}
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
+                "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons - {"gpu_idle"}),
+                "samples": len(self.samples)}
+
+
+# ------------------------------------------------------------------ dist
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def max_over_ranks(x: float, world: int, dev) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+# ------------------------------------------------------------------ our arm
+def fill_cache(ctx, torch, dev, seed, n_layers, pos, stream):
+    """Layer l: k_t, v_t ~ N(0,1) (streams l*16+1, l*16+2), k normed and
+    rotated at t by the library's own append kernel, rows 0..pos-1."""
+    import q3attn
+    kraw = torch.empty(pos * KV_DIM, device=dev)
+    vraw = torch.empty(pos * KV_DIM, device=dev)
+    ones = torch.ones(HD, device=dev)
+    for l in range(n_layers):
+        ctx.randn(kraw, q3attn.OUT_F32, kraw.numel(), seed, l * 16 + 1)
+        ctx.randn(vraw, q3attn.OUT_F32, vraw.numel(), seed, l * 16 + 2)
+        ctx.kv_append(0, l, 0, pos, kraw, vraw, ones)
+    stream.synchronize()
+
+
+def decode_run(args, torch, dev, local, kv_dtype, seed, world, with_e2e, with_cpu):
+    import q3attn
+    esize = 4 if kv_dtype == q3attn.KV_F32 else 2
+    stream = torch.cuda.Stream(device=dev)
+    ctx = q3attn.Context(n_layers=N_LAYERS, max_seq=L_CTX, kv_dtype=kv_dtype,
+                         ptr_mode=q3attn.PTR_DEVICE, device=local)
+    ctx.set_stream(stream.cuda_stream)
+    fill_cache(ctx, torch, dev, seed, N_LAYERS, POS, stream)
+    # per-layer new-token inputs (raw projections), streams l*16+3/4/5
+    q_raw = torch.empty(N_LAYERS, HQ * HD, device=dev)
+    k_raw = torch.empty(N_LAYERS, KV_DIM, device=dev)
+    v_in = torch.empty(N_LAYERS, KV_DIM, device=dev)
+    for l in range(N_LAYERS):
+        ctx.randn(q_raw[l], q3attn.OUT_F32, HQ * HD, seed, l * 16 + 3)
+        ctx.randn(k_raw[l], q3attn.OUT_F32, KV_DIM, seed, l * 16 + 4)
+        ctx.randn(v_in[l], q3attn.OUT_F32, KV_DIM, seed, l * 16 + 5)
+    qw = torch.ones(HD, device=dev)
+    kw = torch.ones(HD, device=dev)
+    q_w = q_raw.clone()
+    k_w = k_raw.clone()
+    xb = torch.zeros(N_LAYERS, HQ * HD, device=dev)
+    stream.synchronize()
+
+    def step(evs=None):
+        # the block rewrites q and k in place (as the reference does): restore
+        q_w.copy_(q_raw)
+        k_w.copy_(k_raw)
+        for l in range(N_LAYERS):
+            if evs is not None:
+                evs[2 * l].record(stream)
+            ctx.attn_layer(xb[l], q_w[l], k_w[l], v_in[l], qw, kw, l, POS)
+            if evs is not None:
+                evs[2 * l + 1].record(stream)
+
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            step()
+    stream.synchronize()
+    ctx.check_device_error()
+
+    # capture the whole timed region (K steps) as one graph with external
+    # CUDA events around every kernel
+    K = args.steps
+    evs = [[torch.cuda.Event(enable_timing=True, external=True) for _ in range(2 * N_LAYERS)]
+           for _ in range(K)]
+    e0 = torch.cuda.Event(enable_timing=True, external=True)
+    e1 = torch.cuda.Event(enable_timing=True, external=True)
+    g = torch.cuda.CUDAGraph()
+    n0 = ctx.launch_count()
+    with torch.cuda.graph(g, stream=stream):
+        e0.record(stream)
+        for kk in range(K):
+            step(evs[kk])
+        e1.record(stream)
+    launches = ctx.launch_count() - n0
+    g.replay()  # untimed replay (instantiation, first-touch)
+    stream.synchronize()
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    with ClockSampler(local) as cs:
+        g.replay()
+        stream.synchronize()
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    ctx.check_device_error()
+    t_ms = e0.elapsed_time(e1)
+    per_launch = [evs[kk][2 * l].elapsed_time(evs[kk][2 * l + 1])
+                  for kk in range(K) for l in range(N_LAYERS)]
+    res = {"t_ms": t_ms, "kernel_us": 1000.0 * statistics.mean(per_launch),
+           "kernel_us_median": 1000.0 * statistics.median(per_launch),
+           "launches": launches, "clocks": cs.report(),
+           "bytes_per_layer": algo_bytes_per_layer(esize), "esize": esize}
+    del g
+
+    if with_e2e:
+        res["e2e"] = e2e_run(args, torch, dev, local, kv_dtype, seed, q_raw, k_raw, v_in, ctx,
+                             stream)
+    ctx.close()
+    return res
+
+
+def e2e_run(args, torch, dev, local, kv_dtype, seed, q_raw, k_raw, v_in, dctx, stream):
+    """Same step through the host-pointer API: every layer copies its inputs
+    in from host memory and its result out, synchronously."""
+    import numpy as np
+    import q3attn
+    hctx = q3attn.Context(n_layers=N_LAYERS, max_seq=L_CTX, kv_dtype=kv_dtype,
+                          ptr_mode=q3attn.PTR_HOST, device=local)
+    # same cache contents: generate on device, copy through host
+    kraw = torch.empty(POS * KV_DIM, device=dev)
+    vraw = torch.empty(POS * KV_DIM, device=dev)
+    kh = torch.empty(POS * KV_DIM, pin_memory=True)
+    vh = torch.empty(POS * KV_DIM, pin_memory=True)
+    ones = np.ones(HD, np.float32)
+    for l in range(N_LAYERS):
+        dctx.randn(kraw, q3attn.OUT_F32, kraw.numel(), seed, l * 16 + 1)
+        dctx.randn(vraw, q3attn.OUT_F32, vraw.numel(), seed, l * 16 + 2)
+        stream.synchronize()
+        kh.copy_(kraw)
+        vh.copy_(vraw)
+        hctx.kv_append(0, l, 0, POS, kh.numpy(), vh.numpy(), ones)
+    qh = q_raw.cpu().numpy()
+    khr = k_raw.cpu().numpy()
+    vhh = v_in.cpu().numpy()
+    qbuf = np.empty(HQ * HD, np.float32)
+    kbuf = np.empty(KV_DIM, np.float32)
+    xbh = np.zeros((N_LAYERS, HQ * HD), np.float32)
+    n0 = hctx.launch_count()
+
+    def step():
+        for l in range(N_LAYERS):
+            np.copyto(qbuf, qh[l])
+            np.copyto(kbuf, khr[l])
+            hctx.attn_layer(xbh[l], qbuf, kbuf, vhh[l], ones, ones, l, POS)
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    K = args.steps
+    t0 = time.perf_counter()
+    for _ in range(K):
+        step()
+    t1 = time.perf_counter()
+    hctx.check_device_error()
+    launches = hctx.launch_count() - n0 - max(3, args.warmup) * N_LAYERS
+    hctx.close()
+    h2d = N_LAYERS * (HQ * HD * 4 + 2 * KV_DIM * 4 + 2 * HD * 4)
+    d2h = N_LAYERS * (2 * HQ * HD * 4 + KV_DIM * 4)
+    return {"t_ms": (t1 - t0) * 1000.0, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "launches": launches}
+
+
+# ------------------------------------------------------------------ CPU reference
+def cpu_reference_sample(n_calls_max: int, budget_s: float, n_layers_sample: int = 4):
+    """Times the reference's own CPU block (oracle/_ref, or the oracle port)
+    on `n_layers_sample` distinct layer caches at KV 8192, fp32."""
+    import ctypes
+    import numpy as np
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import q3a_oracle as orc
+    use_ref = orc.ref_available()
+    kind = "reference" if use_ref else "port"
+    caches = []
+    for l in range(n_layers_sample):
+        kc, vc, _, _ = orc.make_cache(1234, l, POS, HKV, HD, L_CTX)
+        caches.append((kc, vc))
+    q0 = [orc.randn(HQ * HD, 1234, l * 16 + 3) for l in range(n_layers_sample)]
+    k0 = [orc.randn(KV_DIM, 1234, l * 16 + 4) for l in range(n_layers_sample)]
+    v0 = [orc.randn(KV_DIM, 1234, l * 16 + 5) for l in range(n_layers_sample)]
+    w = np.ones(HD, np.float32)
+    att = np.zeros(HQ * L_CTX, np.float32)
+    xb = np.zeros(HQ * HD, np.float32)
+    P = orc._ptr
+    if use_ref:
+        R = orc.ref()
+
+        def block(l):
+            q = q0[l].copy()
+            k = k0[l].copy()
+            kc, vc = caches[l]
+            R.q3ref_rmsnorm_head(P(q), P(w), HQ, HD, 1e-6)
+            R.q3ref_rmsnorm_head(P(k), P(w), HKV, HD, 1e-6)
+            R.q3ref_rope(P(q), HQ, HD, POS, 5e6)
+            R.q3ref_rope(P(k), HKV, HD, POS, 5e6)
+            off = POS * KV_DIM * 4
+            R.q3ref_launch_kv_write(P(k), P(v0[l]), ctypes.c_void_p(kc.ctypes.data + off),
+                                    ctypes.c_void_p(vc.ctypes.data + off), KV_DIM)
+            R.q3ref_launch_attn(P(xb), P(q), P(kc), P(vc), P(att), 0, POS, HQ, HQ // HKV, HD,
+                                KV_DIM, L_CTX)
+    else:
+        def block(l):
+            q = q0[l].copy()
+            k = k0[l].copy()
+            kc, vc = caches[l]
+            orc.attn_block(q, k, v0[l], w, w, kc, vc, 0, POS, HQ, HKV, HD, L_CTX)
+    block(0)  # warm
+    calls = 0
+    t0 = time.perf_counter()
+    while calls < n_calls_max and (time.perf_counter() - t0) < budget_s:
+        block(calls % n_layers_sample)
+        calls += 1
+    dt = time.perf_counter() - t0
+    bytes_ = calls * algo_bytes_per_layer(4)
+    threads = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
+    return {"value": bytes_ / dt / 1e9, "unit": "GB/s", "cores": min(threads, HQ), "kind": kind,
+            "us_per_layer": dt / calls * 1e6, "calls": calls,
+            "sample": f"{calls} layer calls of the fp32 block at KV 8192 cycling "
+                      f"{n_layers_sample} distinct layer caches (OpenMP over the 32 heads, "
+                      f"{threads} threads available)"}
+
+
+def run_reference(args, world, rank):
+    if rank != 0:
+        return
+    # one step = one full-depth pass sample: 4 layer calls on distinct caches
+    n_per_step = 4
+    cpu = cpu_reference_sample(n_calls_max=n_per_step * (args.steps + args.warmup),
+                               budget_s=1e9, n_layers_sample=n_per_step)
+    us = cpu["us_per_layer"]
+    line = {"metric": METRIC, "value": cpu["value"], "unit": "GB/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": us * N_LAYERS / 1000.0, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": config_dict(args, "f32"), "impl": "reference",
+            "us_per_layer": us,
+            "cpu_baseline": {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            "e2e": {"value": cpu["value"], "unit": "GB/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0},
+            "note": "step = 4 reference block calls (rmsnorm_head, rope, kv write, launch_attn) "
+                    "on distinct layer caches; ms_per_step scaled to 36 layers"}
+    print(json.dumps(line), flush=True)
+
+
+def config_dict(args, dtype):
+    return {"workload": "configs[1]: full-depth decode attention, 36 layers, KV 8192 "
+                        f"(new token at pos 8191), {dtype} cache, batch 1 per GPU",
+            "model": "Qwen3-8B GQA attention block (Hq=32, Hkv=8, d=128)",
+            "global_batch": args.gpus, "seq_len": L_CTX,
+            "parallelism": f"replicas{args.gpus}" if args.gpus > 1 else "single",
+            "l2": "inputs larger than L2 (36 layer caches cycled per step)"}
+
+
+# ------------------------------------------------------------------ main
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-variants", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    world, rank, local = dist_setup()
+    if args.impl == "reference":
+        run_reference(args, world, rank)
+        return
+
+    import torch
+    dev = torch.device(f"cuda:{local}")
+    torch.cuda.set_device(dev)
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+    import q3attn
+    seed = 1234 + 7919 * rank
+    hbm_peak, tf_peak, tf_sus, peak_src = measured_peaks()
+
+    main_res = decode_run(args, torch, dev, local, q3attn.KV_F32, seed, world,
+                          with_e2e=not args.no_e2e, with_cpu=False)
+    t_max = max_over_ranks(main_res["t_ms"], world, dev)
+    bpl = main_res["bytes_per_layer"]
+    K = args.steps
+    value = world * K * N_LAYERS * bpl / (t_max / 1000.0) / 1e9
+    us_per_layer = t_max * 1000.0 / (K * N_LAYERS)
+    kern_us = main_res["kernel_us"]
+    achieved = bpl / (kern_us * 1e-6) / 1e9
+    traffic = profile_traffic("decode_f32_8k")
+    line = {"metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": K,
+            "warmup": args.warmup, "ms_per_step": t_max / K, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": config_dict(args, "f32"), "us_per_layer": us_per_layer,
+            "gpu_launches": main_res["launches"], "clocks": main_res["clocks"],
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                         "frac": achieved / hbm_peak, "traffic": traffic,
+                         "kernel": "q3a::decode_kernel<float>",
+                         "kernel_us_mean": kern_us,
+                         "kernel_us_median": main_res["kernel_us_median"],
+                         "peak_source": f"{peak_src} hbm_gbs (MEASURED_PEAKS.json)",
+                         "algorithmic_bytes_per_launch": bpl}}
+    if "e2e" in main_res:
+        e = main_res["e2e"]
+        t_e = max_over_ranks(e["t_ms"], world, dev)
+        line["e2e"] = {"value": world * K * N_LAYERS * bpl / (t_e / 1000.0) / 1e9, "unit": "GB/s",
+                       "h2d_bytes_per_step": e["h2d_bytes_per_step"],
+                       "d2h_bytes_per_step": e["d2h_bytes_per_step"],
+                       "us_per_layer": t_e * 1000.0 / (K * N_LAYERS),
+                       "api": "q3a_attn_layer, host pointers, synchronous per layer",
+                       "timer": "host perf_counter around K steps"}
+    if not args.no_variants:
+        b = decode_run(args, torch, dev, local, q3attn.KV_BF16, seed, world, with_e2e=False,
+                       with_cpu=False)
+        tb = max_over_ranks(b["t_ms"], world, dev)
+        bb = b["bytes_per_layer"]
+        ach_b = bb / (b["kernel_us"] * 1e-6) / 1e9
+        line["bf16"] = {"value": world * K * N_LAYERS * bb / (tb / 1000.0) / 1e9, "unit": "GB/s",
+                        "us_per_layer": tb * 1000.0 / (K * N_LAYERS),
+                        "kernel_us_mean": b["kernel_us"], "achieved": ach_b,
+                        "frac": ach_b / hbm_peak, "clocks": b["clocks"],
+                        "gpu_launches": b["launches"]}
+        line["gpu_launches"] += b["launches"]
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = cpu_reference_sample(n_calls_max=400, budget_s=15.0)
+        line["cpu_baseline"] = {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")}
+        line["cpu_baseline"]["us_per_layer"] = cpu["us_per_layer"]
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,192 @@
+/*
+ * q3attn.h -- C ABI of the B200 (sm_100a) grouped-query attention block of
+ * Qwen3.c (Qwen3-VL-8B text decoder: 32 query heads share 8 KV heads,
+ * head_dim 128).
+ *
+ * The reference (thamada/Qwen3.c) has no exported API: the block lives inline
+ * in forward() (qwen3-8b/cpu/main.c:1319-1353, qwen3-8b/cpu-multicore/main.c:
+ * 1331-1369, qwen3-8b/gpu/main.c:2093-2126) and works on the run-state
+ * buffers of `State` (qwen3-8b/cpu/main.c:646-650): q, k, v, att, xb and the
+ * caches kc, vc.  The entry points below take those same buffers, so a C host
+ * replaces that block by one call.  Conventions:
+ *   - every call returns Q3A_OK (0) or an error code; nothing calls exit()
+ *     (the reference's HIPCHK exits, qwen3-8b/gpu/main.c:47-53); the message
+ *     of the last failure on the calling thread is q3a_last_error();
+ *   - one host thread per context; work is ordered on the context's stream;
+ *   - pointer mode (q3a_cfg.ptr_mode): Q3A_PTR_HOST takes host pointers, like
+ *     the CPU forward(), and returns after the result is in host memory;
+ *     Q3A_PTR_DEVICE takes device pointers, like forward_gpu()'s device
+ *     `State` (qwen3-8b/gpu/main.c:1287-1323), and returns once the work is
+ *     queued on the stream.
+ * Only head_dim 128 with 4 query heads per KV head is implemented (the
+ * Qwen3-8B shape, qwen3-8b/gpu/main.c:8-10); other shapes return
+ * Q3A_ERR_UNSUPPORTED.
+ */
+#ifndef Q3ATTN_H
+#define Q3ATTN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define Q3A_OK 0
+#define Q3A_ERR_INVALID 1      /* bad argument, shape or position */
+#define Q3A_ERR_CUDA 2         /* CUDA runtime / driver error */
+#define Q3A_ERR_OOM 3          /* device or pinned allocation failed */
+#define Q3A_ERR_UNSUPPORTED 4  /* shape outside the implemented set */
+#define Q3A_ERR_TIMEOUT 5      /* a bounded device-side wait expired */
+
+#define Q3A_KV_F32 0           /* fp32 cache (the reference's layout dtype) */
+#define Q3A_KV_BF16 1          /* bf16 cache, round-to-nearest-even on append */
+
+#define Q3A_PTR_HOST 0
+#define Q3A_PTR_DEVICE 1
+
+#define Q3A_OUT_F32 0
+#define Q3A_OUT_BF16 1
+
+#define Q3A_MAX_BATCH 256      /* sequences per batched call */
+
+/* Shape and placement of one context.  Fields follow Config
+ * (qwen3-8b/cpu/main.c:603-607) and the defaults parse_gguf applies
+ * (qwen3-8b/cpu/main.c:874-876, 938-941). */
+typedef struct q3a_cfg {
+    int n_layers;       /* Config.n_layers (36) */
+    int n_heads;        /* Config.n_heads (32) */
+    int n_kv_heads;     /* Config.n_kv_heads (8) */
+    int head_dim;       /* Config.head_dim (128) */
+    int max_seq;        /* Config.max_seq: cache positions per sequence */
+    int n_seqs;         /* sequences (cache slots) held; 1 for the reference */
+    int kv_dtype;       /* Q3A_KV_F32 or Q3A_KV_BF16 */
+    int page_tokens;    /* tokens per cache page, multiple of 64 (0: 64) */
+    int ptr_mode;       /* Q3A_PTR_HOST or Q3A_PTR_DEVICE */
+    int device;         /* CUDA device ordinal */
+    float norm_eps;     /* Config.norm_eps (1e-6) */
+    float rope_theta;   /* Config.rope_theta (5e6) */
+    int kv_head_begin;  /* first KV head held (KV-head sharding); 0 */
+    int kv_head_count;  /* KV heads held; 0 means all n_kv_heads */
+} q3a_cfg;
+
+typedef struct q3a_ctx q3a_ctx;
+
+/* Fills cfg with the Qwen3-8B shape: 36 layers, 32/8 heads, head_dim 128,
+ * max_seq 4096, one sequence, fp32 cache, 64-token pages, host pointers,
+ * device 0, eps 1e-6, theta 5e6. */
+void q3a_cfg_default(q3a_cfg *cfg);
+
+/* Allocates the device KV cache ([layer][kv head][page][token][128], pages
+ * 128-byte aligned, zero-filled) and the context's scratch.  Replaces
+ * alloc_state / alloc_state_gpu for the cache (qwen3-8b/cpu/main.c:1134-1148,
+ * qwen3-8b/gpu/main.c:1287-1323); sizes are size_t, so 36 layers x 131072
+ * positions do not overflow as the reference's int kv_cache_len does. */
+int q3a_create(q3a_ctx **ctx, const q3a_cfg *cfg);
+int q3a_destroy(q3a_ctx *ctx);
+
+/* Message of the last failed call on this thread ("" if none). */
+const char *q3a_last_error(void);
+
+/* Sets the CUDA stream (a cudaStream_t) the context queues work on; NULL
+ * selects the context's own stream. */
+int q3a_set_stream(q3a_ctx *ctx, void *cuda_stream);
+int q3a_sync(q3a_ctx *ctx);
+
+/* Reads and clears the device error flag set by bounded waits in the kernels
+ * (Q3A_ERR_TIMEOUT when one expired, else Q3A_OK). */
+int q3a_check_device_error(q3a_ctx *ctx);
+
+/* The whole attention block of one layer for one new token at `pos`
+ * (qwen3-8b/cpu/main.c:1319-1353; HIP: qwen3-8b/gpu/main.c:2093-2126):
+ * per-head QK-RMSNorm of q (n_heads) and k (n_kv_heads) with the layer's
+ * q_norm_w / k_norm_w [head_dim], RoPE at pos, append of k and v to the
+ * context's cache of sequence 0 at pos, then softmax(q.K^T/sqrt(hd)).V over
+ * positions 0..pos into xb.  q and k are normalised and rotated in place as
+ * in the reference.  Buffers: xb, q [n_heads*head_dim]; k, v [n_kv*head_dim]. */
+int q3a_attn_layer(q3a_ctx *ctx, float *xb, float *q, float *k, const float *v,
+                   const float *q_norm_w, const float *k_norm_w, int layer, int pos);
+
+/* Decode attention with the argument list of launch_attn
+ * (qwen3-8b/xdna2/main.c:2724-2727) over a caller-owned position-major cache
+ * kc/vc [layers][max_seq][kv_dim] (fp32): q already normalised and rotated,
+ * position pos already appended.  att is accepted and unused (the reference
+ * GPU build allocates it only for head_dim > 256, qwen3-8b/gpu/main.c:1305).
+ * In host mode the rows 0..pos of layer offset loff are uploaded per call. */
+int q3a_attn_decode(q3a_ctx *ctx, float *xb, const float *q, const float *kc,
+                    const float *vc, float *att, size_t loff, int pos, int n_heads,
+                    int kv_mul, int hd, int kv_dim, int max_seq);
+
+/* Batched ragged decode: n new tokens, token i belongs to cache slot
+ * seq_ids[i] (distinct) at position pos[i] (host arrays).  The block of
+ * q3a_attn_layer runs for each; q, xb are [n][n_heads*hd], k, v
+ * [n][n_kv*hd].  With KV-head sharding (kv_head_count < n_kv_heads) only the
+ * held heads' xb slices are written.  The reference has no batch; this is its
+ * block applied to n independent sequences. */
+int q3a_attn_layer_batched(q3a_ctx *ctx, float *xb, float *q, float *k, const float *v,
+                           const float *q_norm_w, const float *k_norm_w, int layer,
+                           const int *seq_ids, const int *pos, int n);
+
+/* KV append of n consecutive tokens of slot `seq` at positions pos0..:
+ * QK-RMSNorm + RoPE of k (as in the block), then the write of k and v
+ * (qwen3-8b/cpu/main.c:1325-1329; HIP kv_cache_write_kernel
+ * qwen3-8b/gpu/main.c:1447-1467).  k, v are [n][n_kv*hd] raw projections; k is
+ * not modified. */
+int q3a_kv_append(q3a_ctx *ctx, int seq, int layer, int pos0, int n, const float *k,
+                  const float *v, const float *k_norm_w);
+
+/* Writes already-prepared rows (position-major [n][n_kv*hd], fp32) into the
+ * cache at pos0.. without norm or RoPE, converting to the cache dtype. */
+int q3a_kv_load(q3a_ctx *ctx, int seq, int layer, int pos0, int n, const float *k,
+                const float *v);
+
+/* Reads cache rows back as fp32 position-major [n][n_kv*hd]. */
+int q3a_kv_read(q3a_ctx *ctx, int seq, int layer, int pos0, int n, float *k, float *v);
+
+/* Causal prefill of n_tok prompt tokens of slot `seq` at positions
+ * pos0..pos0+n_tok-1: QK-RMSNorm + RoPE of q and k, append of k/v, then for
+ * every prompt row s the attention over positions 0..pos0+s.  This is the
+ * reference's prompt loop (qwen3-8b/cpu/main.c:1481-1499, one forward() per
+ * token) done as one batched causal attention on the tensor cores.
+ * q [n_tok][n_heads*hd] raw (left unmodified), k, v [n_tok][n_kv*hd] raw; out
+ * [n_tok][n_heads*hd] in out_dtype (Q3A_OUT_F32 / Q3A_OUT_BF16).  Requires a
+ * bf16 cache (the tensor-core operands are bf16, softmax and accumulation
+ * fp32). */
+int q3a_prefill(q3a_ctx *ctx, void *out, int out_dtype, const float *q, const float *k,
+                const float *v, const float *q_norm_w, const float *k_norm_w, int seq,
+                int layer, int pos0, int n_tok);
+
+/* Causal attention only, on already-prepared bf16 operands: q_bf16
+ * [n_tok][n_heads][hd] (normed, rotated) over the cache of slot seq, rows
+ * pos0+s attending to 0..pos0+s.  Same output contract as q3a_prefill. */
+int q3a_prefill_attn(q3a_ctx *ctx, void *out, int out_dtype, const void *q_bf16,
+                     int seq, int layer, int pos0, int n_tok);
+
+/* Sequence-sharded decode, step 1: attention of one already-prepared query
+ * q [n_heads*hd] over cache positions [t0, t1) of slot seq (t0 < t1), giving
+ * the chunk's normalised output o [n_heads*hd] and its log-sum-exp lse
+ * [n_heads] in log2 units (log2 sum_t 2^(s_t log2 e), s_t = q.k_t/sqrt(hd)).
+ * Empty chunks (t0 == t1) give o = 0, lse = -inf. */
+int q3a_attn_partial(q3a_ctx *ctx, float *o, float *lse, const float *q, int seq,
+                     int layer, int t0, int t1);
+
+/* Sequence-sharded decode, step 2: merges n_parts chunk results
+ * (o_parts [n_parts][n_heads*hd], lse_parts [n_parts][n_heads]) into xb by
+ * log-sum-exp weights. */
+int q3a_lse_combine(q3a_ctx *ctx, float *xb, const float *o_parts,
+                    const float *lse_parts, int n_parts);
+
+/* Seeded N(0,1) fill of n elements (fp32 or bf16 by out_dtype): element i is
+ * the Box-Muller transform of uniforms u(2j), u(2j+1), j = (offset+i)/2, with
+ * u from a splitmix64-hashed counter passed through the xorshift64* output
+ * step of rng_f32 (qwen3-8b/cpu/main.c:1377-1382).  dst is device memory. */
+int q3a_randn(q3a_ctx *ctx, void *dst, int out_dtype, size_t n, uint64_t seed,
+              uint64_t stream_id, uint64_t offset);
+
+/* Number of kernels the library launched on this context so far. */
+uint64_t q3a_launch_count(const q3a_ctx *ctx);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* Q3ATTN_H */

@@ -1,0 +1,852 @@
+// q3a_api.cu -- the extern "C" entry points of include/q3attn.h.
+//
+// Owns the context: the paged head-major KV cache, its TMA tensor maps, the
+// decode scratch (partials and arrival counters), host<->device staging for
+// host-pointer mode, and the unit schedule the decode kernel consumes.
+#include <math.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <algorithm>
+#include <vector>
+
+#include "q3a_common.cuh"
+#include "q3a_internal.h"
+
+using namespace q3a;
+
+// ------------------------------------------------------------------ errors
+static thread_local char g_err[512] = "";
+
+static int fail(int code, const char* fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_err, sizeof(g_err), fmt, ap);
+    va_end(ap);
+    return code;
+}
+
+#define CUDA_TRY(expr)                                                                  \
+    do {                                                                                \
+        cudaError_t _e = (expr);                                                        \
+        if (_e != cudaSuccess)                                                          \
+            return fail(Q3A_ERR_CUDA, "%s failed: %s (%s:%d)", #expr, cudaGetErrorString(_e), \
+                        __FILE__, __LINE__);                                            \
+    } while (0)
+
+// ------------------------------------------------------------------ tensor maps
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    }
+    return fn;
+}
+
+// 2-D map over a row-major [rows][cols] tensor; box = box_cols x box_rows.
+static int make_map_2d(CUtensorMap* m, const void* base, bool bf16, uint64_t cols, uint64_t rows,
+                       uint32_t box_cols, uint32_t box_rows, CUtensorMapSwizzle sw) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return fail(Q3A_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
+    const size_t es = bf16 ? 2 : 4;
+    cuuint64_t dims[2] = {cols, rows};
+    cuuint64_t strides[1] = {cols * es};
+    cuuint32_t box[2] = {box_cols, box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2,
+                    const_cast<void*>(base), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return fail(Q3A_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d): cols=%llu rows=%llu", (int)r,
+                    (unsigned long long)cols, (unsigned long long)rows);
+    return Q3A_OK;
+}
+
+// ------------------------------------------------------------------ context
+struct q3a_ctx {
+    q3a_cfg cfg;
+    int nkv;              // kv heads held
+    int kv0;
+    int bf16;
+    size_t esize;
+    int pages_per_seq;
+    int n_pages;          // per (layer, kv head)
+    long long total_rows; // cache rows per K (or V) pool
+    void* kcache = nullptr;
+    void* vcache = nullptr;
+    int* page_table = nullptr;
+    float* partials = nullptr;
+    long long part_slots = 0;
+    int* counters = nullptr;
+    int* err = nullptr;
+    cudaStream_t own_stream = nullptr;
+    cudaStream_t stream = nullptr;
+    int num_sms = 148;
+    CUtensorMap tmK, tmV;          // decode maps of the paged cache
+    CUtensorMap tmKp, tmVp;        // prefill maps (bf16, 128B swizzle)
+    float inv_freq[64];
+    // host-mode staging
+    float* h_stage = nullptr;      // pinned
+    float* d_stage = nullptr;
+    size_t stage_floats = 0;
+    // growable device scratch (uploads of caller caches, prefill q)
+    void* d_scratch = nullptr;
+    size_t scratch_bytes = 0;
+    uint64_t launches = 0;
+};
+
+static int ensure_device(const q3a_ctx* c) {
+    int cur = -1;
+    CUDA_TRY(cudaGetDevice(&cur));
+    if (cur != c->cfg.device) CUDA_TRY(cudaSetDevice(c->cfg.device));
+    return Q3A_OK;
+}
+
+static int grow_stage(q3a_ctx* c, size_t floats) {
+    if (floats <= c->stage_floats) return Q3A_OK;
+    if (c->h_stage) cudaFreeHost(c->h_stage);
+    if (c->d_stage) cudaFree(c->d_stage);
+    c->h_stage = nullptr;
+    c->d_stage = nullptr;
+    c->stage_floats = 0;
+    if (cudaMallocHost(&c->h_stage, floats * 4) != cudaSuccess)
+        return fail(Q3A_ERR_OOM, "pinned staging of %zu bytes", floats * 4);
+    if (cudaMalloc(&c->d_stage, floats * 4) != cudaSuccess)
+        return fail(Q3A_ERR_OOM, "device staging of %zu bytes", floats * 4);
+    c->stage_floats = floats;
+    return Q3A_OK;
+}
+
+static int grow_scratch(q3a_ctx* c, size_t bytes) {
+    if (bytes <= c->scratch_bytes) return Q3A_OK;
+    if (c->d_scratch) {
+        cudaStreamSynchronize(c->stream);
+        cudaFree(c->d_scratch);
+    }
+    c->d_scratch = nullptr;
+    c->scratch_bytes = 0;
+    if (cudaMalloc(&c->d_scratch, bytes) != cudaSuccess)
+        return fail(Q3A_ERR_OOM, "device scratch of %zu bytes", bytes);
+    c->scratch_bytes = bytes;
+    return Q3A_OK;
+}
+
+extern "C" void q3a_cfg_default(q3a_cfg* cfg) {
+    memset(cfg, 0, sizeof(*cfg));
+    cfg->n_layers = 36;
+    cfg->n_heads = 32;
+    cfg->n_kv_heads = 8;
+    cfg->head_dim = 128;
+    cfg->max_seq = 4096;
+    cfg->n_seqs = 1;
+    cfg->kv_dtype = Q3A_KV_F32;
+    cfg->page_tokens = 64;
+    cfg->ptr_mode = Q3A_PTR_HOST;
+    cfg->device = 0;
+    cfg->norm_eps = 1e-6f;
+    cfg->rope_theta = 5e6f;
+    cfg->kv_head_begin = 0;
+    cfg->kv_head_count = 0;
+}
+
+extern "C" const char* q3a_last_error(void) { return g_err; }
+
+static void destroy_ctx(q3a_ctx* c) {
+    if (!c) return;
+    if (c->stream) cudaStreamSynchronize(c->stream);
+    cudaFree(c->kcache);
+    cudaFree(c->vcache);
+    cudaFree(c->page_table);
+    cudaFree(c->partials);
+    cudaFree(c->counters);
+    cudaFree(c->err);
+    cudaFree(c->d_stage);
+    cudaFree(c->d_scratch);
+    if (c->h_stage) cudaFreeHost(c->h_stage);
+    if (c->own_stream) cudaStreamDestroy(c->own_stream);
+    delete c;
+}
+
+extern "C" int q3a_create(q3a_ctx** out, const q3a_cfg* cfg_in) {
+    g_err[0] = 0;
+    if (!out || !cfg_in) return fail(Q3A_ERR_INVALID, "null argument");
+    *out = nullptr;
+    q3a_cfg cfg = *cfg_in;
+    if (cfg.page_tokens == 0) cfg.page_tokens = 64;
+    if (cfg.kv_head_count == 0) cfg.kv_head_count = cfg.n_kv_heads - cfg.kv_head_begin;
+    if (cfg.head_dim != HD)
+        return fail(Q3A_ERR_UNSUPPORTED, "head_dim %d: only 128 is implemented", cfg.head_dim);
+    if (cfg.n_kv_heads <= 0 || cfg.n_heads != GQA * cfg.n_kv_heads)
+        return fail(Q3A_ERR_UNSUPPORTED, "n_heads %d / n_kv_heads %d: only 4 query heads per KV "
+                    "head are implemented", cfg.n_heads, cfg.n_kv_heads);
+    if (cfg.n_layers <= 0 || cfg.max_seq <= 0 || cfg.n_seqs <= 0)
+        return fail(Q3A_ERR_INVALID, "n_layers, max_seq and n_seqs must be positive");
+    if (cfg.page_tokens % DEC_TILE != 0)
+        return fail(Q3A_ERR_INVALID, "page_tokens %d is not a multiple of %d", cfg.page_tokens,
+                    DEC_TILE);
+    if (cfg.kv_dtype != Q3A_KV_F32 && cfg.kv_dtype != Q3A_KV_BF16)
+        return fail(Q3A_ERR_INVALID, "kv_dtype %d", cfg.kv_dtype);
+    if (cfg.ptr_mode != Q3A_PTR_HOST && cfg.ptr_mode != Q3A_PTR_DEVICE)
+        return fail(Q3A_ERR_INVALID, "ptr_mode %d", cfg.ptr_mode);
+    if (cfg.kv_head_begin < 0 || cfg.kv_head_count <= 0 ||
+        cfg.kv_head_begin + cfg.kv_head_count > cfg.n_kv_heads)
+        return fail(Q3A_ERR_INVALID, "kv head range [%d, +%d) outside 0..%d", cfg.kv_head_begin,
+                    cfg.kv_head_count, cfg.n_kv_heads);
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0)
+        return fail(Q3A_ERR_CUDA, "no CUDA device available");
+    if (cfg.device < 0 || cfg.device >= ndev)
+        return fail(Q3A_ERR_INVALID, "device %d of %d", cfg.device, ndev);
+    CUDA_TRY(cudaSetDevice(cfg.device));
+    cudaDeviceProp prop;
+    CUDA_TRY(cudaGetDeviceProperties(&prop, cfg.device));
+    if (prop.major != 10)
+        return fail(Q3A_ERR_UNSUPPORTED, "device %d is sm_%d%d; this library is built for sm_100a",
+                    cfg.device, prop.major, prop.minor);
+
+    q3a_ctx* c = new q3a_ctx();
+    c->cfg = cfg;
+    c->nkv = cfg.kv_head_count;
+    c->kv0 = cfg.kv_head_begin;
+    c->bf16 = cfg.kv_dtype == Q3A_KV_BF16;
+    c->esize = c->bf16 ? 2 : 4;
+    c->num_sms = prop.multiProcessorCount;
+    c->pages_per_seq = (cfg.max_seq + cfg.page_tokens - 1) / cfg.page_tokens;
+    c->n_pages = c->pages_per_seq * cfg.n_seqs;
+    c->total_rows = (long long)cfg.n_layers * c->nkv * c->n_pages * cfg.page_tokens;
+    if (c->total_rows >= (1LL << 31)) {
+        destroy_ctx(c);
+        return fail(Q3A_ERR_INVALID, "cache of %lld rows exceeds the 2^31 TMA coordinate range",
+                    c->total_rows);
+    }
+    // RoPE inverse frequencies exactly as apply_rope forms them
+    // (qwen3-8b/cpu/main.c:1285): 1.0f / powf(theta, (float)i / head_dim).
+    for (int i = 0; i < HD; i += 2)
+        c->inv_freq[i / 2] = 1.0f / powf(cfg.rope_theta, (float)i / HD);
+
+    const size_t cache_bytes = (size_t)c->total_rows * HD * c->esize;
+    int rc = Q3A_OK;
+    if (cudaMalloc(&c->kcache, cache_bytes) != cudaSuccess ||
+        cudaMalloc(&c->vcache, cache_bytes) != cudaSuccess) {
+        destroy_ctx(c);
+        return fail(Q3A_ERR_OOM, "KV cache of 2 x %zu bytes", cache_bytes);
+    }
+    std::vector<int> pt((size_t)cfg.n_seqs * c->pages_per_seq);
+    for (size_t i = 0; i < pt.size(); i++) pt[i] = (int)i;  // slot s owns pages [s*pps, (s+1)*pps)
+    const int max_groups = Q3A_MAX_BATCH * cfg.n_kv_heads;
+    c->part_slots = (long long)c->num_sms + max_groups;
+    if (cudaMalloc(&c->page_table, pt.size() * sizeof(int)) != cudaSuccess ||
+        cudaMalloc(&c->partials, (size_t)c->part_slots * PART_STRIDE * 4) != cudaSuccess ||
+        cudaMalloc(&c->counters, (size_t)max_groups * sizeof(int)) != cudaSuccess ||
+        cudaMalloc(&c->err, sizeof(int)) != cudaSuccess) {
+        destroy_ctx(c);
+        return fail(Q3A_ERR_OOM, "context scratch");
+    }
+    if (cudaStreamCreateWithFlags(&c->own_stream, cudaStreamNonBlocking) != cudaSuccess) {
+        destroy_ctx(c);
+        return fail(Q3A_ERR_CUDA, "stream creation");
+    }
+    c->stream = c->own_stream;
+    if (cudaMemsetAsync(c->kcache, 0, cache_bytes, c->stream) != cudaSuccess ||
+        cudaMemsetAsync(c->vcache, 0, cache_bytes, c->stream) != cudaSuccess ||
+        cudaMemsetAsync(c->counters, 0, (size_t)max_groups * sizeof(int), c->stream) != cudaSuccess ||
+        cudaMemsetAsync(c->err, 0, sizeof(int), c->stream) != cudaSuccess ||
+        cudaMemcpyAsync(c->page_table, pt.data(), pt.size() * sizeof(int), cudaMemcpyHostToDevice,
+                        c->stream) != cudaSuccess ||
+        cudaStreamSynchronize(c->stream) != cudaSuccess) {
+        destroy_ctx(c);
+        return fail(Q3A_ERR_CUDA, "cache initialisation");
+    }
+    rc = make_map_2d(&c->tmK, c->kcache, c->bf16, HD, (uint64_t)c->total_rows, HD, DEC_TILE,
+                     CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc == Q3A_OK)
+        rc = make_map_2d(&c->tmV, c->vcache, c->bf16, HD, (uint64_t)c->total_rows, HD, DEC_TILE,
+                         CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc == Q3A_OK && c->bf16) {
+        rc = make_map_2d(&c->tmKp, c->kcache, true, HD, (uint64_t)c->total_rows, 64, 128,
+                         CU_TENSOR_MAP_SWIZZLE_128B);
+        if (rc == Q3A_OK)
+            rc = make_map_2d(&c->tmVp, c->vcache, true, HD, (uint64_t)c->total_rows, 64, 128,
+                             CU_TENSOR_MAP_SWIZZLE_128B);
+    }
+    if (rc != Q3A_OK) {
+        destroy_ctx(c);
+        return rc;
+    }
+    const size_t stage = 2 * (size_t)cfg.n_heads * HD + 2 * (size_t)cfg.n_kv_heads * HD + 2 * HD;
+    rc = grow_stage(c, stage);
+    if (rc != Q3A_OK) {
+        destroy_ctx(c);
+        return rc;
+    }
+    *out = c;
+    return Q3A_OK;
+}
+
+extern "C" int q3a_destroy(q3a_ctx* c) {
+    if (!c) return Q3A_OK;
+    ensure_device(c);
+    destroy_ctx(c);
+    return Q3A_OK;
+}
+
+extern "C" int q3a_set_stream(q3a_ctx* c, void* s) {
+    if (!c) return fail(Q3A_ERR_INVALID, "null context");
+    c->stream = s ? reinterpret_cast<cudaStream_t>(s) : c->own_stream;
+    return Q3A_OK;
+}
+
+extern "C" int q3a_sync(q3a_ctx* c) {
+    if (!c) return fail(Q3A_ERR_INVALID, "null context");
+    int rc = ensure_device(c);
+    if (rc) return rc;
+    CUDA_TRY(cudaStreamSynchronize(c->stream));
+    return Q3A_OK;
+}
+
+extern "C" int q3a_check_device_error(q3a_ctx* c) {
+    if (!c) return fail(Q3A_ERR_INVALID, "null context");
+    int rc = ensure_device(c);
+    if (rc) return rc;
+    int h = 0;
+    CUDA_TRY(cudaMemcpyAsync(&h, c->err, sizeof(int), cudaMemcpyDeviceToHost, c->stream));
+    CUDA_TRY(cudaStreamSynchronize(c->stream));
+    if (h != 0) {
+        const int max_groups = Q3A_MAX_BATCH * c->cfg.n_kv_heads;
+        CUDA_TRY(cudaMemsetAsync(c->err, 0, sizeof(int), c->stream));
+        // an abandoned launch may have left arrival counters behind
+        CUDA_TRY(cudaMemsetAsync(c->counters, 0, (size_t)max_groups * sizeof(int), c->stream));
+        CUDA_TRY(cudaStreamSynchronize(c->stream));
+        return fail(Q3A_ERR_TIMEOUT, "a bounded device wait expired (device error %d)", h);
+    }
+    return Q3A_OK;
+}
+
+extern "C" uint64_t q3a_launch_count(const q3a_ctx* c) { return c ? c->launches : 0; }
+
+// ------------------------------------------------------------------ decode dispatch
+static void base_params(q3a_ctx* c, DecodeParams& p, int layer) {
+    memset(&p, 0, sizeof(p));
+    p.kcache = c->kcache;
+    p.vcache = c->vcache;
+    p.page_table = c->page_table;
+    p.partials = c->partials;
+    p.counters = c->counters;
+    p.err = c->err;
+    p.eps = c->cfg.norm_eps;
+    p.scale_log2e = (float)(1.4426950408889634 / sqrt((double)HD));
+    p.nkv = c->nkv;
+    p.kv0 = c->kv0;
+    p.hq_total = c->cfg.n_heads;
+    p.nkv_total = c->cfg.n_kv_heads;
+    p.layer = layer;
+    p.pages_per_seq = c->pages_per_seq;
+    p.page_tokens = c->cfg.page_tokens;
+    p.n_pages = c->n_pages;
+    p.cache_mode = CACHE_PAGED;
+    memcpy(p.inv_freq, c->inv_freq, sizeof(p.inv_freq));
+}
+
+// Fills unit_prefix / total_units / n_ctas from t_begin, t_end, fused.
+static int schedule(q3a_ctx* c, DecodeParams& p) {
+    long long acc = 0;
+    p.unit_prefix[0] = 0;
+    for (int b = 0; b < p.nb; b++) {
+        const int tb = p.t_begin[b], te = p.t_end[b];
+        const int a0 = tb / DEC_TILE;
+        const long long ncu = te > tb ? (te + DEC_TILE - 1) / DEC_TILE - a0 : 0;
+        const long long units = ncu + (p.fused ? 1 : 0);
+        if (units == 0) return fail(Q3A_ERR_INVALID, "sequence %d has nothing to attend", b);
+        acc += units * p.nkv;
+        p.unit_prefix[b + 1] = acc;
+    }
+    p.total_units = acc;
+    p.n_ctas = (int)std::min<long long>(c->num_sms, acc);
+    const long long slots = (long long)p.n_ctas + (long long)p.nb * p.nkv;
+    if (slots > c->part_slots) return fail(Q3A_ERR_INVALID, "decode scratch too small");
+    return Q3A_OK;
+}
+
+static int run_decode(q3a_ctx* c, DecodeParams& p, const CUtensorMap& tk, const CUtensorMap& tv,
+                      bool bf16) {
+    int rc = schedule(c, p);
+    if (rc) return rc;
+    CUDA_TRY(launch_decode(p, tk, tv, bf16, c->stream));
+    c->launches++;
+    return Q3A_OK;
+}
+
+extern "C" int q3a_attn_layer(q3a_ctx* c, float* xb, float* q, float* k, const float* v,
+                              const float* qw, const float* kw, int layer, int pos) {
+    g_err[0] = 0;
+    if (!c || !xb || !q || !k || !v || !qw || !kw) return fail(Q3A_ERR_INVALID, "null argument");
+    if (c->nkv != c->cfg.n_kv_heads)
+        return fail(Q3A_ERR_INVALID, "q3a_attn_layer needs a context holding all KV heads");
+    if (layer < 0 || layer >= c->cfg.n_layers) return fail(Q3A_ERR_INVALID, "layer %d", layer);
+    if (pos < 0 || pos >= c->cfg.max_seq)
+        return fail(Q3A_ERR_INVALID, "pos %d outside [0, %d)", pos, c->cfg.max_seq);
+    int rc = ensure_device(c);
+    if (rc) return rc;
+    const size_t qd = (size_t)c->cfg.n_heads * HD, kd = (size_t)c->cfg.n_kv_heads * HD;
+    DecodeParams p;
+    base_params(c, p, layer);
+    p.nb = 1;
+    p.fused = 1;
+    p.t_begin[0] = 0;
+    p.t_end[0] = pos;
+    p.pos[0] = pos;
+    p.slot[0] = 0;
+    if (c->cfg.ptr_mode == Q3A_PTR_DEVICE) {
+        p.q = q; p.k_new = k; p.v_new = v; p.q_norm_w = qw; p.k_norm_w = kw;
+        p.q_out = q; p.k_out = k; p.xb = xb;
+        return run_decode(c, p, c->tmK, c->tmV, c->bf16);
+    }
+    // host mode: one H2D of [q|k|v|qw|kw], one D2H of [xb|q|k]
+    float* hs = c->h_stage;
+    float* ds = c->d_stage;
+    float *h_xb = hs, *h_q = hs + qd, *h_k = h_q + qd, *h_v = h_k + kd, *h_qw = h_v + kd,
+          *h_kw = h_qw + HD;
+    float *d_xb = ds, *d_q = ds + qd, *d_k = d_q + qd, *d_v = d_k + kd, *d_qw = d_v + kd,
+          *d_kw = d_qw + HD;
+    memcpy(h_q, q, qd * 4);
+    memcpy(h_k, k, kd * 4);
+    memcpy(h_v, v, kd * 4);
+    memcpy(h_qw, qw, HD * 4);
+    memcpy(h_kw, kw, HD * 4);
+    CUDA_TRY(cudaMemcpyAsync(d_q, h_q, (qd + 2 * kd + 2 * HD) * 4, cudaMemcpyHostToDevice,
+                             c->stream));
+    p.q = d_q; p.k_new = d_k; p.v_new = d_v; p.q_norm_w = d_qw; p.k_norm_w = d_kw;
+    p.q_out = d_q; p.k_out = d_k; p.xb = d_xb;
+    rc = run_decode(c, p, c->tmK, c->tmV, c->bf16);
+    if (rc) return rc;
+    CUDA_TRY(cudaMemcpyAsync(h_xb, d_xb, (2 * qd + kd) * 4, cudaMemcpyDeviceToHost, c->stream));
+    CUDA_TRY(cudaStreamSynchronize(c->stream));
+    memcpy(xb, h_xb, qd * 4);
+    memcpy(q, h_q, qd * 4);
+    memcpy(k, h_k, kd * 4);
+    return Q3A_OK;
+}
+
+extern "C" int q3a_attn_layer_batched(q3a_ctx* c, float* xb, float* q, float* k, const float* v,
+                                      const float* qw, const float* kw, int layer,
+                                      const int* seq_ids, const int* pos, int n) {
+    g_err[0] = 0;
+    if (!c || !xb || !q || !k || !v || !qw || !kw || !seq_ids || !pos)
+        return fail(Q3A_ERR_INVALID, "null argument");
+    if (n <= 0 || n > Q3A_MAX_BATCH) return fail(Q3A_ERR_INVALID, "batch of %d", n);
+    if (layer < 0 || layer >= c->cfg.n_layers) return fail(Q3A_ERR_INVALID, "layer %d", layer);
+    int rc = ensure_device(c);
+    if (rc) return rc;
+    DecodeParams p;
+    base_params(c, p, layer);
+    p.nb = n;
+    p.fused = 1;
+    std::vector<char> seen(c->cfg.n_seqs, 0);
+    for (int b = 0; b < n; b++) {
+        if (seq_ids[b] < 0 || seq_ids[b] >= c->cfg.n_seqs || seen[seq_ids[b]])
+            return fail(Q3A_ERR_INVALID, "seq_ids[%d] = %d invalid or repeated", b, seq_ids[b]);
+        seen[seq_ids[b]] = 1;
+        if (pos[b] < 0 || pos[b] >= c->cfg.max_seq)
+            return fail(Q3A_ERR_INVALID, "pos[%d] = %d outside [0, %d)", b, pos[b], c->cfg.max_seq);
+        p.slot[b] = seq_ids[b];
+        p.pos[b] = pos[b];
+        p.t_begin[b] = 0;
+        p.t_end[b] = pos[b];
+    }
+    const size_t qd = (size_t)n * c->cfg.n_heads * HD, kd = (size_t)n * c->cfg.n_kv_heads * HD;
+    if (c->cfg.ptr_mode == Q3A_PTR_DEVICE) {
+        p.q = q; p.k_new = k; p.v_new = v; p.q_norm_w = qw; p.k_norm_w = kw;
+        p.q_out = q; p.k_out = k; p.xb = xb;
+        return run_decode(c, p, c->tmK, c->tmV, c->bf16);
+    }
+    rc = grow_stage(c, 2 * qd + 2 * kd + 2 * HD);
+    if (rc) return rc;
+    float* hs = c->h_stage;
+    float* ds = c->d_stage;
+    float *h_xb = hs, *h_q = hs + qd, *h_k = h_q + qd, *h_v = h_k + kd, *h_qw = h_v + kd,
+          *h_kw = h_qw + HD;
+    float *d_xb = ds, *d_q = ds + qd, *d_k = d_q + qd, *d_v = d_k + kd, *d_qw = d_v + kd,
+          *d_kw = d_qw + HD;
+    memcpy(h_q, q, qd * 4);
+    memcpy(h_k, k, kd * 4);
+    memcpy(h_v, v, kd * 4);
+    memcpy(h_qw, qw, HD * 4);
+    memcpy(h_kw, kw, HD * 4);
+    CUDA_TRY(cudaMemcpyAsync(d_q, h_q, (qd + 2 * kd + 2 * HD) * 4, cudaMemcpyHostToDevice,
+                             c->stream));
+    p.q = d_q; p.k_new = d_k; p.v_new = d_v; p.q_norm_w = d_qw; p.k_norm_w = d_kw;
+    p.q_out = d_q; p.k_out = d_k; p.xb = d_xb;
+    if (c->nkv != c->cfg.n_kv_heads)  // sharded: keep the caller's other xb slices
+        memcpy(h_xb, xb, qd * 4);
+    if (c->nkv != c->cfg.n_kv_heads)
+        CUDA_TRY(cudaMemcpyAsync(d_xb, h_xb, qd * 4, cudaMemcpyHostToDevice, c->stream));
+    rc = run_decode(c, p, c->tmK, c->tmV, c->bf16);
+    if (rc) return rc;
+    CUDA_TRY(cudaMemcpyAsync(h_xb, d_xb, (2 * qd + kd) * 4, cudaMemcpyDeviceToHost, c->stream));
+    CUDA_TRY(cudaStreamSynchronize(c->stream));
+    memcpy(xb, h_xb, qd * 4);
+    memcpy(q, h_q, qd * 4);
+    memcpy(k, h_k, kd * 4);
+    return Q3A_OK;
+}
+
+extern "C" int q3a_attn_decode(q3a_ctx* c, float* xb, const float* q, const float* kc,
+                               const float* vc, float* att, size_t loff, int pos, int n_heads,
+                               int kv_mul, int hd, int kv_dim, int max_seq) {
+    (void)att;
+    g_err[0] = 0;
+    if (!c || !xb || !q || !kc || !vc) return fail(Q3A_ERR_INVALID, "null argument");
+    if (hd != HD || kv_mul != GQA)
+        return fail(Q3A_ERR_UNSUPPORTED, "hd %d kv_mul %d: only 128 / 4 are implemented", hd,
+                    kv_mul);
+    if (kv_dim <= 0 || kv_dim % HD != 0 || n_heads != kv_mul * (kv_dim / HD))
+        return fail(Q3A_ERR_INVALID, "n_heads %d kv_dim %d inconsistent", n_heads, kv_dim);
+    if (kv_dim / HD > c->cfg.n_kv_heads)
+        return fail(Q3A_ERR_INVALID, "kv_dim %d wider than the context's %d KV heads", kv_dim,
+                    c->cfg.n_kv_heads);
+    if (pos < 0 || pos >= max_seq) return fail(Q3A_ERR_INVALID, "pos %d of max_seq %d", pos, max_seq);
+    if (loff % (size_t)kv_dim != 0) return fail(Q3A_ERR_INVALID, "loff not a row multiple");
+    int rc = ensure_device(c);
+    if (rc) return rc;
+    const int nkv = kv_dim / HD;
+    const size_t rows = (size_t)pos + 1;
+    const size_t qd = (size_t)n_heads * HD;
+    DecodeParams p;
+    base_params(c, p, 0);
+    p.cache_mode = CACHE_POSMAJOR;
+    p.nkv = nkv;
+    p.kv0 = 0;
+    p.hq_total = n_heads;
+    p.nkv_total = nkv;
+    p.nb = 1;
+    p.fused = 0;
+    p.t_begin[0] = 0;
+    p.t_end[0] = pos + 1;
+    const float *dk, *dv, *dq;
+    float* dxb;
+    if (c->cfg.ptr_mode == Q3A_PTR_DEVICE) {
+        dk = kc + loff;
+        dv = vc + loff;
+        dq = q;
+        dxb = xb;
+    } else {
+        const size_t cache_bytes = rows * kv_dim * 4;
+        rc = grow_scratch(c, 2 * cache_bytes + 2 * qd * 4);
+        if (rc) return rc;
+        float* s = reinterpret_cast<float*>(c->d_scratch);
+        float* sk = s;
+        float* sv = s + rows * kv_dim;
+        float* sq = sv + rows * kv_dim;
+        dxb = sq + qd;
+        CUDA_TRY(cudaMemcpyAsync(sk, kc + loff, cache_bytes, cudaMemcpyHostToDevice, c->stream));
+        CUDA_TRY(cudaMemcpyAsync(sv, vc + loff, cache_bytes, cudaMemcpyHostToDevice, c->stream));
+        CUDA_TRY(cudaMemcpyAsync(sq, q, qd * 4, cudaMemcpyHostToDevice, c->stream));
+        dk = sk;
+        dv = sv;
+        dq = sq;
+    }
+    CUtensorMap tk, tv;
+    rc = make_map_2d(&tk, dk, false, (uint64_t)kv_dim, rows, HD, DEC_TILE, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc) return rc;
+    rc = make_map_2d(&tv, dv, false, (uint64_t)kv_dim, rows, HD, DEC_TILE, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc) return rc;
+    p.q = dq;
+    p.xb = dxb;
+    rc = run_decode(c, p, tk, tv, false);
+    if (rc) return rc;
+    if (c->cfg.ptr_mode == Q3A_PTR_HOST) {
+        CUDA_TRY(cudaMemcpyAsync(xb, dxb, qd * 4, cudaMemcpyDeviceToHost, c->stream));
+        CUDA_TRY(cudaStreamSynchronize(c->stream));
+    }
+    return Q3A_OK;
+}
+
+extern "C" int q3a_attn_partial(q3a_ctx* c, float* o, float* lse, const float* q, int seq,
+                                int layer, int t0, int t1) {
+    g_err[0] = 0;
+    if (!c || !o || !lse || !q) return fail(Q3A_ERR_INVALID, "null argument");
+    if (seq < 0 || seq >= c->cfg.n_seqs) return fail(Q3A_ERR_INVALID, "seq %d", seq);
+    if (layer < 0 || layer >= c->cfg.n_layers) return fail(Q3A_ERR_INVALID, "layer %d", layer);
+    if (t0 < 0 || t1 < t0 || t1 > c->cfg.max_seq)
+        return fail(Q3A_ERR_INVALID, "chunk [%d, %d) outside [0, %d]", t0, t1, c->cfg.max_seq);
+    if (c->nkv != c->cfg.n_kv_heads)
+        return fail(Q3A_ERR_INVALID, "q3a_attn_partial needs a context holding all KV heads");
+    int rc = ensure_device(c);
+    if (rc) return rc;
+    const size_t qd = (size_t)c->cfg.n_heads * HD;
+    const int nh = c->cfg.n_heads;
+    if (t0 == t1) {  // empty chunk: o = 0, lse = -inf
+        if (c->cfg.ptr_mode == Q3A_PTR_DEVICE) {
+            CUDA_TRY(cudaMemsetAsync(o, 0, qd * 4, c->stream));
+            std::vector<float> ninf(nh, -INFINITY);
+            CUDA_TRY(cudaMemcpyAsync(lse, ninf.data(), nh * 4, cudaMemcpyHostToDevice, c->stream));
+            CUDA_TRY(cudaStreamSynchronize(c->stream));
+        } else {
+            memset(o, 0, qd * 4);
+            for (int h = 0; h < nh; h++) lse[h] = -INFINITY;
+        }
+        return Q3A_OK;
+    }
+    DecodeParams p;
+    base_params(c, p, layer);
+    p.nb = 1;
+    p.fused = 0;
+    p.partial_out = 1;
+    p.slot[0] = seq;
+    p.t_begin[0] = t0;
+    p.t_end[0] = t1;
+    if (c->cfg.ptr_mode == Q3A_PTR_DEVICE) {
+        p.q = q;
+        p.xb = o;
+        p.lse_out = lse;
+        return run_decode(c, p, c->tmK, c->tmV, c->bf16);
+    }
+    float* ds = c->d_stage;
+    float *d_o = ds, *d_q = ds + qd, *d_l = d_q + qd;
+    CUDA_TRY(cudaMemcpyAsync(d_q, q, qd * 4, cudaMemcpyHostToDevice, c->stream));
+    p.q = d_q;
+    p.xb = d_o;
+    p.lse_out = d_l;
+    rc = run_decode(c, p, c->tmK, c->tmV, c->bf16);
+    if (rc) return rc;
+    CUDA_TRY(cudaMemcpyAsync(o, d_o, qd * 4, cudaMemcpyDeviceToHost, c->stream));
+    CUDA_TRY(cudaMemcpyAsync(lse, d_l, nh * 4, cudaMemcpyDeviceToHost, c->stream));
+    CUDA_TRY(cudaStreamSynchronize(c->stream));
+    return Q3A_OK;
+}
+
+extern "C" int q3a_lse_combine(q3a_ctx* c, float* xb, const float* o_parts, const float* lse_parts,
+                               int n_parts) {
+    g_err[0] = 0;
+    if (!c || !xb || !o_parts || !lse_parts || n_parts <= 0)
+        return fail(Q3A_ERR_INVALID, "bad argument");
+    int rc = ensure_device(c);
+    if (rc) return rc;
+    const int nh = c->cfg.n_heads;
+    const size_t qd = (size_t)nh * HD;
+    if (c->cfg.ptr_mode == Q3A_PTR_DEVICE) {
+        CUDA_TRY(launch_lse_combine(xb, o_parts, lse_parts, n_parts, nh, c->stream));
+        c->launches++;
+        return Q3A_OK;
+    }
+    rc = grow_scratch(c, ((size_t)n_parts * (qd + nh) + qd) * 4);
+    if (rc) return rc;
+    float* s = reinterpret_cast<float*>(c->d_scratch);
+    float *d_o = s, *d_l = s + (size_t)n_parts * qd, *d_x = d_l + (size_t)n_parts * nh;
+    CUDA_TRY(cudaMemcpyAsync(d_o, o_parts, (size_t)n_parts * qd * 4, cudaMemcpyHostToDevice, c->stream));
+    CUDA_TRY(cudaMemcpyAsync(d_l, lse_parts, (size_t)n_parts * nh * 4, cudaMemcpyHostToDevice, c->stream));
+    CUDA_TRY(launch_lse_combine(d_x, d_o, d_l, n_parts, nh, c->stream));
+    c->launches++;
+    CUDA_TRY(cudaMemcpyAsync(xb, d_x, qd * 4, cudaMemcpyDeviceToHost, c->stream));
+    CUDA_TRY(cudaStreamSynchronize(c->stream));
+    return Q3A_OK;
+}
+
+// ------------------------------------------------------------------ cache I/O
+static int cache_io_params(q3a_ctx* c, AppendParams& a, int seq, int layer, int pos0, int n) {
+    if (seq < 0 || seq >= c->cfg.n_seqs) return fail(Q3A_ERR_INVALID, "seq %d", seq);
+    if (layer < 0 || layer >= c->cfg.n_layers) return fail(Q3A_ERR_INVALID, "layer %d", layer);
+    if (n < 0 || pos0 < 0 || (long long)pos0 + n > c->cfg.max_seq)
+        return fail(Q3A_ERR_INVALID, "rows [%d, +%d) outside [0, %d)", pos0, n, c->cfg.max_seq);
+    memset(&a, 0, sizeof(a));
+    a.kcache = c->kcache;
+    a.vcache = c->vcache;
+    a.page_table = c->page_table;
+    a.eps = c->cfg.norm_eps;
+    a.n = n;
+    a.nkv = c->nkv;
+    a.kv0 = c->kv0;
+    a.nkv_total = c->cfg.n_kv_heads;
+    a.layer = layer;
+    a.slot = seq;
+    a.pos0 = pos0;
+    a.pages_per_seq = c->pages_per_seq;
+    a.page_tokens = c->cfg.page_tokens;
+    a.n_pages = c->n_pages;
+    a.bf16 = c->bf16;
+    memcpy(a.inv_freq, c->inv_freq, sizeof(a.inv_freq));
+    return Q3A_OK;
+}
+
+static int append_common(q3a_ctx* c, int seq, int layer, int pos0, int n, const float* k,
+                         const float* v, const float* kw, int norm_rope) {
+    g_err[0] = 0;
+    if (!c || !k || !v || (norm_rope && !kw)) return fail(Q3A_ERR_INVALID, "null argument");
+    int rc = ensure_device(c);
+    if (rc) return rc;
+    AppendParams a;
+    rc = cache_io_params(c, a, seq, layer, pos0, n);
+    if (rc) return rc;
+    if (n == 0) return Q3A_OK;
+    a.do_norm_rope = norm_rope;
+    const size_t kd = (size_t)n * c->cfg.n_kv_heads * HD;
+    if (c->cfg.ptr_mode == Q3A_PTR_DEVICE) {
+        a.k = k; a.v = v; a.k_norm_w = kw;
+    } else {
+        rc = grow_scratch(c, (2 * kd + HD) * 4);
+        if (rc) return rc;
+        float* s = reinterpret_cast<float*>(c->d_scratch);
+        CUDA_TRY(cudaMemcpyAsync(s, k, kd * 4, cudaMemcpyHostToDevice, c->stream));
+        CUDA_TRY(cudaMemcpyAsync(s + kd, v, kd * 4, cudaMemcpyHostToDevice, c->stream));
+        if (norm_rope)
+            CUDA_TRY(cudaMemcpyAsync(s + 2 * kd, kw, HD * 4, cudaMemcpyHostToDevice, c->stream));
+        a.k = s; a.v = s + kd; a.k_norm_w = s + 2 * kd;
+    }
+    CUDA_TRY(launch_append(a, c->stream));
+    c->launches++;
+    if (c->cfg.ptr_mode == Q3A_PTR_HOST) CUDA_TRY(cudaStreamSynchronize(c->stream));
+    return Q3A_OK;
+}
+
+extern "C" int q3a_kv_append(q3a_ctx* c, int seq, int layer, int pos0, int n, const float* k,
+                             const float* v, const float* kw) {
+    return append_common(c, seq, layer, pos0, n, k, v, kw, 1);
+}
+
+extern "C" int q3a_kv_load(q3a_ctx* c, int seq, int layer, int pos0, int n, const float* k,
+                           const float* v) {
+    return append_common(c, seq, layer, pos0, n, k, v, nullptr, 0);
+}
+
+extern "C" int q3a_kv_read(q3a_ctx* c, int seq, int layer, int pos0, int n, float* k, float* v) {
+    g_err[0] = 0;
+    if (!c || !k || !v) return fail(Q3A_ERR_INVALID, "null argument");
+    int rc = ensure_device(c);
+    if (rc) return rc;
+    AppendParams a;
+    rc = cache_io_params(c, a, seq, layer, pos0, n);
+    if (rc) return rc;
+    if (n == 0) return Q3A_OK;
+    const size_t kd = (size_t)n * c->nkv * HD;
+    if (c->cfg.ptr_mode == Q3A_PTR_DEVICE) {
+        CUDA_TRY(launch_kv_read(a, k, v, c->stream));
+        c->launches++;
+        return Q3A_OK;
+    }
+    rc = grow_scratch(c, 2 * kd * 4);
+    if (rc) return rc;
+    float* s = reinterpret_cast<float*>(c->d_scratch);
+    CUDA_TRY(launch_kv_read(a, s, s + kd, c->stream));
+    c->launches++;
+    CUDA_TRY(cudaMemcpyAsync(k, s, kd * 4, cudaMemcpyDeviceToHost, c->stream));
+    CUDA_TRY(cudaMemcpyAsync(v, s + kd, kd * 4, cudaMemcpyDeviceToHost, c->stream));
+    CUDA_TRY(cudaStreamSynchronize(c->stream));
+    return Q3A_OK;
+}
+
+extern "C" int q3a_randn(q3a_ctx* c, void* dst, int out_dtype, size_t n, uint64_t seed,
+                         uint64_t stream_id, uint64_t offset) {
+    g_err[0] = 0;
+    if (!c || !dst) return fail(Q3A_ERR_INVALID, "null argument");
+    if (out_dtype != Q3A_OUT_F32 && out_dtype != Q3A_OUT_BF16)
+        return fail(Q3A_ERR_INVALID, "out_dtype %d", out_dtype);
+    int rc = ensure_device(c);
+    if (rc) return rc;
+    CUDA_TRY(launch_randn(dst, out_dtype == Q3A_OUT_BF16, n, stream_key(seed, stream_id), offset,
+                          c->stream));
+    c->launches++;
+    return Q3A_OK;
+}
+
+// ------------------------------------------------------------------ prefill
+extern "C" int q3a_prefill_attn(q3a_ctx* c, void* out, int out_dtype, const void* q_bf16, int seq,
+                                int layer, int pos0, int n_tok);
+
+extern "C" int q3a_prefill(q3a_ctx* c, void* out, int out_dtype, const float* q, const float* k,
+                           const float* v, const float* qw, const float* kw, int seq, int layer,
+                           int pos0, int n_tok) {
+    g_err[0] = 0;
+    if (!c || !out || !q || !k || !v || !qw || !kw) return fail(Q3A_ERR_INVALID, "null argument");
+    if (!c->bf16) return fail(Q3A_ERR_UNSUPPORTED, "prefill needs a bf16 cache");
+    if (c->nkv != c->cfg.n_kv_heads)
+        return fail(Q3A_ERR_INVALID, "q3a_prefill needs a context holding all KV heads");
+    if (n_tok <= 0) return fail(Q3A_ERR_INVALID, "n_tok %d", n_tok);
+    int rc = ensure_device(c);
+    if (rc) return rc;
+    AppendParams a;
+    rc = cache_io_params(c, a, seq, layer, pos0, n_tok);
+    if (rc) return rc;
+    const size_t qd = (size_t)n_tok * c->cfg.n_heads * HD;
+    const size_t kd = (size_t)n_tok * c->cfg.n_kv_heads * HD;
+    const size_t out_bytes = qd * (out_dtype == Q3A_OUT_BF16 ? 2 : 4);
+    // scratch: [q bf16 | (host mode) q f32 | k | v | qw | kw | out]
+    const bool host = c->cfg.ptr_mode == Q3A_PTR_HOST;
+    size_t need = qd * 2 + 256;
+    if (host) need += (qd + 2 * kd + 2 * HD) * 4 + out_bytes + 256;
+    rc = grow_scratch(c, need);
+    if (rc) return rc;
+    uint8_t* s = reinterpret_cast<uint8_t*>(c->d_scratch);
+    __nv_bfloat16* qb = reinterpret_cast<__nv_bfloat16*>(s);
+    const float *dq = q, *dk = k, *dv = v, *dqw = qw, *dkw = kw;
+    void* dout = out;
+    if (host) {
+        float* f = reinterpret_cast<float*>(s + ((qd * 2 + 255) & ~(size_t)255));
+        float *fq = f, *fk = fq + qd, *fv = fk + kd, *fqw = fv + kd, *fkw = fqw + HD;
+        void* fo = fkw + HD;
+        CUDA_TRY(cudaMemcpyAsync(fq, q, qd * 4, cudaMemcpyHostToDevice, c->stream));
+        CUDA_TRY(cudaMemcpyAsync(fk, k, kd * 4, cudaMemcpyHostToDevice, c->stream));
+        CUDA_TRY(cudaMemcpyAsync(fv, v, kd * 4, cudaMemcpyHostToDevice, c->stream));
+        CUDA_TRY(cudaMemcpyAsync(fqw, qw, HD * 4, cudaMemcpyHostToDevice, c->stream));
+        CUDA_TRY(cudaMemcpyAsync(fkw, kw, HD * 4, cudaMemcpyHostToDevice, c->stream));
+        dq = fq; dk = fk; dv = fv; dqw = fqw; dkw = fkw; dout = fo;
+    }
+    PrepParams pp;
+    memset(&pp, 0, sizeof(pp));
+    pp.src = dq;
+    pp.dst_bf16 = qb;
+    pp.w = dqw;
+    pp.eps = c->cfg.norm_eps;
+    pp.n = n_tok;
+    pp.nheads = c->cfg.n_heads;
+    pp.head0 = 0;
+    pp.nheads_total = c->cfg.n_heads;
+    pp.pos0 = pos0;
+    pp.do_norm_rope = 1;
+    memcpy(pp.inv_freq, c->inv_freq, sizeof(pp.inv_freq));
+    CUDA_TRY(launch_prep_rows(pp, c->stream));
+    c->launches++;
+    a.k = dk;
+    a.v = dv;
+    a.k_norm_w = dkw;
+    a.do_norm_rope = 1;
+    CUDA_TRY(launch_append(a, c->stream));
+    c->launches++;
+    // run the attention in device mode on the staged operands
+    const int saved_mode = c->cfg.ptr_mode;
+    c->cfg.ptr_mode = Q3A_PTR_DEVICE;
+    rc = q3a_prefill_attn(c, dout, out_dtype, qb, seq, layer, pos0, n_tok);
+    c->cfg.ptr_mode = saved_mode;
+    if (rc) return rc;
+    if (host) {
+        CUDA_TRY(cudaMemcpyAsync(out, dout, out_bytes, cudaMemcpyDeviceToHost, c->stream));
+        CUDA_TRY(cudaStreamSynchronize(c->stream));
+    }
+    return Q3A_OK;
+}
+
+extern "C" int q3a_prefill_attn(q3a_ctx* c, void* out, int out_dtype, const void* q_bf16, int seq,
+                                int layer, int pos0, int n_tok) {
+    if (!c || !out || !q_bf16) return fail(Q3A_ERR_INVALID, "null argument");
+    if (!c->bf16) return fail(Q3A_ERR_UNSUPPORTED, "prefill needs a bf16 cache");
+    if (out_dtype != Q3A_OUT_F32 && out_dtype != Q3A_OUT_BF16)
+        return fail(Q3A_ERR_INVALID, "out_dtype %d", out_dtype);
+    if (c->nkv != c->cfg.n_kv_heads)
+        return fail(Q3A_ERR_INVALID, "q3a_prefill_attn needs a context holding all KV heads");
+    if (seq < 0 || seq >= c->cfg.n_seqs) return fail(Q3A_ERR_INVALID, "seq %d", seq);
+    if (layer < 0 || layer >= c->cfg.n_layers) return fail(Q3A_ERR_INVALID, "layer %d", layer);
+    if (n_tok <= 0 || pos0 < 0 || (long long)pos0 + n_tok > c->cfg.max_seq)
+        return fail(Q3A_ERR_INVALID, "rows [%d, +%d) outside [0, %d)", pos0, n_tok, c->cfg.max_seq);
+    return fail(Q3A_ERR_UNSUPPORTED, "the tensor-core prefill kernel is not built yet");
+}

@@ -1,0 +1,168 @@
+// q3a_common.cuh -- shared device helpers for the sm_100a attention kernels:
+// mbarrier and TMA (cp.async.bulk.tensor) wrappers in inline PTX, bounded
+// waits, bf16 packing, and the per-head QK-RMSNorm / RoPE arithmetic written
+// in the reference's operation order.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace q3a {
+
+constexpr int HD = 128;        // head_dim (Qwen3-8B)
+constexpr int GQA = 4;         // query heads per KV head (32 / 8)
+constexpr unsigned FULL = 0xffffffffu;
+
+// Bounded waits: a spin that has not completed after this many SM clocks
+// (about one second at B200 clocks) gives up, records Q3A device error
+// ERR_TIMEOUT and lets the kernel return instead of hanging the GPU.
+constexpr long long WAIT_LIMIT_CYCLES = 2000000000LL;
+constexpr int DEV_ERR_TIMEOUT = 5;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// ---------------------------------------------------------------- mbarrier
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
+                 : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Waits for the phase with the given parity to complete; false on timeout.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const long long t0 = clock64();
+    while (!mbar_try_wait(bar, parity)) {
+        if (clock64() - t0 > WAIT_LIMIT_CYCLES) return false;
+    }
+    return true;
+}
+
+// ---------------------------------------------------------------- TMA
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+
+__device__ __forceinline__ uint64_t l2_policy_evict_last() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+
+__device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// 2-D tiled bulk tensor load global -> shared (this CTA), completion counted
+// on `bar` in bytes.  x is the innermost coordinate (elements).
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar,
+                                            int x, int y, uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        ".L2::cache_hint [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "l"(policy)
+        : "memory");
+}
+
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar,
+                                            int x, int y, int z, uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        ".L2::cache_hint [%0], [%1, {%3, %4, %5}], [%2], %6;" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z),
+        "l"(policy)
+        : "memory");
+}
+
+// Named barrier over `nthreads` threads (id 0 is __syncthreads).
+__device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// ---------------------------------------------------------------- bf16
+__device__ __forceinline__ float bf16lo(uint32_t u) { return __uint_as_float(u << 16); }
+__device__ __forceinline__ float bf16hi(uint32_t u) { return __uint_as_float(u & 0xffff0000u); }
+
+template <typename T>
+__device__ __forceinline__ T from_f32(float x);
+template <>
+__device__ __forceinline__ float from_f32<float>(float x) {
+    return x;
+}
+template <>
+__device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float x) {
+    return __float2bfloat16_rn(x);
+}
+
+template <typename T>
+__device__ __forceinline__ float to_f32(T x);
+template <>
+__device__ __forceinline__ float to_f32<float>(float x) {
+    return x;
+}
+template <>
+__device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 x) {
+    return __bfloat162float(x);
+}
+
+// ---------------------------------------------------------------- norm / rope
+// Sum of squares of one 128-wide head in index order with separately rounded
+// multiply and add, the order of rmsnorm_head_inplace
+// (qwen3-8b/cpu/main.c:1179): the scale is then bit-identical to the
+// reference's 1/sqrtf(ss/hd + eps).
+__device__ __forceinline__ float head_rms_scale(const float* x, float eps) {
+    float ss = 0.0f;
+#pragma unroll 8
+    for (int i = 0; i < HD; i++) ss = __fadd_rn(ss, __fmul_rn(x[i], x[i]));
+    return 1.0f / sqrtf(__fadd_rn(ss / (float)HD, eps));
+}
+
+// One RoPE pair (qwen3-8b/cpu/main.c:1284-1293) at position pos with the
+// pair's inverse frequency (host-computed as 1/powf(theta, 2i/hd)); products
+// are rounded separately as in the reference (no FMA contraction).
+__device__ __forceinline__ void rope_pair(float& v0, float& v1, int pos, float inv_freq) {
+    const float ang = __fmul_rn((float)pos, inv_freq);
+    float s, c;
+    sincosf(ang, &s, &c);
+    const float a = __fsub_rn(__fmul_rn(v0, c), __fmul_rn(v1, s));
+    const float b = __fadd_rn(__fmul_rn(v0, s), __fmul_rn(v1, c));
+    v0 = a;
+    v1 = b;
+}
+
+}  // namespace q3a

@@ -1,0 +1,142 @@
+// q3a_internal.h -- parameter blocks and launchers shared between the C-ABI
+// layer (q3a_api.cu) and the kernel translation units.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/q3attn.h"
+
+namespace q3a {
+
+constexpr int MAX_B = Q3A_MAX_BATCH;
+constexpr int DEC_TILE = 64;        // cache tokens per pipeline stage (decode)
+constexpr int PART_STRIDE = 4 * 128 + 4;  // floats per partial slot: o[4][128], lse[4]
+
+// Where the decode kernel finds K/V rows.
+enum CacheMode : int {
+    CACHE_PAGED = 0,      // context cache [layer][kvh][page][tok][128]
+    CACHE_POSMAJOR = 1,   // caller cache [pos][kv_dim] (launch_attn layout)
+};
+
+// One decode launch.  The work is a list of units: for every (sequence b,
+// local kv head) group, ceil(Lc_b / DEC_TILE) cache tiles plus, when `fused`,
+// one unit for the new token (prepared and appended inside the kernel).
+// Units are numbered sequence-major, then kv head, then tile; CTA c owns
+// units [c*total/n_ctas, (c+1)*total/n_ctas).
+struct DecodeParams {
+    const float* q;          // [nb][hq_total*128]; raw (fused) or prepared
+    const float* k_new;      // [nb][nkv_total*128] raw (fused)
+    const float* v_new;
+    const float* q_norm_w;   // [128]
+    const float* k_norm_w;
+    float* q_out;            // normalised/rotated q written back (fused), may be null
+    float* k_out;            // normalised/rotated k written back (fused), may be null
+    float* xb;               // [nb][hq_total*128]; or partial o for attn_partial
+    float* lse_out;          // [nb][hq_total] log2-sum-exp output (partial mode), may be null
+    void* kcache;            // paged caches (append target in fused mode)
+    void* vcache;
+    const int* page_table;   // [n_seqs][pages_per_seq]
+    float* partials;         // scratch: slots of PART_STRIDE floats
+    int* counters;           // scratch: one per group, zero between launches
+    int* err;                // device error flag
+    float eps;
+    float scale_log2e;       // log2(e)/sqrt(128)
+    int nb;                  // sequences in this launch
+    int nkv;                 // kv heads processed (local)
+    int kv0;                 // global index of local kv head 0
+    int hq_total;            // query heads per row of q / xb
+    int nkv_total;           // kv heads per row of k_new / v_new
+    int layer;
+    int pages_per_seq;
+    int page_tokens;
+    int n_pages;             // pages per (layer, kv head)
+    int cache_mode;          // CacheMode
+    int fused;               // 1: new token prepared + appended in-kernel
+    int partial_out;         // 1: write normalised o + lse instead of xb
+    long long total_units;
+    int n_ctas;
+    float inv_freq[64];      // RoPE inverse frequencies (host powf, reference formula)
+    int t_begin[MAX_B];      // first cache position attended per sequence
+    int t_end[MAX_B];        // one past the last cache position read from the cache
+    int pos[MAX_B];          // new-token position (fused)
+    int slot[MAX_B];         // cache slot per sequence
+    long long unit_prefix[MAX_B + 1];  // prefix of nkv * units_b
+};
+
+struct PrepParams {
+    const float* src;        // raw rows [n][nheads_total*128]
+    float* dst_f32;          // prepared rows (may be null)
+    __nv_bfloat16* dst_bf16; // prepared rows (may be null)
+    const float* w;          // norm gains [128]
+    float eps;
+    int n;                   // rows (tokens)
+    int nheads;              // heads per row processed
+    int head0;               // first head processed
+    int nheads_total;        // heads per row in src / dst
+    int pos0;                // position of row 0
+    int do_norm_rope;
+    float inv_freq[64];
+};
+
+struct AppendParams {
+    const float* k;          // [n][nkv_total*128]
+    const float* v;
+    const float* k_norm_w;
+    void* kcache;
+    void* vcache;
+    const int* page_table;
+    float eps;
+    int n;
+    int nkv;                 // local kv heads
+    int kv0;
+    int nkv_total;
+    int layer;
+    int slot;
+    int pos0;
+    int pages_per_seq;
+    int page_tokens;
+    int n_pages;
+    int do_norm_rope;        // 0: rows are already prepared (kv_load)
+    int bf16;
+    float inv_freq[64];
+};
+
+// ---------------------------------------------------------------- launchers
+// All return a cudaError_t of the launch.
+cudaError_t launch_decode(const DecodeParams& p, const CUtensorMap& tmK, const CUtensorMap& tmV,
+                          bool bf16, cudaStream_t st);
+int decode_smem_bytes(bool bf16);
+cudaError_t launch_append(const AppendParams& p, cudaStream_t st);
+cudaError_t launch_kv_read(const AppendParams& p, float* k_out, float* v_out, cudaStream_t st);
+cudaError_t launch_prep_rows(const PrepParams& p, cudaStream_t st);
+cudaError_t launch_randn(void* dst, int out_bf16, size_t n, uint64_t key, uint64_t offset,
+                         cudaStream_t st);
+cudaError_t launch_lse_combine(float* xb, const float* o_parts, const float* lse_parts,
+                               int n_parts, int n_heads, cudaStream_t st);
+
+struct PrefillParams {
+    float* out_f32;
+    __nv_bfloat16* out_bf16;
+    const int* page_table;
+    int n_tok;
+    int pos0;
+    int hq_total;            // query heads per row
+    int nkv;                 // local kv heads
+    int kv0;
+    int layer;
+    int slot;
+    int pages_per_seq;
+    int page_tokens;
+    int n_pages;
+    float scale_log2e;
+    int* err;
+};
+cudaError_t launch_prefill(const PrefillParams& p, const CUtensorMap& tmQ,
+                           const CUtensorMap& tmK, const CUtensorMap& tmV, cudaStream_t st);
+int prefill_smem_bytes();
+
+uint64_t stream_key(uint64_t seed, uint64_t stream);
+
+}  // namespace q3a

@@ -1,0 +1,187 @@
+"""ctypes binding of lib/libq3attn.so (include/q3attn.h).
+
+This is how the Python harness (tests, bench) reaches the library: the same
+extern "C" entry points a C host such as Qwen3.c's forward() links against.
+Loading fails loudly if the library was not built; there is no fallback.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "lib", "libq3attn.so")
+
+OK, ERR_INVALID, ERR_CUDA, ERR_OOM, ERR_UNSUPPORTED, ERR_TIMEOUT = 0, 1, 2, 3, 4, 5
+KV_F32, KV_BF16 = 0, 1
+PTR_HOST, PTR_DEVICE = 0, 1
+OUT_F32, OUT_BF16 = 0, 1
+MAX_BATCH = 256
+
+# Every symbol include/q3attn.h declares.
+EXPORTS = [
+    "q3a_cfg_default", "q3a_create", "q3a_destroy", "q3a_last_error", "q3a_set_stream",
+    "q3a_sync", "q3a_check_device_error", "q3a_attn_layer", "q3a_attn_decode",
+    "q3a_attn_layer_batched", "q3a_kv_append", "q3a_kv_load", "q3a_kv_read", "q3a_prefill",
+    "q3a_prefill_attn", "q3a_attn_partial", "q3a_lse_combine", "q3a_randn",
+    "q3a_launch_count",
+]
+
+
+class Cfg(ctypes.Structure):
+    _fields_ = [
+        ("n_layers", ctypes.c_int), ("n_heads", ctypes.c_int), ("n_kv_heads", ctypes.c_int),
+        ("head_dim", ctypes.c_int), ("max_seq", ctypes.c_int), ("n_seqs", ctypes.c_int),
+        ("kv_dtype", ctypes.c_int), ("page_tokens", ctypes.c_int), ("ptr_mode", ctypes.c_int),
+        ("device", ctypes.c_int), ("norm_eps", ctypes.c_float), ("rope_theta", ctypes.c_float),
+        ("kv_head_begin", ctypes.c_int), ("kv_head_count", ctypes.c_int),
+    ]
+
+
+class Q3AError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"q3attn error {code}: {msg}")
+        self.code = code
+
+
+_lib = None
+_P = ctypes.c_void_p
+_I = ctypes.c_int
+_SZ = ctypes.c_size_t
+_U64 = ctypes.c_uint64
+
+
+def load():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(f"{LIB_PATH} is missing: build it (make -C qwen3.c_b200)")
+        L = ctypes.CDLL(LIB_PATH)
+        L.q3a_cfg_default.argtypes = [ctypes.POINTER(Cfg)]
+        L.q3a_cfg_default.restype = None
+        L.q3a_create.argtypes = [ctypes.POINTER(_P), ctypes.POINTER(Cfg)]
+        L.q3a_destroy.argtypes = [_P]
+        L.q3a_last_error.restype = ctypes.c_char_p
+        L.q3a_set_stream.argtypes = [_P, _P]
+        L.q3a_sync.argtypes = [_P]
+        L.q3a_check_device_error.argtypes = [_P]
+        L.q3a_attn_layer.argtypes = [_P, _P, _P, _P, _P, _P, _P, _I, _I]
+        L.q3a_attn_decode.argtypes = [_P, _P, _P, _P, _P, _P, _SZ, _I, _I, _I, _I, _I, _I]
+        L.q3a_attn_layer_batched.argtypes = [_P, _P, _P, _P, _P, _P, _P, _I, _P, _P, _I]
+        L.q3a_kv_append.argtypes = [_P, _I, _I, _I, _I, _P, _P, _P]
+        L.q3a_kv_load.argtypes = [_P, _I, _I, _I, _I, _P, _P]
+        L.q3a_kv_read.argtypes = [_P, _I, _I, _I, _I, _P, _P]
+        L.q3a_prefill.argtypes = [_P, _P, _I, _P, _P, _P, _P, _P, _I, _I, _I, _I]
+        L.q3a_prefill_attn.argtypes = [_P, _P, _I, _P, _I, _I, _I, _I]
+        L.q3a_attn_partial.argtypes = [_P, _P, _P, _P, _I, _I, _I, _I]
+        L.q3a_lse_combine.argtypes = [_P, _P, _P, _P, _I]
+        L.q3a_randn.argtypes = [_P, _P, _I, _SZ, _U64, _U64, _U64]
+        L.q3a_launch_count.argtypes = [_P]
+        L.q3a_launch_count.restype = _U64
+        _lib = L
+    return _lib
+
+
+def check(rc: int):
+    if rc != OK:
+        raise Q3AError(rc, load().q3a_last_error().decode())
+
+
+def ptr(x) -> int:
+    """Address of a numpy array (host) or a torch tensor (host or device)."""
+    if x is None:
+        return None
+    if hasattr(x, "data_ptr"):
+        assert x.is_contiguous()
+        return x.data_ptr()
+    assert x.flags["C_CONTIGUOUS"]
+    return x.ctypes.data
+
+
+def default_cfg(**kw) -> Cfg:
+    c = Cfg()
+    load().q3a_cfg_default(ctypes.byref(c))
+    for k, v in kw.items():
+        setattr(c, k, v)
+    return c
+
+
+class Context:
+    """Owns one q3a_ctx.  Methods mirror the C entry points one to one."""
+
+    def __init__(self, **cfg):
+        self.lib = load()
+        self.cfg = default_cfg(**cfg)
+        h = _P()
+        check(self.lib.q3a_create(ctypes.byref(h), ctypes.byref(self.cfg)))
+        self.h = h
+
+    def close(self):
+        if getattr(self, "h", None):
+            self.lib.q3a_destroy(self.h)
+            self.h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def set_stream(self, stream_handle: int | None):
+        check(self.lib.q3a_set_stream(self.h, stream_handle))
+
+    def sync(self):
+        check(self.lib.q3a_sync(self.h))
+
+    def check_device_error(self):
+        check(self.lib.q3a_check_device_error(self.h))
+
+    def launch_count(self) -> int:
+        return int(self.lib.q3a_launch_count(self.h))
+
+    def attn_layer(self, xb, q, k, v, qw, kw, layer, pos):
+        check(self.lib.q3a_attn_layer(self.h, ptr(xb), ptr(q), ptr(k), ptr(v), ptr(qw), ptr(kw),
+                                      layer, pos))
+
+    def attn_layer_batched(self, xb, q, k, v, qw, kw, layer, seq_ids, pos):
+        import numpy as np
+        sid = np.ascontiguousarray(seq_ids, np.int32)
+        ps = np.ascontiguousarray(pos, np.int32)
+        check(self.lib.q3a_attn_layer_batched(self.h, ptr(xb), ptr(q), ptr(k), ptr(v), ptr(qw),
+                                              ptr(kw), layer, ptr(sid), ptr(ps), len(sid)))
+
+    def attn_decode(self, xb, q, kc, vc, att, loff, pos, n_heads, kv_mul, hd, kv_dim, max_seq):
+        check(self.lib.q3a_attn_decode(self.h, ptr(xb), ptr(q), ptr(kc), ptr(vc), ptr(att), loff,
+                                       pos, n_heads, kv_mul, hd, kv_dim, max_seq))
+
+    def kv_append(self, seq, layer, pos0, n, k, v, kw):
+        check(self.lib.q3a_kv_append(self.h, seq, layer, pos0, n, ptr(k), ptr(v), ptr(kw)))
+
+    def kv_load(self, seq, layer, pos0, n, k, v):
+        check(self.lib.q3a_kv_load(self.h, seq, layer, pos0, n, ptr(k), ptr(v)))
+
+    def kv_read(self, seq, layer, pos0, n, k, v):
+        check(self.lib.q3a_kv_read(self.h, seq, layer, pos0, n, ptr(k), ptr(v)))
+
+    def prefill(self, out, out_dtype, q, k, v, qw, kw, seq, layer, pos0, n_tok):
+        check(self.lib.q3a_prefill(self.h, ptr(out), out_dtype, ptr(q), ptr(k), ptr(v), ptr(qw),
+                                   ptr(kw), seq, layer, pos0, n_tok))
+
+    def prefill_attn(self, out, out_dtype, q_bf16, seq, layer, pos0, n_tok):
+        check(self.lib.q3a_prefill_attn(self.h, ptr(out), out_dtype, ptr(q_bf16), seq, layer, pos0,
+                                        n_tok))
+
+    def attn_partial(self, o, lse, q, seq, layer, t0, t1):
+        check(self.lib.q3a_attn_partial(self.h, ptr(o), ptr(lse), ptr(q), seq, layer, t0, t1))
+
+    def lse_combine(self, xb, o_parts, lse_parts, n_parts):
+        check(self.lib.q3a_lse_combine(self.h, ptr(xb), ptr(o_parts), ptr(lse_parts), n_parts))
+
+    def randn(self, dst, out_dtype, n, seed, stream_id, offset=0):
+        check(self.lib.q3a_randn(self.h, ptr(dst), out_dtype, n, seed, stream_id, offset))
