@@ -86,7 +86,6 @@ struct q3a_ctx {
     long long total_rows; // cache rows per K (or V) pool
     void* kcache = nullptr;
     void* vcache = nullptr;
-    int* page_table = nullptr;
     float* partials = nullptr;
     long long part_slots = 0;
     int* counters = nullptr;
@@ -97,6 +96,7 @@ struct q3a_ctx {
     CUtensorMap tmK, tmV;          // decode maps of the paged cache
     CUtensorMap tmKp, tmVp;        // prefill maps (bf16, 128B swizzle)
     float inv_freq[64];
+    float* d_inv_freq = nullptr;   // the same table in device memory
     // host-mode staging
     float* h_stage = nullptr;      // pinned
     float* d_stage = nullptr;
@@ -168,10 +168,10 @@ static void destroy_ctx(q3a_ctx* c) {
     if (c->stream) cudaStreamSynchronize(c->stream);
     cudaFree(c->kcache);
     cudaFree(c->vcache);
-    cudaFree(c->page_table);
     cudaFree(c->partials);
     cudaFree(c->counters);
     cudaFree(c->err);
+    cudaFree(c->d_inv_freq);
     cudaFree(c->d_stage);
     cudaFree(c->d_scratch);
     if (c->h_stage) cudaFreeHost(c->h_stage);
@@ -243,14 +243,12 @@ extern "C" int q3a_create(q3a_ctx** out, const q3a_cfg* cfg_in) {
         destroy_ctx(c);
         return fail(Q3A_ERR_OOM, "KV cache of 2 x %zu bytes", cache_bytes);
     }
-    std::vector<int> pt((size_t)cfg.n_seqs * c->pages_per_seq);
-    for (size_t i = 0; i < pt.size(); i++) pt[i] = (int)i;  // slot s owns pages [s*pps, (s+1)*pps)
     const int max_groups = Q3A_MAX_BATCH * cfg.n_kv_heads;
     c->part_slots = (long long)c->num_sms + max_groups;
-    if (cudaMalloc(&c->page_table, pt.size() * sizeof(int)) != cudaSuccess ||
-        cudaMalloc(&c->partials, (size_t)c->part_slots * PART_STRIDE * 4) != cudaSuccess ||
+    if (cudaMalloc(&c->partials, (size_t)c->part_slots * PART_STRIDE * 4) != cudaSuccess ||
         cudaMalloc(&c->counters, (size_t)max_groups * sizeof(int)) != cudaSuccess ||
-        cudaMalloc(&c->err, sizeof(int)) != cudaSuccess) {
+        cudaMalloc(&c->err, sizeof(int)) != cudaSuccess ||
+        cudaMalloc(&c->d_inv_freq, sizeof(c->inv_freq)) != cudaSuccess) {
         destroy_ctx(c);
         return fail(Q3A_ERR_OOM, "context scratch");
     }
@@ -263,16 +261,16 @@ extern "C" int q3a_create(q3a_ctx** out, const q3a_cfg* cfg_in) {
         cudaMemsetAsync(c->vcache, 0, cache_bytes, c->stream) != cudaSuccess ||
         cudaMemsetAsync(c->counters, 0, (size_t)max_groups * sizeof(int), c->stream) != cudaSuccess ||
         cudaMemsetAsync(c->err, 0, sizeof(int), c->stream) != cudaSuccess ||
-        cudaMemcpyAsync(c->page_table, pt.data(), pt.size() * sizeof(int), cudaMemcpyHostToDevice,
+        cudaMemcpyAsync(c->d_inv_freq, c->inv_freq, sizeof(c->inv_freq), cudaMemcpyHostToDevice,
                         c->stream) != cudaSuccess ||
         cudaStreamSynchronize(c->stream) != cudaSuccess) {
         destroy_ctx(c);
         return fail(Q3A_ERR_CUDA, "cache initialisation");
     }
-    rc = make_map_2d(&c->tmK, c->kcache, c->bf16, HD, (uint64_t)c->total_rows, HD, DEC_TILE,
+    rc = make_map_2d(&c->tmK, c->kcache, c->bf16, HD, (uint64_t)c->total_rows, HD, DEC_BOX,
                      CU_TENSOR_MAP_SWIZZLE_NONE);
     if (rc == Q3A_OK)
-        rc = make_map_2d(&c->tmV, c->vcache, c->bf16, HD, (uint64_t)c->total_rows, HD, DEC_TILE,
+        rc = make_map_2d(&c->tmV, c->vcache, c->bf16, HD, (uint64_t)c->total_rows, HD, DEC_BOX,
                          CU_TENSOR_MAP_SWIZZLE_NONE);
     if (rc == Q3A_OK && c->bf16) {
         rc = make_map_2d(&c->tmKp, c->kcache, true, HD, (uint64_t)c->total_rows, 64, 128,
@@ -341,7 +339,6 @@ static void base_params(q3a_ctx* c, DecodeParams& p, int layer) {
     memset(&p, 0, sizeof(p));
     p.kcache = c->kcache;
     p.vcache = c->vcache;
-    p.page_table = c->page_table;
     p.partials = c->partials;
     p.counters = c->counters;
     p.err = c->err;
@@ -356,10 +353,83 @@ static void base_params(q3a_ctx* c, DecodeParams& p, int layer) {
     p.page_tokens = c->cfg.page_tokens;
     p.n_pages = c->n_pages;
     p.cache_mode = CACHE_PAGED;
-    memcpy(p.inv_freq, c->inv_freq, sizeof(p.inv_freq));
+    p.inv_freq = c->d_inv_freq;
 }
 
-// Fills unit_prefix / total_units / n_ctas from t_begin, t_end, fused.
+// Piece-mode schedule: every (sequence, kv head) group gets k_g >= 1 CTAs in
+// proportion to its rows (largest-quotient rounding to the SM count), and its
+// rows are cut into k_g ranges at multiples of the 16-row TMA box, so one CTA
+// handles one range of one group.  Pieces are numbered group-major, which
+// makes the pieces (and partial slots) of a group consecutive.
+static void schedule_pieces(q3a_ctx* c, DecodeParams& p) {
+    const int nkv = p.nkv;
+    const int ng = p.nb * nkv;
+    const int G = std::min(c->num_sms, MAX_PIECES);
+    std::vector<double> work(ng);
+    std::vector<int> k(ng), cap(ng);
+    double total = 0.0;
+    for (int g = 0; g < ng; g++) {
+        const int b = g / nkv;
+        const int tb = p.t_begin[b], te = p.t_end[b];
+        const int rows = te - tb;
+        work[g] = rows + (p.fused ? 16.0 : 0.0);  // the new token costs about one box
+        total += work[g];
+        const int first = (tb / DEC_BOX + 1) * DEC_BOX;
+        const int last = te > 0 ? ((te - 1) / DEC_BOX) * DEC_BOX : -1;
+        cap[g] = 1 + (last >= first ? (last - first) / DEC_BOX + 1 : 0);
+    }
+    int sum = 0;
+    for (int g = 0; g < ng; g++) {
+        int kk = (int)std::floor(G * work[g] / total);
+        k[g] = std::max(1, std::min(kk, cap[g]));
+        sum += k[g];
+    }
+    while (sum > G) {  // only when many small groups were lifted to 1
+        int best = -1;
+        for (int g = 0; g < ng; g++)
+            if (k[g] > 1 && (best < 0 || work[g] / (k[g] - 1) < work[best] / (k[best] - 1))) best = g;
+        if (best < 0) break;
+        k[best]--;
+        sum--;
+    }
+    while (sum < G) {
+        int best = -1;
+        for (int g = 0; g < ng; g++)
+            if (k[g] < cap[g] && (best < 0 || work[g] / k[g] > work[best] / k[best])) best = g;
+        if (best < 0) break;
+        k[best]++;
+        sum++;
+    }
+    int np = 0;
+    for (int g = 0; g < ng; g++) {
+        const int b = g / nkv;
+        const int tb = p.t_begin[b], te = p.t_end[b];
+        const long long rows = te - tb;
+        int bnd[MAX_PIECES + 1];
+        int nb = 0;
+        bnd[nb++] = tb;
+        for (int j = 1; j < k[g]; j++) {
+            const long long target = tb + j * rows / k[g];
+            int a = (int)(((target + DEC_BOX / 2) / DEC_BOX) * DEC_BOX);
+            if (a > bnd[nb - 1] && a < te) bnd[nb++] = a;
+        }
+        bnd[nb++] = te;
+        const int kg = nb - 1;
+        for (int j = 0; j < kg; j++) {
+            Piece& pc = p.pieces[np++];
+            pc.g = g;
+            pc.r0 = bnd[j];
+            pc.r1 = bnd[j + 1];
+            pc.i = (short)j;
+            pc.k = (short)kg;
+        }
+    }
+    p.n_pieces = np;
+    p.n_ctas = np;
+}
+
+// Fills the schedule: piece mode when every group can have its own CTA,
+// else the linear unit list (unit_prefix / total_units / n_ctas).
 static int schedule(q3a_ctx* c, DecodeParams& p) {
     long long acc = 0;
     p.unit_prefix[0] = 0;
@@ -373,7 +443,12 @@ static int schedule(q3a_ctx* c, DecodeParams& p) {
         p.unit_prefix[b + 1] = acc;
     }
     p.total_units = acc;
-    p.n_ctas = (int)std::min<long long>(c->num_sms, acc);
+    p.n_pieces = 0;
+    if ((long long)p.nb * p.nkv <= std::min(c->num_sms, MAX_PIECES)) {
+        schedule_pieces(c, p);
+    } else {
+        p.n_ctas = (int)std::min<long long>(c->num_sms, acc);
+    }
     const long long slots = (long long)p.n_ctas + (long long)p.nb * p.nkv;
     if (slots > c->part_slots) return fail(Q3A_ERR_INVALID, "decode scratch too small");
     return Q3A_OK;
@@ -558,9 +633,9 @@ extern "C" int q3a_attn_decode(q3a_ctx* c, float* xb, const float* q, const floa
         dq = sq;
     }
     CUtensorMap tk, tv;
-    rc = make_map_2d(&tk, dk, false, (uint64_t)kv_dim, rows, HD, DEC_TILE, CU_TENSOR_MAP_SWIZZLE_NONE);
+    rc = make_map_2d(&tk, dk, false, (uint64_t)kv_dim, rows, HD, DEC_BOX, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (rc) return rc;
-    rc = make_map_2d(&tv, dv, false, (uint64_t)kv_dim, rows, HD, DEC_TILE, CU_TENSOR_MAP_SWIZZLE_NONE);
+    rc = make_map_2d(&tv, dv, false, (uint64_t)kv_dim, rows, HD, DEC_BOX, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (rc) return rc;
     p.q = dq;
     p.xb = dxb;
@@ -663,7 +738,6 @@ static int cache_io_params(q3a_ctx* c, AppendParams& a, int seq, int layer, int 
     memset(&a, 0, sizeof(a));
     a.kcache = c->kcache;
     a.vcache = c->vcache;
-    a.page_table = c->page_table;
     a.eps = c->cfg.norm_eps;
     a.n = n;
     a.nkv = c->nkv;
@@ -676,7 +750,7 @@ static int cache_io_params(q3a_ctx* c, AppendParams& a, int seq, int layer, int 
     a.page_tokens = c->cfg.page_tokens;
     a.n_pages = c->n_pages;
     a.bf16 = c->bf16;
-    memcpy(a.inv_freq, c->inv_freq, sizeof(a.inv_freq));
+    a.inv_freq = c->d_inv_freq;
     return Q3A_OK;
 }
 
@@ -814,7 +888,7 @@ extern "C" int q3a_prefill(q3a_ctx* c, void* out, int out_dtype, const float* q,
     pp.nheads_total = c->cfg.n_heads;
     pp.pos0 = pos0;
     pp.do_norm_rope = 1;
-    memcpy(pp.inv_freq, c->inv_freq, sizeof(pp.inv_freq));
+    pp.inv_freq = c->d_inv_freq;
     CUDA_TRY(launch_prep_rows(pp, c->stream));
     c->launches++;
     a.k = dk;

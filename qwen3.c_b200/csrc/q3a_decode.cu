@@ -6,25 +6,32 @@
 // and KV append of the new token (qwen3-8b/cpu/main.c:1319-1329).
 //
 // Design (one launch per layer):
-//  * Work = 64-token cache tiles of every (sequence, KV head) group, plus one
-//    "new token" unit per group in fused mode.  A persistent grid of at most
-//    one CTA per SM takes an equal contiguous share of the unit list, so any
-//    mix of sequence lengths (the ragged batch included) is balanced to within
-//    one tile per SM.
-//  * Warp 8 of each CTA is the producer: one lane streams K and V tiles into a
-//    ring of shared-memory stages with 2-D TMA loads (cp.async.bulk.tensor)
-//    completing on per-stage mbarriers, with an L2 evict-first policy since
-//    the cache is read once per step.
-//  * Warps 0-7 consume: each takes 8 rows of a tile, so every K/V element
-//    leaves shared memory once and feeds all 4 query heads of its KV head (the
-//    HIP kernel re-reads K/V once per query head).  q.k uses 8 lanes per row
-//    with 16 dims each and a reduce-scatter of 7 shuffles for 8 rows x 4
-//    heads; each warp keeps its own online-softmax state (max, sum, o) in
-//    registers in log2 units, so no CTA-wide barrier is taken per tile.
-//  * At the end of a group's share the 8 warp states merge through shared
-//    memory; if several CTAs share a group they write normalised partials
-//    (o, lse) to scratch and the last CTA to arrive (atomic counter, reset by
-//    that CTA) merges them by log-sum-exp and writes xb.
+//  * Work is split into contiguous cache-row ranges of (sequence, KV head)
+//    groups.  With at most one group per SM (the single-sequence decode of the
+//    reference) every CTA gets exactly one range, sized so that ranges are
+//    equal to within one 16-row TMA box; larger batches use a linear list of
+//    64-row tiles cut into equal shares.  Grid size <= SM count, one CTA per
+//    SM.
+//  * Warp 8 is the producer: one lane streams K and V into a ring of
+//    64-row shared-memory stages, each tile of the paged cache as one bulk
+//    copy per tensor (cp.async.bulk; a tile lies in one page, so it is
+//    contiguous), with an L2 evict-first policy since each cache row is read
+//    once per step, completing on per-stage mbarriers.  The caller-owned
+//    position-major cache of q3a_attn_decode is strided and moves in 16-row
+//    2-D TMA boxes (cp.async.bulk.tensor) instead.
+//  * Warps 0-7 consume: each takes 8 rows of a stage, so every K/V element
+//    leaves shared memory once and feeds all 4 query heads of its KV head.
+//    q.k uses 8 lanes per row with 16 dims each (packed fp32x2 FMA), then a
+//    7-shuffle reduce-scatter gives one (row, head) score per lane; each warp
+//    keeps its own online-softmax state (log2 domain) in registers, so no
+//    CTA-wide barrier is taken per tile.
+//  * The prologue issues every global load of the range's inputs at once (q,
+//    norm gains, the new token's k and v) and reduces the RMS norms with warp
+//    shuffles, overlapping the first TMA round trip.
+//  * At the end of a range the 8 warp states merge through shared memory;
+//    ranges sharing a group write normalised partials (o, lse) to scratch and
+//    the last CTA to arrive (atomic counter, reset by that CTA) merges them by
+//    log-sum-exp into xb.
 #include "q3a_common.cuh"
 #include "q3a_internal.h"
 
@@ -38,31 +45,61 @@ struct DecCfg {
     static constexpr int NTHREADS = NCONS + 32;
     static constexpr int STAGES = sizeof(KV) == 4 ? 3 : 6;
     static constexpr int TILE_BYTES = TILE * HD * (int)sizeof(KV);
+    static constexpr int BOX_BYTES = DEC_BOX * HD * (int)sizeof(KV);
     static constexpr int OFF_K = 0;
     static constexpr int OFF_V = STAGES * TILE_BYTES;
     static constexpr int OFF_QS = 2 * STAGES * TILE_BYTES;       // float [4][128]
-    static constexpr int OFF_NEWK = OFF_QS + GQA * HD * 4;       // KV [8][128] (row 0 used)
-    static constexpr int OFF_NEWV = OFF_NEWK + 8 * HD * (int)sizeof(KV);
-    static constexpr int OFF_P = OFF_NEWV + 8 * HD * (int)sizeof(KV);  // float [8 warps][32]
-    static constexpr int WST = GQA * HD + 8;                     // o[4][128], m[4], l[4]
-    static constexpr int OFF_WST = OFF_P + CWARPS * 32 * 4;
+    static constexpr int OFF_RAW = OFF_QS + GQA * HD * 4;        // float [256] norm gains / raw k,v
+    static constexpr int OFF_RAW2 = OFF_RAW + 256 * 4;           // float [256]
+    static constexpr int OFF_NEWK = OFF_RAW2 + 256 * 4;          // KV [128]
+    static constexpr int OFF_NEWV = OFF_NEWK + HD * (int)sizeof(KV);
+    static constexpr int OFF_P = OFF_NEWV + HD * (int)sizeof(KV);  // float2 [8 warps][32]
+    static constexpr int WST = GQA * HD + 8;                       // o[4][128], m[4], l[4]
+    static constexpr int OFF_WST = OFF_P + CWARPS * 32 * 8;
     static constexpr int OFF_BAR = OFF_WST + CWARPS * WST * 4;
     static constexpr int OFF_MISC = OFF_BAR + 2 * STAGES * 8;
     static constexpr int SMEM = OFF_MISC + 64;
     static_assert(SMEM <= 232448, "decode shared memory exceeds the sm_100 limit");
 };
 
-// Segment of the unit list that one CTA processes for one group.
-struct Seg {
-    int b;                 // sequence index within the launch
-    int kvh;               // local kv head
-    long long gstart;      // first unit of the group
-    long long gend;        // one past its last unit
-    int ncu;               // cache-tile units of the group
-    int a0;                // absolute tile index of cache unit 0
+// One contiguous range of cache rows of one group, as processed by a CTA.
+struct SegInfo {
+    int b;          // sequence index within the launch
+    int kvh;        // local kv head
+    int r0, r1;     // cache rows [r0, r1) streamed from the cache
+    int has_new;    // this range also handles the new token (fused)
+    int slot;       // partial slot of this range
+    int slot0;      // first partial slot of the group
+    int ncontrib;   // ranges of the group
+    int grp;        // group index (arrival counter)
 };
 
-__device__ __forceinline__ void locate(const DecodeParams& P, long long x, Seg& s) {
+__device__ __forceinline__ int cta_of(const DecodeParams& P, long long x) {
+    return (int)(((x + 1) * (long long)P.n_ctas - 1) / P.total_units);
+}
+
+// Next range of CTA c; `cur` is the linear-mode cursor (unit index).
+__device__ __forceinline__ bool next_seg(const DecodeParams& P, int c, long long& cur,
+                                         SegInfo& s) {
+    if (P.n_pieces > 0) {
+        if (cur != 0) return false;
+        cur = 1;
+        const Piece pc = P.pieces[c];
+        s.b = pc.g / P.nkv;
+        s.kvh = pc.g % P.nkv;
+        s.r0 = pc.r0;
+        s.r1 = pc.r1;
+        s.has_new = P.fused && pc.i == pc.k - 1;
+        s.slot = c;
+        s.slot0 = c - pc.i;
+        s.ncontrib = pc.k;
+        s.grp = pc.g;
+        return true;
+    }
+    const long long u_hi = (long long)(c + 1) * P.total_units / P.n_ctas;
+    if (cur == 0) cur = (long long)c * P.total_units / P.n_ctas + 1;  // stored +1
+    const long long x = cur - 1;
+    if (x >= u_hi) return false;
     int lo = 0, hi = P.nb;
     while (hi - lo > 1) {
         const int mid = (lo + hi) >> 1;
@@ -71,33 +108,59 @@ __device__ __forceinline__ void locate(const DecodeParams& P, long long x, Seg& 
     const int b = lo;
     const long long per = (P.unit_prefix[b + 1] - P.unit_prefix[b]) / P.nkv;
     const long long off = x - P.unit_prefix[b];
-    s.b = b;
-    s.kvh = (int)(off / per);
-    s.gstart = P.unit_prefix[b] + (long long)s.kvh * per;
-    s.gend = s.gstart + per;
+    const int kvh = (int)(off / per);
+    const long long gstart = P.unit_prefix[b] + (long long)kvh * per;
+    const long long gend = gstart + per;
+    const long long seg_end = min(u_hi, gend);
     const int tb = P.t_begin[b], te = P.t_end[b];
-    s.a0 = tb / DEC_TILE;
-    s.ncu = te > tb ? (te + DEC_TILE - 1) / DEC_TILE - s.a0 : 0;
-}
-
-__device__ __forceinline__ int cta_of(const DecodeParams& P, long long x) {
-    return (int)(((x + 1) * (long long)P.n_ctas - 1) / P.total_units);
+    const int a0 = tb / DEC_TILE;
+    const int ncu = te > tb ? (te + DEC_TILE - 1) / DEC_TILE - a0 : 0;
+    const int uf = (int)(x - gstart), ul = (int)(seg_end - 1 - gstart);
+    if (uf < ncu) {
+        s.r0 = max(tb, (a0 + uf) * DEC_TILE);
+        s.r1 = min(te, (a0 + min(ul, ncu - 1) + 1) * DEC_TILE);
+    } else {
+        s.r0 = s.r1 = te;
+    }
+    s.b = b;
+    s.kvh = kvh;
+    s.has_new = P.fused && seg_end == gend;
+    const int grp = b * P.nkv + kvh;
+    const int cs = cta_of(P, gstart), ce = cta_of(P, gend - 1);
+    s.slot = c + grp;
+    s.slot0 = cs + grp;
+    s.ncontrib = ce - cs + 1;
+    s.grp = grp;
+    cur = seg_end + 1;
+    return true;
 }
 
 // Row of the paged cache holding position `t` of (slot, local kv head).
+// Slot s owns pages [s*pages_per_seq, (s+1)*pages_per_seq) of every
+// (layer, kv head) region, so the address is arithmetic only.
 __device__ __forceinline__ long long paged_row(const DecodeParams& P, int slot, int kvh, int t) {
     const int pt = P.page_tokens;
-    const int phys = P.page_table[(long long)slot * P.pages_per_seq + t / pt];
+    const long long phys = (long long)slot * P.pages_per_seq + t / pt;
     return (((long long)P.layer * P.nkv + kvh) * P.n_pages + phys) * pt + (t % pt);
 }
 
-// q registers of one lane: 4 heads x 16 dims, pre-scaled by log2(e)/sqrt(hd).
-// fp32 tiles: lane j=lane&7 holds dims 4j+32s+e (s<4, e<4);
-// bf16 tiles: dims 8j+64s+e (s<2, e<8); both give conflict-free 16-byte
-// shared loads (8 lanes of a row read 128 consecutive bytes).
+// acq_rel atomic add at GPU scope: releases this CTA's partial (ordered
+// before it by the preceding CTA barrier) and, for the last arrival,
+// acquires every other contributor's.
+__device__ __forceinline__ int atom_add_acq_rel(int* p, int v) {
+    int old;
+    asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v)
+                 : "memory");
+    return old;
+}
+
+// q registers of one lane as fp32 pairs, 4 heads x 16 dims, pre-scaled by
+// log2(e)/sqrt(hd).  fp32 tiles: lane j=lane&7 holds dims 4j+32s+e (s<4,
+// e<4); bf16 tiles: dims 8j+64s+e (s<2, e<8); both give conflict-free 16-byte
+// shared loads (the 8 lanes of a row read 128 consecutive bytes).
 template <typename KV>
 __device__ __forceinline__ void load_q_regs(const float* sQ, int lane, float sl2e,
-                                            float (&qr)[GQA][16]) {
+                                            float2 (&qr)[GQA][8]) {
     const int j = lane & 7;
 #pragma unroll
     for (int h = 0; h < GQA; h++) {
@@ -105,10 +168,8 @@ __device__ __forceinline__ void load_q_regs(const float* sQ, int lane, float sl2
 #pragma unroll
             for (int s = 0; s < 4; s++) {
                 const float4 t = *reinterpret_cast<const float4*>(sQ + h * HD + 4 * j + 32 * s);
-                qr[h][4 * s + 0] = t.x * sl2e;
-                qr[h][4 * s + 1] = t.y * sl2e;
-                qr[h][4 * s + 2] = t.z * sl2e;
-                qr[h][4 * s + 3] = t.w * sl2e;
+                qr[h][2 * s] = make_float2(t.x * sl2e, t.y * sl2e);
+                qr[h][2 * s + 1] = make_float2(t.z * sl2e, t.w * sl2e);
             }
         } else {
 #pragma unroll
@@ -116,14 +177,10 @@ __device__ __forceinline__ void load_q_regs(const float* sQ, int lane, float sl2
                 const float4 t0 = *reinterpret_cast<const float4*>(sQ + h * HD + 8 * j + 64 * s);
                 const float4 t1 =
                     *reinterpret_cast<const float4*>(sQ + h * HD + 8 * j + 64 * s + 4);
-                qr[h][8 * s + 0] = t0.x * sl2e;
-                qr[h][8 * s + 1] = t0.y * sl2e;
-                qr[h][8 * s + 2] = t0.z * sl2e;
-                qr[h][8 * s + 3] = t0.w * sl2e;
-                qr[h][8 * s + 4] = t1.x * sl2e;
-                qr[h][8 * s + 5] = t1.y * sl2e;
-                qr[h][8 * s + 6] = t1.z * sl2e;
-                qr[h][8 * s + 7] = t1.w * sl2e;
+                qr[h][4 * s + 0] = make_float2(t0.x * sl2e, t0.y * sl2e);
+                qr[h][4 * s + 1] = make_float2(t0.z * sl2e, t0.w * sl2e);
+                qr[h][4 * s + 2] = make_float2(t1.x * sl2e, t1.y * sl2e);
+                qr[h][4 * s + 3] = make_float2(t1.z * sl2e, t1.w * sl2e);
             }
         }
     }
@@ -133,59 +190,142 @@ __device__ __forceinline__ float sel4(const float (&a)[4], int i) {
     return i == 0 ? a[0] : i == 1 ? a[1] : i == 2 ? a[2] : a[3];
 }
 
-// One warp's share (rows 8w..8w+7, restricted to [lo, hi)) of a K/V tile.
-template <typename KV>
-__device__ __forceinline__ void process_rows(const KV* Kt, const KV* Vt, int lo, int hi, int warp,
-                                             int lane, const float (&qr)[GQA][16],
-                                             float (&m)[GQA], float& lpart,
-                                             float (&O)[GQA][4], float* pw) {
-    const int r0 = warp * 8;
-    const int rlo = max(lo - r0, 0), rhi = min(hi - r0, 8);
-    if (rlo >= rhi) return;
-    const int g = lane >> 3, j = lane & 7;
+__device__ __forceinline__ float2 bf16pair(uint32_t u) { return make_float2(bf16lo(u), bf16hi(u)); }
 
-    // ---- scores: acc[tt*4+h] for rows r0+2g+tt
-    float acc[8];
-#pragma unroll
-    for (int i = 0; i < 8; i++) acc[i] = 0.0f;
+// Scores of rows 2g and 2g+1 (relative to r0) of one warp's 8-row share:
+// acc[tt][h] holds fp32 pairs (even/odd dims) for row 2g+tt.  FULL_ROWS
+// selects the branch-free body (all 8 rows valid), so every shared-memory
+// load can be issued ahead of the math.
+template <typename KV, bool FULL_ROWS>
+__device__ __forceinline__ void qk_rows(const KV* Kt, int r0, int rlo, int rhi, int g, int j,
+                                        const float2 (&qr)[GQA][8], float2 (&acc)[2][GQA]) {
 #pragma unroll
     for (int tt = 0; tt < 2; tt++) {
-        const int rr = 2 * g + tt;
-        if (rr >= rlo && rr < rhi) {
-            const KV* kr = Kt + (r0 + rr) * HD;
-            if constexpr (sizeof(KV) == 4) {
 #pragma unroll
-                for (int s = 0; s < 4; s++) {
-                    const float4 kv =
-                        *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(kr) +
-                                                         4 * j + 32 * s);
+        for (int h = 0; h < GQA; h++) acc[tt][h] = make_float2(0.0f, 0.0f);
+    }
+    if constexpr (sizeof(KV) == 4) {
+        float4 kv[2][4];
 #pragma unroll
-                    for (int h = 0; h < GQA; h++) {
-                        float a = acc[tt * 4 + h];
-                        a = fmaf(qr[h][4 * s + 0], kv.x, a);
-                        a = fmaf(qr[h][4 * s + 1], kv.y, a);
-                        a = fmaf(qr[h][4 * s + 2], kv.z, a);
-                        a = fmaf(qr[h][4 * s + 3], kv.w, a);
-                        acc[tt * 4 + h] = a;
-                    }
-                }
-            } else {
+        for (int tt = 0; tt < 2; tt++) {
+            const int rr = 2 * g + tt;
+            const float* kr = reinterpret_cast<const float*>(Kt) + (r0 + rr) * HD + 4 * j;
 #pragma unroll
-                for (int s = 0; s < 2; s++) {
-                    const uint4 u = *reinterpret_cast<const uint4*>(
-                        reinterpret_cast<const __nv_bfloat16*>(kr) + 8 * j + 64 * s);
-                    const float k8[8] = {bf16lo(u.x), bf16hi(u.x), bf16lo(u.y), bf16hi(u.y),
-                                         bf16lo(u.z), bf16hi(u.z), bf16lo(u.w), bf16hi(u.w)};
+            for (int s = 0; s < 4; s++) {
+                if (FULL_ROWS || (rr >= rlo && rr < rhi))
+                    kv[tt][s] = *reinterpret_cast<const float4*>(kr + 32 * s);
+                else
+                    kv[tt][s] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            }
+        }
 #pragma unroll
-                    for (int h = 0; h < GQA; h++) {
-                        float a = acc[tt * 4 + h];
+        for (int tt = 0; tt < 2; tt++) {
 #pragma unroll
-                        for (int e = 0; e < 8; e++) a = fmaf(qr[h][8 * s + e], k8[e], a);
-                        acc[tt * 4 + h] = a;
-                    }
+            for (int s = 0; s < 4; s++) {
+                const float2 ka = make_float2(kv[tt][s].x, kv[tt][s].y);
+                const float2 kb = make_float2(kv[tt][s].z, kv[tt][s].w);
+#pragma unroll
+                for (int h = 0; h < GQA; h++) {
+                    acc[tt][h] = __ffma2_rn(qr[h][2 * s], ka, acc[tt][h]);
+                    acc[tt][h] = __ffma2_rn(qr[h][2 * s + 1], kb, acc[tt][h]);
                 }
             }
         }
+    } else {
+        uint4 ku[2][2];
+#pragma unroll
+        for (int tt = 0; tt < 2; tt++) {
+            const int rr = 2 * g + tt;
+            const __nv_bfloat16* kr =
+                reinterpret_cast<const __nv_bfloat16*>(Kt) + (r0 + rr) * HD + 8 * j;
+#pragma unroll
+            for (int s = 0; s < 2; s++) {
+                if (FULL_ROWS || (rr >= rlo && rr < rhi))
+                    ku[tt][s] = *reinterpret_cast<const uint4*>(kr + 64 * s);
+                else
+                    ku[tt][s] = make_uint4(0u, 0u, 0u, 0u);
+            }
+        }
+#pragma unroll
+        for (int tt = 0; tt < 2; tt++) {
+#pragma unroll
+            for (int s = 0; s < 2; s++) {
+                const float2 k2[4] = {bf16pair(ku[tt][s].x), bf16pair(ku[tt][s].y),
+                                      bf16pair(ku[tt][s].z), bf16pair(ku[tt][s].w)};
+#pragma unroll
+                for (int h = 0; h < GQA; h++) {
+#pragma unroll
+                    for (int e = 0; e < 4; e++)
+                        acc[tt][h] = __ffma2_rn(qr[h][4 * s + e], k2[e], acc[tt][h]);
+                }
+            }
+        }
+    }
+}
+
+// o += p . v over rows [rlo, rhi) of the warp's share; lane owns dims
+// 4*lane .. 4*lane+3; p for (row, head) is duplicated in pw[row*4+head].
+template <typename KV, bool FULL_ROWS>
+__device__ __forceinline__ void pv_rows(const KV* Vt, int r0, int rlo, int rhi, int lane,
+                                        const float2* pw, float2 (&O)[GQA][2]) {
+    float2 va[8], vb[8];
+#pragma unroll
+    for (int tt = 0; tt < 8; tt++) {
+        if (FULL_ROWS || (tt >= rlo && tt < rhi)) {
+            if constexpr (sizeof(KV) == 4) {
+                const float4 t = *reinterpret_cast<const float4*>(
+                    reinterpret_cast<const float*>(Vt) + (r0 + tt) * HD + 4 * lane);
+                va[tt] = make_float2(t.x, t.y);
+                vb[tt] = make_float2(t.z, t.w);
+            } else {
+                const uint2 u = *reinterpret_cast<const uint2*>(
+                    reinterpret_cast<const __nv_bfloat16*>(Vt) + (r0 + tt) * HD + 4 * lane);
+                va[tt] = bf16pair(u.x);
+                vb[tt] = bf16pair(u.y);
+            }
+        } else {
+            va[tt] = vb[tt] = make_float2(0.0f, 0.0f);  // p is 0 there too
+        }
+    }
+#pragma unroll
+    for (int tt = 0; tt < 8; tt++) {
+        const float4 pa = *reinterpret_cast<const float4*>(pw + 4 * tt);
+        const float4 pb = *reinterpret_cast<const float4*>(pw + 4 * tt + 2);
+        const float2 p0 = make_float2(pa.x, pa.y), p1 = make_float2(pa.z, pa.w);
+        const float2 p2 = make_float2(pb.x, pb.y), p3 = make_float2(pb.z, pb.w);
+        O[0][0] = __ffma2_rn(p0, va[tt], O[0][0]);
+        O[0][1] = __ffma2_rn(p0, vb[tt], O[0][1]);
+        O[1][0] = __ffma2_rn(p1, va[tt], O[1][0]);
+        O[1][1] = __ffma2_rn(p1, vb[tt], O[1][1]);
+        O[2][0] = __ffma2_rn(p2, va[tt], O[2][0]);
+        O[2][1] = __ffma2_rn(p2, vb[tt], O[2][1]);
+        O[3][0] = __ffma2_rn(p3, va[tt], O[3][0]);
+        O[3][1] = __ffma2_rn(p3, vb[tt], O[3][1]);
+    }
+}
+
+// One warp's share (rows 8w..8w+7, restricted to [lo, hi)) of a K/V tile.
+template <typename KV>
+__device__ __forceinline__ void process_rows(const KV* Kt, const KV* Vt, int lo, int hi, int warp,
+                                             int lane, const float2 (&qr)[GQA][8],
+                                             float (&m)[GQA], float& lpart,
+                                             float2 (&O)[GQA][2], float2* pw) {
+    const int r0 = warp * 8;
+    const int rlo = max(lo - r0, 0), rhi = min(hi - r0, 8);
+    if (rlo >= rhi) return;
+    const bool full = (rlo == 0 && rhi == 8);
+    const int g = lane >> 3, j = lane & 7;
+
+    float2 acc[2][GQA];
+    if (full)
+        qk_rows<KV, true>(Kt, r0, rlo, rhi, g, j, qr, acc);
+    else
+        qk_rows<KV, false>(Kt, r0, rlo, rhi, g, j, qr, acc);
+    float a8[8];
+#pragma unroll
+    for (int tt = 0; tt < 2; tt++) {
+#pragma unroll
+        for (int h = 0; h < GQA; h++) a8[tt * 4 + h] = acc[tt][h].x + acc[tt][h].y;
     }
     // ---- reduce-scatter over the 8 lanes of a row group: lane j ends with
     // the full sum of value index j (row 2g + (j>>2), head j&3).
@@ -194,8 +334,8 @@ __device__ __forceinline__ void process_rows(const KV* Kt, const KV* Vt, int lo,
         const bool b2 = (j & 4) != 0;
 #pragma unroll
         for (int i = 0; i < 4; i++) {
-            const float send = b2 ? acc[i] : acc[i + 4];
-            const float keep = b2 ? acc[i + 4] : acc[i];
+            const float send = b2 ? a8[i] : a8[i + 4];
+            const float keep = b2 ? a8[i + 4] : a8[i];
             r4[i] = keep + __shfl_xor_sync(FULL, send, 4);
         }
     }
@@ -236,38 +376,58 @@ __device__ __forceinline__ void process_rows(const KV* Kt, const KV* Vt, int lo,
         m[h] = __shfl_sync(FULL, m_new, h);
         al[h] = __shfl_sync(FULL, alpha, h);
     }
-    pw[lane] = p;  // index = row*4 + head
+    pw[lane] = make_float2(p, p);  // index = row*4 + head, duplicated for fp32x2 math
     __syncwarp();
 #pragma unroll
     for (int h = 0; h < GQA; h++) {
-#pragma unroll
-        for (int e = 0; e < 4; e++) O[h][e] *= al[h];
+        const float2 a2 = make_float2(al[h], al[h]);
+        O[h][0] = __fmul2_rn(O[h][0], a2);
+        O[h][1] = __fmul2_rn(O[h][1], a2);
     }
-    // ---- o += p . v  (lane owns dims 4*lane .. 4*lane+3)
-#pragma unroll
-    for (int tt = 0; tt < 8; tt++) {
-        if (tt >= rlo && tt < rhi) {
-            const float4 pv = reinterpret_cast<const float4*>(pw)[tt];
-            float v[4];
-            if constexpr (sizeof(KV) == 4) {
-                const float4 t = *reinterpret_cast<const float4*>(
-                    reinterpret_cast<const float*>(Vt) + (r0 + tt) * HD + 4 * lane);
-                v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
-            } else {
-                const uint2 u = *reinterpret_cast<const uint2*>(
-                    reinterpret_cast<const __nv_bfloat16*>(Vt) + (r0 + tt) * HD + 4 * lane);
-                v[0] = bf16lo(u.x); v[1] = bf16hi(u.x); v[2] = bf16lo(u.y); v[3] = bf16hi(u.y);
-            }
-#pragma unroll
-            for (int e = 0; e < 4; e++) {
-                O[0][e] = fmaf(pv.x, v[e], O[0][e]);
-                O[1][e] = fmaf(pv.y, v[e], O[1][e]);
-                O[2][e] = fmaf(pv.z, v[e], O[2][e]);
-                O[3][e] = fmaf(pv.w, v[e], O[3][e]);
-            }
-        }
-    }
+    if (full)
+        pv_rows<KV, true>(Vt, r0, rlo, rhi, lane, pw, O);
+    else
+        pv_rows<KV, false>(Vt, r0, rlo, rhi, lane, pw, O);
     __syncwarp();
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(FULL, v, o);
+    return v;
+}
+
+// QK-RMSNorm + RoPE of one 128-wide head held by a warp (lane: dims
+// 4*lane..4*lane+3, i.e. RoPE pairs 2*lane and 2*lane+1), as in
+// rmsnorm_head_inplace + apply_rope (qwen3-8b/cpu/main.c:1175-1183,
+// 1282-1295): v *= (1/sqrtf(mean(v^2)+eps)) * w, then pair rotation.
+__device__ __forceinline__ float4 norm_rope_lane(float4 x, float4 w, float eps, int pos,
+                                                 float2 inv_freq) {
+    float ss = __fadd_rn(__fadd_rn(__fmul_rn(x.x, x.x), __fmul_rn(x.y, x.y)),
+                         __fadd_rn(__fmul_rn(x.z, x.z), __fmul_rn(x.w, x.w)));
+    ss = warp_sum(ss);
+    const float sc = 1.0f / sqrtf(__fadd_rn(ss / (float)HD, eps));
+    float v0 = __fmul_rn(x.x, __fmul_rn(sc, w.x));
+    float v1 = __fmul_rn(x.y, __fmul_rn(sc, w.y));
+    float v2 = __fmul_rn(x.z, __fmul_rn(sc, w.z));
+    float v3 = __fmul_rn(x.w, __fmul_rn(sc, w.w));
+    rope_pair(v0, v1, pos, inv_freq.x);
+    rope_pair(v2, v3, pos, inv_freq.y);
+    return make_float4(v0, v1, v2, v3);
+}
+
+template <typename KV>
+__device__ __forceinline__ void store4(KV* dst, float4 v) {
+    if constexpr (sizeof(KV) == 4) {
+        *reinterpret_cast<float4*>(dst) = v;
+    } else {
+        __nv_bfloat162 a = __floats2bfloat162_rn(v.x, v.y);
+        __nv_bfloat162 b = __floats2bfloat162_rn(v.z, v.w);
+        uint2 u;
+        u.x = *reinterpret_cast<uint32_t*>(&a);
+        u.y = *reinterpret_cast<uint32_t*>(&b);
+        *reinterpret_cast<uint2*>(dst) = u;
+    }
 }
 
 template <typename KV>
@@ -279,49 +439,46 @@ __global__ void __launch_bounds__(DecCfg<KV>::NTHREADS, 1)
     KV* sK = reinterpret_cast<KV*>(smem + C::OFF_K);
     KV* sV = reinterpret_cast<KV*>(smem + C::OFF_V);
     float* sQ = reinterpret_cast<float*>(smem + C::OFF_QS);
+    float* sRaw = reinterpret_cast<float*>(smem + C::OFF_RAW);    // q gains | k gains
+    float* sRaw2 = reinterpret_cast<float*>(smem + C::OFF_RAW2);  // raw k | raw v
     KV* sNewK = reinterpret_cast<KV*>(smem + C::OFF_NEWK);
     KV* sNewV = reinterpret_cast<KV*>(smem + C::OFF_NEWV);
-    float* sP = reinterpret_cast<float*>(smem + C::OFF_P);
+    float2* sP = reinterpret_cast<float2*>(smem + C::OFF_P);
     float* sW = reinterpret_cast<float*>(smem + C::OFF_WST);
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
     uint64_t* empty = full + C::STAGES;
     volatile int* misc = reinterpret_cast<volatile int*>(smem + C::OFF_MISC);
-    float* sScale = reinterpret_cast<float*>(smem + C::OFF_MISC + 16);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int c = blockIdx.x;
-    if (tid == 0) {
-#pragma unroll
-        for (int s = 0; s < C::STAGES; s++) {
-            mbar_init(&full[s], 1);
-            mbar_init(&empty[s], C::CWARPS);
-        }
-        fence_mbar_init();
-    }
-    if (warp == C::CWARPS && lane == 0) {
-        tma_prefetch_desc(&tmK);
-        tma_prefetch_desc(&tmV);
-    }
-    __syncthreads();
-
-    const long long u_lo = (long long)c * P.total_units / P.n_ctas;
-    const long long u_hi = (long long)(c + 1) * P.total_units / P.n_ctas;
 
     if (warp == C::CWARPS) {
         // ================================================= producer
+        // The producer initialises the stage barriers and starts streaming
+        // at once; the consumers wait on named barrier 2 for the init only.
+        if (lane == 0) {
+#pragma unroll
+            for (int s = 0; s < C::STAGES; s++) {
+                mbar_init(&full[s], 1);
+                mbar_init(&empty[s], C::CWARPS);
+            }
+            fence_mbar_init();
+            tma_prefetch_desc(&tmK);
+            tma_prefetch_desc(&tmV);
+        }
+        __syncwarp();
+        named_bar_arrive(2, C::NTHREADS);
         if (lane == 0) {
             const uint64_t pol = l2_policy_evict_first();
             int it = 0;
             bool dead = false;
-            long long x = u_lo;
-            while (x < u_hi && !dead) {
-                Seg s;
-                locate(P, x, s);
-                const long long seg_end = min(u_hi, s.gend);
+            long long cur = 0;
+            SegInfo s;
+            while (!dead && next_seg(P, c, cur, s)) {
                 const int slot = P.slot[s.b];
-                for (long long y = x; y < seg_end; y++) {
-                    const int u = (int)(y - s.gstart);
-                    if (u >= s.ncu) continue;  // the new-token unit needs no load
+                const int lo_all = s.r0 & ~(DEC_BOX - 1);
+                const int hi_all = (s.r1 + DEC_BOX - 1) & ~(DEC_BOX - 1);
+                for (int t0 = (s.r0 / C::TILE) * C::TILE; t0 < s.r1; t0 += C::TILE) {
                     const int stage = it % C::STAGES;
                     const uint32_t ph = (uint32_t)(it / C::STAGES) & 1u;
                     if (it >= C::STAGES && !mbar_wait(&empty[stage], ph ^ 1u)) {
@@ -329,21 +486,29 @@ __global__ void __launch_bounds__(DecCfg<KV>::NTHREADS, 1)
                         dead = true;
                         break;
                     }
-                    const int t0 = (s.a0 + u) * DEC_TILE;
-                    int xc, yc;
+                    // rows [lo, hi) of this 64-aligned tile, 16-row aligned;
+                    // they lie in one cache page, so in the paged layout they
+                    // are contiguous and move as one bulk copy per tensor
+                    const int lo = max(t0, lo_all), hi = min(t0 + C::TILE, hi_all);
+                    const uint32_t bytes = (uint32_t)((hi - lo) * HD * (int)sizeof(KV));
+                    mbar_arrive_expect_tx(&full[stage], 2u * bytes);
+                    const int doff = (stage * C::TILE + (lo - t0)) * HD;
                     if (P.cache_mode == CACHE_PAGED) {
-                        xc = 0;
-                        yc = (int)paged_row(P, slot, s.kvh, t0);
+                        const long long row = paged_row(P, slot, s.kvh, lo);
+                        bulk_load(sK + doff, reinterpret_cast<const KV*>(P.kcache) + row * HD, bytes,
+                                  &full[stage], pol);
+                        bulk_load(sV + doff, reinterpret_cast<const KV*>(P.vcache) + row * HD, bytes,
+                                  &full[stage], pol);
                     } else {
-                        xc = (P.kv0 + s.kvh) * HD;
-                        yc = t0;
+                        const int xc = (P.kv0 + s.kvh) * HD;
+                        for (int t = lo; t < hi; t += DEC_BOX) {
+                            const int bo = doff + (t - lo) * HD;
+                            tma_load_2d(sK + bo, &tmK, &full[stage], xc, t, pol);
+                            tma_load_2d(sV + bo, &tmV, &full[stage], xc, t, pol);
+                        }
                     }
-                    mbar_arrive_expect_tx(&full[stage], 2u * C::TILE_BYTES);
-                    tma_load_2d(sK + stage * C::TILE * HD, &tmK, &full[stage], xc, yc, pol);
-                    tma_load_2d(sV + stage * C::TILE * HD, &tmV, &full[stage], xc, yc, pol);
                     it++;
                 }
-                x = seg_end;
             }
             // Drain: the CTA never exits with a bulk copy still writing its
             // shared memory (bounded, like every wait here).
@@ -359,111 +524,90 @@ __global__ void __launch_bounds__(DecCfg<KV>::NTHREADS, 1)
     }
 
     // ===================================================== consumers
+    named_bar_sync(2, C::NTHREADS);  // stage barriers initialised
     int it = 0;
-    long long x = u_lo;
-    float* pw = sP + warp * 32;
-    while (x < u_hi) {
-        Seg s;
-        locate(P, x, s);
-        const long long seg_end = min(u_hi, s.gend);
+    long long cur = 0;
+    SegInfo s;
+    float2* pw = sP + warp * 32;
+    while (next_seg(P, c, cur, s)) {
         const int b = s.b, kvh = s.kvh;
         const int hq0 = (P.kv0 + kvh) * GQA;
         const int slot = P.slot[b];
-        const bool has_new = P.fused && seg_end == s.gend;
 
-        // ---- query of the group: raw -> QK-RMSNorm -> RoPE (fused) or as is
-        const float* qsrc = P.q + (size_t)b * P.hq_total * HD + (size_t)hq0 * HD;
-        for (int i = tid; i < GQA * HD; i += C::NCONS) sQ[i] = qsrc[i];
-        if (has_new) {
-            const float* ksrc = P.k_new + (size_t)b * P.nkv_total * HD + (size_t)(P.kv0 + kvh) * HD;
-            if (tid < HD) sW[tid] = ksrc[tid];
+        // ---- prologue: one round of global loads, then norm + RoPE
+        float2 fr = make_float2(0.0f, 0.0f);
+        {
+            const float* qsrc = P.q + (size_t)b * P.hq_total * HD + (size_t)hq0 * HD;
+            const float2 qv = reinterpret_cast<const float2*>(qsrc)[tid];
+            if (P.fused) fr = reinterpret_cast<const float2*>(P.inv_freq)[lane];
+            float wv = 0.0f, kv = 0.0f;
+            if (P.fused) wv = tid < HD ? P.q_norm_w[tid] : P.k_norm_w[tid - HD];
+            if (s.has_new) {
+                const size_t o = (size_t)b * P.nkv_total * HD + (size_t)(P.kv0 + kvh) * HD;
+                kv = tid < HD ? P.k_new[o + tid] : P.v_new[o + tid - HD];
+            }
+            reinterpret_cast<float2*>(sQ)[tid] = qv;
+            sRaw[tid] = wv;
+            sRaw2[tid] = kv;
         }
         named_bar_sync(1, C::NCONS);
         if (P.fused) {
-            if (tid < GQA) sScale[tid] = head_rms_scale(sQ + tid * HD, P.eps);
-            if (has_new && tid == 32) sScale[4] = head_rms_scale(sW, P.eps);
-            named_bar_sync(1, C::NCONS);
-            {
-                const int h = tid >> 6, pi = tid & 63;
-                float* qp = sQ + h * HD + 2 * pi;
-                const float sc = sScale[h];
-                float v0 = __fmul_rn(qp[0], __fmul_rn(sc, P.q_norm_w[2 * pi]));
-                float v1 = __fmul_rn(qp[1], __fmul_rn(sc, P.q_norm_w[2 * pi + 1]));
-                rope_pair(v0, v1, P.pos[b], P.inv_freq[pi]);
-                qp[0] = v0;
-                qp[1] = v1;
-            }
-            if (has_new) {
-                // new token: k normed + rotated, v as is; stored in the cache
-                // dtype, appended at pos, and kept in shared memory for use.
+            if (warp < GQA) {
+                const float4 x = reinterpret_cast<const float4*>(sQ + warp * HD)[lane];
+                const float4 w = reinterpret_cast<const float4*>(sRaw)[lane];
+                reinterpret_cast<float4*>(sQ + warp * HD)[lane] =
+                    norm_rope_lane(x, w, P.eps, P.pos[b], fr);
+            } else if (warp == GQA && s.has_new) {
+                // new token's k: normalised, rotated, stored in the cache
+                // dtype, appended at pos and kept in shared memory for use
                 const int pos = P.pos[b];
-                const long long row = paged_row(P, slot, kvh, pos);
-                KV* kdst = reinterpret_cast<KV*>(P.kcache) + row * HD;
-                KV* vdst = reinterpret_cast<KV*>(P.vcache) + row * HD;
-                if (tid < 64) {
-                    const float sc = sScale[4];
-                    float v0 = __fmul_rn(sW[2 * tid], __fmul_rn(sc, P.k_norm_w[2 * tid]));
-                    float v1 = __fmul_rn(sW[2 * tid + 1], __fmul_rn(sc, P.k_norm_w[2 * tid + 1]));
-                    rope_pair(v0, v1, pos, P.inv_freq[tid]);
-                    if (P.k_out) {
-                        float* ko = P.k_out + (size_t)b * P.nkv_total * HD +
-                                    (size_t)(P.kv0 + kvh) * HD;
-                        ko[2 * tid] = v0;
-                        ko[2 * tid + 1] = v1;
-                    }
-                    const KV k0 = from_f32<KV>(v0), k1 = from_f32<KV>(v1);
-                    sNewK[2 * tid] = k0;
-                    sNewK[2 * tid + 1] = k1;
-                    kdst[2 * tid] = k0;
-                    kdst[2 * tid + 1] = k1;
-                } else if (tid < 64 + HD) {
-                    const int i = tid - 64;
-                    const float* vsrc = P.v_new + (size_t)b * P.nkv_total * HD +
-                                        (size_t)(P.kv0 + kvh) * HD;
-                    const KV vv = from_f32<KV>(vsrc[i]);
-                    sNewV[i] = vv;
-                    vdst[i] = vv;
+                const float4 x = reinterpret_cast<const float4*>(sRaw2)[lane];
+                const float4 w = reinterpret_cast<const float4*>(sRaw + HD)[lane];
+                const float4 kr = norm_rope_lane(x, w, P.eps, pos, fr);
+                if (P.k_out) {
+                    float* ko = P.k_out + (size_t)b * P.nkv_total * HD + (size_t)(P.kv0 + kvh) * HD;
+                    reinterpret_cast<float4*>(ko)[lane] = kr;
                 }
+                store4<KV>(sNewK + 4 * lane, kr);
+                const long long row = paged_row(P, slot, kvh, pos);
+                store4<KV>(reinterpret_cast<KV*>(P.kcache) + row * HD + 4 * lane, kr);
+            } else if (warp == GQA + 1 && s.has_new) {
+                const float4 vv = reinterpret_cast<const float4*>(sRaw2 + HD)[lane];
+                store4<KV>(sNewV + 4 * lane, vv);
+                const long long row = paged_row(P, slot, kvh, P.pos[b]);
+                store4<KV>(reinterpret_cast<KV*>(P.vcache) + row * HD + 4 * lane, vv);
             }
             named_bar_sync(1, C::NCONS);
         }
 
-        float qr[GQA][16];
+        float2 qr[GQA][8];
         load_q_regs<KV>(sQ, lane, P.scale_log2e, qr);
         float m[GQA] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
         float lpart = 0.0f;
-        float O[GQA][4];
+        float2 O[GQA][2];
 #pragma unroll
-        for (int h = 0; h < GQA; h++) {
-#pragma unroll
-            for (int e = 0; e < 4; e++) O[h][e] = 0.0f;
-        }
+        for (int h = 0; h < GQA; h++) O[h][0] = O[h][1] = make_float2(0.0f, 0.0f);
 
         bool dead = false;
-        for (long long y = x; y < seg_end; y++) {
-            const int u = (int)(y - s.gstart);
-            if (u < s.ncu) {
-                const int stage = it % C::STAGES;
-                const uint32_t ph = (uint32_t)(it / C::STAGES) & 1u;
-                if (!mbar_wait(&full[stage], ph)) {
-                    atomicExch(P.err, DEV_ERR_TIMEOUT);
-                    dead = true;
-                    break;
-                }
-                const int t0 = (s.a0 + u) * DEC_TILE;
-                const int lo = max(P.t_begin[b] - t0, 0);
-                const int hi = min(P.t_end[b] - t0, DEC_TILE);
-                process_rows<KV>(sK + stage * C::TILE * HD, sV + stage * C::TILE * HD, lo, hi,
-                                 warp, lane, qr, m, lpart, O, pw);
-                if (lane == 0) mbar_arrive(&empty[stage]);
-                it++;
-            } else {
-                process_rows<KV>(sNewK, sNewV, 0, 1, warp, lane, qr, m, lpart, O, pw);
+        for (int t0 = (s.r0 / C::TILE) * C::TILE; t0 < s.r1; t0 += C::TILE) {
+            const int stage = it % C::STAGES;
+            const uint32_t ph = (uint32_t)(it / C::STAGES) & 1u;
+            if (!mbar_wait(&full[stage], ph)) {
+                atomicExch(P.err, DEV_ERR_TIMEOUT);
+                dead = true;
+                break;
             }
+            const int lo = max(s.r0 - t0, 0);
+            const int hi = min(s.r1 - t0, C::TILE);
+            process_rows<KV>(sK + stage * C::TILE * HD, sV + stage * C::TILE * HD, lo, hi, warp,
+                             lane, qr, m, lpart, O, pw);
+            if (lane == 0) mbar_arrive(&empty[stage]);
+            it++;
         }
         if (dead) return;
+        if (s.has_new) process_rows<KV>(sNewK, sNewV, 0, 1, warp, lane, qr, m, lpart, O, pw);
 
-        // ---- merge the 8 warp states of this segment
+        // ---- merge the 8 warp states of this range
         float lsum = lpart;
         lsum += __shfl_xor_sync(FULL, lsum, 4);
         lsum += __shfl_xor_sync(FULL, lsum, 8);
@@ -473,7 +617,7 @@ __global__ void __launch_bounds__(DecCfg<KV>::NTHREADS, 1)
 #pragma unroll
             for (int h = 0; h < GQA; h++)
                 *reinterpret_cast<float4*>(ws + h * HD + 4 * lane) =
-                    make_float4(O[h][0], O[h][1], O[h][2], O[h][3]);
+                    make_float4(O[h][0].x, O[h][0].y, O[h][1].x, O[h][1].y);
             if (lane < 4) {
                 ws[GQA * HD + lane] = sel4(m, lane);
                 ws[GQA * HD + 4 + lane] = lsum;
@@ -493,49 +637,62 @@ __global__ void __launch_bounds__(DecCfg<KV>::NTHREADS, 1)
             o0 = fmaf(sW[w * C::WST + h * HD + d], sc, o0);
             o1 = fmaf(sW[w * C::WST + h * HD + d + 1], sc, o1);
         }
-        float inv = 1.0f / L;
+        const float inv = 1.0f / L;
         o0 *= inv;
         o1 *= inv;
         float lse = M + log2f(L);
 
-        const int cs = cta_of(P, s.gstart), ce = cta_of(P, s.gend - 1);
-        const int ncontrib = ce - cs + 1;
-        const int grp = b * P.nkv + kvh;
         bool write_out = true;
-        if (ncontrib > 1) {
-            const long long pslot = (long long)cs + grp + (c - cs);
-            float* ps = P.partials + pslot * PART_STRIDE;
-            ps[h * HD + d] = o0;
-            ps[h * HD + d + 1] = o1;
+        if (s.ncontrib > 1) {
+            float* ps = P.partials + (long long)s.slot * PART_STRIDE;
+            *reinterpret_cast<float2*>(ps + h * HD + d) = make_float2(o0, o1);
             if ((tid & 63) == 0) ps[GQA * HD + h] = lse;
-            __threadfence();
             named_bar_sync(1, C::NCONS);
             if (tid == 0) {
-                const int old = atomicAdd(&P.counters[grp], 1);
-                misc[0] = (old == ncontrib - 1) ? 1 : 0;
+                const int old = atom_add_acq_rel(&P.counters[s.grp], 1);
+                misc[0] = (old == s.ncontrib - 1) ? 1 : 0;
             }
             named_bar_sync(1, C::NCONS);
             write_out = misc[0] != 0;
             if (write_out) {
-                __threadfence();
-                const float* pb = P.partials + ((long long)cs + grp) * PART_STRIDE;
-                float Mx = -INFINITY;
-                for (int jj = 0; jj < ncontrib; jj++)
-                    Mx = fmaxf(Mx, __ldcg(pb + (long long)jj * PART_STRIDE + GQA * HD + h));
-                float W = 0.0f, a0 = 0.0f, a1 = 0.0f;
-                for (int jj = 0; jj < ncontrib; jj++) {
-                    const float* pj = pb + (long long)jj * PART_STRIDE;
-                    const float lj = __ldcg(pj + GQA * HD + h);
-                    const float wj = (lj == -INFINITY) ? 0.0f : exp2f(lj - Mx);
-                    W += wj;
-                    a0 = fmaf(wj, __ldcg(pj + h * HD + d), a0);
-                    a1 = fmaf(wj, __ldcg(pj + h * HD + d + 1), a1);
+                // every contributor's (lse, o) in one round of L2 loads per
+                // chunk of 32, merged with a running log-sum-exp
+                const float* pb = P.partials + (long long)s.slot0 * PART_STRIDE;
+                float Mx = -INFINITY, W = 0.0f, a0 = 0.0f, a1 = 0.0f;
+                for (int base = 0; base < s.ncontrib; base += 32) {
+                    float lj[32];
+                    float2 oj[32];
+#pragma unroll
+                    for (int jj = 0; jj < 32; jj++) {
+                        lj[jj] = -INFINITY;
+                        oj[jj] = make_float2(0.0f, 0.0f);
+                        if (base + jj < s.ncontrib) {
+                            const float* pj = pb + (long long)(base + jj) * PART_STRIDE;
+                            lj[jj] = __ldcg(pj + GQA * HD + h);
+                            oj[jj] = __ldcg(reinterpret_cast<const float2*>(pj + h * HD + d));
+                        }
+                    }
+                    float mc = Mx;
+#pragma unroll
+                    for (int jj = 0; jj < 32; jj++) mc = fmaxf(mc, lj[jj]);
+                    const float rs = (Mx == -INFINITY) ? 0.0f : exp2f(Mx - mc);
+                    W *= rs;
+                    a0 *= rs;
+                    a1 *= rs;
+#pragma unroll
+                    for (int jj = 0; jj < 32; jj++) {
+                        const float wj = (lj[jj] == -INFINITY) ? 0.0f : exp2f(lj[jj] - mc);
+                        W += wj;
+                        a0 = fmaf(wj, oj[jj].x, a0);
+                        a1 = fmaf(wj, oj[jj].y, a1);
+                    }
+                    Mx = mc;
                 }
                 const float iw = 1.0f / W;
                 o0 = a0 * iw;
                 o1 = a1 * iw;
                 lse = Mx + log2f(W);
-                if (tid == 0) P.counters[grp] = 0;
+                if (tid == 0) P.counters[s.grp] = 0;
             }
         }
         if (write_out) {
@@ -544,11 +701,10 @@ __global__ void __launch_bounds__(DecCfg<KV>::NTHREADS, 1)
             if (P.lse_out && (tid & 63) == 0) P.lse_out[(size_t)b * P.hq_total + hq0 + h] = lse;
             if (P.fused && P.q_out) {
                 float* qo = P.q_out + (size_t)b * P.hq_total * HD + (size_t)hq0 * HD;
-                for (int i = tid; i < GQA * HD; i += C::NCONS) qo[i] = sQ[i];
+                reinterpret_cast<float2*>(qo)[tid] = reinterpret_cast<const float2*>(sQ)[tid];
             }
         }
         named_bar_sync(1, C::NCONS);
-        x = seg_end;
     }
 }
 

@@ -12,7 +12,22 @@ namespace q3a {
 
 constexpr int MAX_B = Q3A_MAX_BATCH;
 constexpr int DEC_TILE = 64;        // cache tokens per pipeline stage (decode)
+constexpr int DEC_BOX = 16;         // rows per TMA box; split points are multiples of it
+constexpr int MAX_PIECES = 160;     // piece-mode schedule capacity (>= SM count)
 constexpr int PART_STRIDE = 4 * 128 + 4;  // floats per partial slot: o[4][128], lse[4]
+
+// One contiguous range of cache rows of one (sequence, kv head) group, the
+// unit of work of a CTA in piece mode.  Pieces of a group are numbered
+// consecutively (piece index = partial slot), i is the index within the
+// group and k the group's piece count; the piece with i == k-1 also handles
+// the new token in fused mode.
+struct Piece {
+    int g;       // group = b * nkv + local kv head
+    int r0;      // first cache row
+    int r1;      // one past the last cache row
+    short i;
+    short k;
+};
 
 // Where the decode kernel finds K/V rows.
 enum CacheMode : int {
@@ -20,11 +35,15 @@ enum CacheMode : int {
     CACHE_POSMAJOR = 1,   // caller cache [pos][kv_dim] (launch_attn layout)
 };
 
-// One decode launch.  The work is a list of units: for every (sequence b,
-// local kv head) group, ceil(Lc_b / DEC_TILE) cache tiles plus, when `fused`,
-// one unit for the new token (prepared and appended inside the kernel).
-// Units are numbered sequence-major, then kv head, then tile; CTA c owns
-// units [c*total/n_ctas, (c+1)*total/n_ctas).
+// One decode launch.  Two schedules:
+//  * piece mode (n_pieces > 0): CTA c processes pieces[c], one group-aligned
+//    row range; used when the groups fit the SMs, so no CTA pays for two
+//    groups' prologue and merge;
+//  * linear mode: the work is a list of units -- for every (sequence b,
+//    local kv head) group, ceil(Lc_b / DEC_TILE) cache tiles plus, when
+//    `fused`, one unit for the new token; units are numbered sequence-major,
+//    then kv head, then tile, and CTA c owns units
+//    [c*total/n_ctas, (c+1)*total/n_ctas).
 struct DecodeParams {
     const float* q;          // [nb][hq_total*128]; raw (fused) or prepared
     const float* k_new;      // [nb][nkv_total*128] raw (fused)
@@ -37,7 +56,6 @@ struct DecodeParams {
     float* lse_out;          // [nb][hq_total] log2-sum-exp output (partial mode), may be null
     void* kcache;            // paged caches (append target in fused mode)
     void* vcache;
-    const int* page_table;   // [n_seqs][pages_per_seq]
     float* partials;         // scratch: slots of PART_STRIDE floats
     int* counters;           // scratch: one per group, zero between launches
     int* err;                // device error flag
@@ -57,7 +75,9 @@ struct DecodeParams {
     int partial_out;         // 1: write normalised o + lse instead of xb
     long long total_units;
     int n_ctas;
-    float inv_freq[64];      // RoPE inverse frequencies (host powf, reference formula)
+    int n_pieces;            // > 0: piece mode with n_ctas == n_pieces
+    const float* inv_freq;   // [64] RoPE inverse frequencies (host powf, reference formula)
+    Piece pieces[MAX_PIECES];
     int t_begin[MAX_B];      // first cache position attended per sequence
     int t_end[MAX_B];        // one past the last cache position read from the cache
     int pos[MAX_B];          // new-token position (fused)
@@ -77,7 +97,7 @@ struct PrepParams {
     int nheads_total;        // heads per row in src / dst
     int pos0;                // position of row 0
     int do_norm_rope;
-    float inv_freq[64];
+    const float* inv_freq;   // [64] device table
 };
 
 struct AppendParams {
@@ -86,7 +106,6 @@ struct AppendParams {
     const float* k_norm_w;
     void* kcache;
     void* vcache;
-    const int* page_table;
     float eps;
     int n;
     int nkv;                 // local kv heads
@@ -100,7 +119,7 @@ struct AppendParams {
     int n_pages;
     int do_norm_rope;        // 0: rows are already prepared (kv_load)
     int bf16;
-    float inv_freq[64];
+    const float* inv_freq;   // [64] device table
 };
 
 // ---------------------------------------------------------------- launchers
@@ -119,7 +138,6 @@ cudaError_t launch_lse_combine(float* xb, const float* o_parts, const float* lse
 struct PrefillParams {
     float* out_f32;
     __nv_bfloat16* out_bf16;
-    const int* page_table;
     int n_tok;
     int pos0;
     int hq_total;            // query heads per row

@@ -53,7 +53,7 @@ __global__ void __launch_bounds__(ROWS_PER_BLOCK * 32)
         norm_rope_row(srow[warp], P.k_norm_w, P.eps, pos, P.inv_freq, lane, k4);
     }
     const int pt = P.page_tokens;
-    const int phys = P.page_table[(long long)P.slot * P.pages_per_seq + pos / pt];
+    const long long phys = (long long)P.slot * P.pages_per_seq + pos / pt;
     const long long row = (((long long)P.layer * P.nkv + kvh) * P.n_pages + phys) * pt + pos % pt;
     KV* kd = reinterpret_cast<KV*>(P.kcache) + row * HD + 4 * lane;
     KV* vd = reinterpret_cast<KV*>(P.vcache) + row * HD + 4 * lane;
@@ -78,7 +78,7 @@ __global__ void kv_read_kernel(const __grid_constant__ AppendParams P, float* __
     const int tok = (int)(r / P.nkv), kvh = (int)(r % P.nkv);
     const int pos = P.pos0 + tok;
     const int pt = P.page_tokens;
-    const int phys = P.page_table[(long long)P.slot * P.pages_per_seq + pos / pt];
+    const long long phys = (long long)P.slot * P.pages_per_seq + pos / pt;
     const long long row = (((long long)P.layer * P.nkv + kvh) * P.n_pages + phys) * pt + pos % pt;
     const size_t dst = (size_t)tok * P.nkv * HD + (size_t)kvh * HD + d;
     ko[dst] = to_f32<KV>(reinterpret_cast<const KV*>(P.kcache)[row * HD + d]);

@@ -295,3 +295,32 @@ def test_launch_count_advances(ctx_f32):
     w = np.ones(HD, np.float32)
     ctx_f32.attn_layer(xb, q, k, k, w, w, 0, 3)
     assert ctx_f32.launch_count() == n0 + 1  # the whole block is one kernel
+
+
+@pytest.mark.parametrize("bf16", [False, True])
+def test_batched_linear_schedule(bf16):
+    """More (sequence, kv head) groups than SMs: the linear unit schedule,
+    where CTAs cross group boundaries, must give the same results."""
+    rng = np.random.default_rng(5)
+    n = 20                                  # 160 groups > 148 SMs
+    lens = [int(x) for x in rng.integers(1, 300, size=n)]
+    lens[0], lens[1] = 1, 299
+    with q3attn.Context(n_layers=1, max_seq=320, n_seqs=n,
+                        kv_dtype=q3attn.KV_BF16 if bf16 else q3attn.KV_F32) as ctx:
+        qw = np.ones(HD, np.float32)
+        refs, qs, ks, vs = [], [], [], []
+        pos = [L - 1 for L in lens]
+        for i, L in enumerate(lens):
+            kc, vc, q, k, v, _, _ = oracle_inputs(900 + i, pos[i], L, bf16)
+            if pos[i] > 0:
+                ctx.kv_load(i, 0, 0, pos[i], kc[: pos[i] * KV_DIM], vc[: pos[i] * KV_DIM])
+            refs.append(oracle_block(kc, vc, q, k, v, qw, qw, pos[i], L, bf16)[0])
+            qs.append(q)
+            ks.append(k)
+            vs.append(v)
+        xb = np.zeros((n, HQ * HD), np.float32)
+        ctx.attn_layer_batched(xb, np.stack(qs), np.stack(ks), np.stack(vs), qw, qw, 0,
+                               list(range(n)), pos)
+        for i in range(n):
+            check_close(xb[i], refs[i], bf16, f"seq {i} len {lens[i]}")
+        ctx.check_device_error()
