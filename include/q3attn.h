@@ -117,6 +117,26 @@ int q3a_attn_decode(q3a_ctx *ctx, float *xb, const float *q, const float *kc,
                     const float *vc, float *att, size_t loff, int pos, int n_heads,
                     int kv_mul, int hd, int kv_dim, int max_seq);
 
+/* Decode attention with the arguments of q3a_attn_decode, for callers that
+ * cannot allocate device memory when they run it.  It has no counterpart in
+ * the reference (whose CPU and HIP builds allocate their run state once,
+ * qwen3-8b/gpu/main.c:1287-1323, and never need per-call scratch).  All
+ * pointers are device memory (q, caches kc/vc at layer offset loff, output
+ * xb); no context is needed and nothing is allocated: the split-KV scratch
+ * is a fixed array of 330,308 bytes in the library's device memory, reserved
+ * when the library's module loads on a device and held until the process
+ * exits.  Limit: at most 16 KV heads (kv_dim <= 2048); larger calls return
+ * Q3A_ERR_INVALID.  The first call on a device looks up the array's device
+ * address (cudaGetSymbolAddress) with that device current; make that first
+ * call before any stream capture.  All calls share the array, so calls that
+ * can overlap on the GPU (other streams, other host threads) race and must be
+ * serialised by the caller.  Work is queued on `cuda_stream` (a
+ * cudaStream_t, NULL for the legacy default stream) and the call returns
+ * without waiting for it. */
+int q3a_attn_decode_noalloc(float *xb, const float *q, const float *kc, const float *vc,
+                            size_t loff, int pos, int n_heads, int kv_mul, int hd, int kv_dim,
+                            int max_seq, void *cuda_stream);
+
 /* Batched ragged decode: n new tokens, token i belongs to cache slot
  * seq_ids[i] (distinct) at position pos[i] (host arrays).  The block of
  * q3a_attn_layer runs for each; q, xb are [n][n_heads*hd], k, v

@@ -163,6 +163,10 @@ extern "C" void q3a_cfg_default(q3a_cfg* cfg) {
 
 extern "C" const char* q3a_last_error(void) { return g_err; }
 
+// Records a failure message for q3a_last_error() from another translation
+// unit of the library and returns `code`.
+int q3a::record_error(int code, const char* msg) { return fail(code, "%s", msg); }
+
 static void destroy_ctx(q3a_ctx* c) {
     if (!c) return;
     if (c->stream) cudaStreamSynchronize(c->stream);

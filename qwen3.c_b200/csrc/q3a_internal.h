@@ -157,4 +157,7 @@ int prefill_smem_bytes();
 
 uint64_t stream_key(uint64_t seed, uint64_t stream);
 
+// Sets the message q3a_last_error() returns on this thread; returns code.
+int record_error(int code, const char* msg);
+
 }  // namespace q3a

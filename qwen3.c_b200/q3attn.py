@@ -24,7 +24,7 @@ EXPORTS = [
     "q3a_sync", "q3a_check_device_error", "q3a_attn_layer", "q3a_attn_decode",
     "q3a_attn_layer_batched", "q3a_kv_append", "q3a_kv_load", "q3a_kv_read", "q3a_prefill",
     "q3a_prefill_attn", "q3a_attn_partial", "q3a_lse_combine", "q3a_randn",
-    "q3a_launch_count",
+    "q3a_launch_count", "q3a_attn_decode_noalloc",
 ]
 
 
@@ -76,6 +76,7 @@ def load():
         L.q3a_attn_partial.argtypes = [_P, _P, _P, _P, _I, _I, _I, _I]
         L.q3a_lse_combine.argtypes = [_P, _P, _P, _P, _I]
         L.q3a_randn.argtypes = [_P, _P, _I, _SZ, _U64, _U64, _U64]
+        L.q3a_attn_decode_noalloc.argtypes = [_P, _P, _P, _P, _SZ, _I, _I, _I, _I, _I, _I, _P]
         L.q3a_launch_count.argtypes = [_P]
         L.q3a_launch_count.restype = _U64
         _lib = L
@@ -96,6 +97,14 @@ def ptr(x) -> int:
         return x.data_ptr()
     assert x.flags["C_CONTIGUOUS"]
     return x.ctypes.data
+
+
+def attn_decode_noalloc(xb, q, kc, vc, loff, pos, n_heads, kv_mul, hd, kv_dim, max_seq,
+                        stream_handle=None):
+    """q3a_attn_decode_noalloc: device pointers only, no context, nothing
+    allocated; queued on the given CUDA stream handle."""
+    check(load().q3a_attn_decode_noalloc(ptr(xb), ptr(q), ptr(kc), ptr(vc), loff, pos, n_heads,
+                                         kv_mul, hd, kv_dim, max_seq, stream_handle))
 
 
 def default_cfg(**kw) -> Cfg:
