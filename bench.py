@@ -490,7 +490,8 @@ def main():
         line["bf16"] = {"value": world * K * N_LAYERS * bb / (tb / 1000.0) / 1e9, "unit": "GB/s",
                         "us_per_layer": tb * 1000.0 / (K * N_LAYERS),
                         "kernel_us_mean": b["kernel_us"], "achieved": ach_b,
-                        "frac": ach_b / hbm_peak, "clocks": b["clocks"],
+                        "frac": ach_b / hbm_peak, "traffic": profile_traffic("decode_bf16_8k"),
+                        "clocks": b["clocks"],
                         "gpu_launches": b["launches"]}
         line["gpu_launches"] += b["launches"]
     if rank == 0 and world == 1 and not args.no_cpu:

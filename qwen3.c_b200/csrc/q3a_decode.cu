@@ -14,8 +14,8 @@
 //    SM.
 //  * Warp 8 is the producer: one lane streams K and V into a ring of
 //    64-row shared-memory stages, each tile of the paged cache as one bulk
-//    copy per tensor (cp.async.bulk; a tile lies in one page, so it is
-//    contiguous), with an L2 evict-first policy since each cache row is read
+//    copy per tensor (cp.async.bulk; two where a tile crosses a page
+//    boundary), with an L2 evict-first policy since each cache row is read
 //    once per step, completing on per-stage mbarriers.  The caller-owned
 //    position-major cache of q3a_attn_decode is strided and moves in 16-row
 //    2-D TMA boxes (cp.async.bulk.tensor) instead.
@@ -476,9 +476,11 @@ __global__ void __launch_bounds__(DecCfg<KV>::NTHREADS, 1)
             SegInfo s;
             while (!dead && next_seg(P, c, cur, s)) {
                 const int slot = P.slot[s.b];
+                // tiles start at the range's own 16-row-aligned start, so a
+                // range of R rows takes ceil(R/64) tiles wherever it begins
                 const int lo_all = s.r0 & ~(DEC_BOX - 1);
                 const int hi_all = (s.r1 + DEC_BOX - 1) & ~(DEC_BOX - 1);
-                for (int t0 = (s.r0 / C::TILE) * C::TILE; t0 < s.r1; t0 += C::TILE) {
+                for (int t0 = lo_all; t0 < s.r1; t0 += C::TILE) {
                     const int stage = it % C::STAGES;
                     const uint32_t ph = (uint32_t)(it / C::STAGES) & 1u;
                     if (it >= C::STAGES && !mbar_wait(&empty[stage], ph ^ 1u)) {
@@ -486,23 +488,34 @@ __global__ void __launch_bounds__(DecCfg<KV>::NTHREADS, 1)
                         dead = true;
                         break;
                     }
-                    // rows [lo, hi) of this 64-aligned tile, 16-row aligned;
-                    // they lie in one cache page, so in the paged layout they
-                    // are contiguous and move as one bulk copy per tensor
-                    const int lo = max(t0, lo_all), hi = min(t0 + C::TILE, hi_all);
-                    const uint32_t bytes = (uint32_t)((hi - lo) * HD * (int)sizeof(KV));
+                    const int hi = min(t0 + C::TILE, hi_all);
+                    const uint32_t bytes = (uint32_t)((hi - t0) * HD * (int)sizeof(KV));
                     mbar_arrive_expect_tx(&full[stage], 2u * bytes);
-                    const int doff = (stage * C::TILE + (lo - t0)) * HD;
+                    const int doff = stage * C::TILE * HD;
                     if (P.cache_mode == CACHE_PAGED) {
-                        const long long row = paged_row(P, slot, s.kvh, lo);
-                        bulk_load(sK + doff, reinterpret_cast<const KV*>(P.kcache) + row * HD, bytes,
+                        // rows [t0, hi) are contiguous within a page; a tile
+                        // that crosses a page boundary moves in two copies
+                        const int pb = (t0 / P.page_tokens + 1) * P.page_tokens;
+                        const int mid = min(hi, pb);
+                        const long long row0 = paged_row(P, slot, s.kvh, t0);
+                        const uint32_t b0 = (uint32_t)((mid - t0) * HD * (int)sizeof(KV));
+                        bulk_load(sK + doff, reinterpret_cast<const KV*>(P.kcache) + row0 * HD, b0,
                                   &full[stage], pol);
-                        bulk_load(sV + doff, reinterpret_cast<const KV*>(P.vcache) + row * HD, bytes,
+                        bulk_load(sV + doff, reinterpret_cast<const KV*>(P.vcache) + row0 * HD, b0,
                                   &full[stage], pol);
+                        if (mid < hi) {
+                            const long long row1 = paged_row(P, slot, s.kvh, mid);
+                            const int o1 = doff + (mid - t0) * HD;
+                            const uint32_t b1 = bytes - b0;
+                            bulk_load(sK + o1, reinterpret_cast<const KV*>(P.kcache) + row1 * HD, b1,
+                                      &full[stage], pol);
+                            bulk_load(sV + o1, reinterpret_cast<const KV*>(P.vcache) + row1 * HD, b1,
+                                      &full[stage], pol);
+                        }
                     } else {
                         const int xc = (P.kv0 + s.kvh) * HD;
-                        for (int t = lo; t < hi; t += DEC_BOX) {
-                            const int bo = doff + (t - lo) * HD;
+                        for (int t = t0; t < hi; t += DEC_BOX) {
+                            const int bo = doff + (t - t0) * HD;
                             tma_load_2d(sK + bo, &tmK, &full[stage], xc, t, pol);
                             tma_load_2d(sV + bo, &tmV, &full[stage], xc, t, pol);
                         }
@@ -589,7 +602,7 @@ __global__ void __launch_bounds__(DecCfg<KV>::NTHREADS, 1)
         for (int h = 0; h < GQA; h++) O[h][0] = O[h][1] = make_float2(0.0f, 0.0f);
 
         bool dead = false;
-        for (int t0 = (s.r0 / C::TILE) * C::TILE; t0 < s.r1; t0 += C::TILE) {
+        for (int t0 = s.r0 & ~(DEC_BOX - 1); t0 < s.r1; t0 += C::TILE) {
             const int stage = it % C::STAGES;
             const uint32_t ph = (uint32_t)(it / C::STAGES) & 1u;
             if (!mbar_wait(&full[stage], ph)) {
