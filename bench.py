@@ -249,6 +249,66 @@ def decode_run(args, torch, dev, local, kv_dtype, seed, world, with_e2e, with_cp
     return res
 
 
+def prefill_run(args, torch, dev, local, seed, world):
+    """causal prefill of S=2048 prompt rows per layer, 36 layers,
+    bf16 Q/K/V (post QK-norm + RoPE), fp32 softmax and accumulation, bf16
+    output.  One step = 36 launches of q3a_prefill_attn (the attention of
+    each layer over its cache), timed as one CUDA graph between two events."""
+    import q3attn
+    S = PREFILL_S
+    stream = torch.cuda.Stream(device=dev)
+    ctx = q3attn.Context(n_layers=N_LAYERS, max_seq=S, kv_dtype=q3attn.KV_BF16,
+                         ptr_mode=q3attn.PTR_DEVICE, device=local)
+    ctx.set_stream(stream.cuda_stream)
+    fill_cache(ctx, torch, dev, seed, N_LAYERS, S, stream)
+    qf = torch.empty(S * HQ * HD, device=dev)
+    qs = []
+    for l in range(N_LAYERS):
+        ctx.randn(qf, q3attn.OUT_F32, qf.numel(), seed, l * 16 + 3)
+        stream.synchronize()
+        # the kernel reads prepared (normed, rotated) bf16 rows; N(0,1) rows
+        # have the same statistics for timing
+        qs.append(qf.to(torch.bfloat16).view(S, HQ * HD).contiguous())
+    out = torch.empty(N_LAYERS, S, HQ * HD, dtype=torch.bfloat16, device=dev)
+    stream.synchronize()
+
+    def step():
+        for l in range(N_LAYERS):
+            ctx.prefill_attn(out[l], q3attn.OUT_BF16, qs[l], 0, l, 0, S)
+
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            step()
+    stream.synchronize()
+    ctx.check_device_error()
+    K = max(1, args.steps // 10)
+    e0 = torch.cuda.Event(enable_timing=True, external=True)
+    e1 = torch.cuda.Event(enable_timing=True, external=True)
+    g = torch.cuda.CUDAGraph()
+    n0 = ctx.launch_count()
+    with torch.cuda.graph(g, stream=stream):
+        e0.record(stream)
+        for _ in range(K):
+            step()
+        e1.record(stream)
+    launches = ctx.launch_count() - n0
+    with torch.cuda.stream(stream):
+        g.replay()
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    with ClockSampler(local) as cs:
+        with torch.cuda.stream(stream):
+            g.replay()
+        torch.cuda.synchronize(dev)
+    barrier(world)
+    ctx.check_device_error()
+    t_ms = e0.elapsed_time(e1)
+    del g
+    ctx.close()
+    return {"t_ms": t_ms, "launches": launches, "kernel_us": 1000.0 * t_ms / launches,
+            "clocks": cs.report(), "steps": K}
+
+
 def e2e_run(args, torch, dev, local, kv_dtype, seed, q_raw, k_raw, v_in, dctx, stream):
     """Same step through the host-pointer API: every layer copies its inputs
     in from host memory and its result out, synchronously."""
@@ -396,6 +456,22 @@ def ncu_case(args):
     import torch
     import q3attn
     dev = torch.device("cuda:0")
+    if args.ncu_case == "prefill":
+        S = PREFILL_S
+        stream = torch.cuda.Stream(device=dev)
+        ctx = q3attn.Context(n_layers=1, max_seq=S, kv_dtype=q3attn.KV_BF16,
+                             ptr_mode=q3attn.PTR_DEVICE)
+        ctx.set_stream(stream.cuda_stream)
+        fill_cache(ctx, torch, dev, 1234, 1, S, stream)
+        qb = torch.randn(S, HQ * HD, device=dev).to(torch.bfloat16)
+        out = torch.empty(S, HQ * HD, dtype=torch.bfloat16, device=dev)
+        for _ in range(args.warmup + args.steps):
+            ctx.prefill_attn(out, q3attn.OUT_BF16, qb, 0, 0, 0, S)
+        stream.synchronize()
+        ctx.check_device_error()
+        ctx.close()
+        print(f"ncu case prefill: {args.warmup + args.steps} launches ok")
+        return
     kv = q3attn.KV_F32 if args.ncu_case == "decode-f32" else q3attn.KV_BF16
     stream = torch.cuda.Stream(device=dev)
     ctx = q3attn.Context(n_layers=2, max_seq=L_CTX, kv_dtype=kv, ptr_mode=q3attn.PTR_DEVICE)
@@ -425,7 +501,7 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-variants", action="store_true")
-    ap.add_argument("--ncu-case", default=None, choices=["decode-f32", "decode-bf16"],
+    ap.add_argument("--ncu-case", default=None, choices=["decode-f32", "decode-bf16", "prefill"],
                     help="small single-kernel run for ncu captures (2 layers, direct launches)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
@@ -494,6 +570,27 @@ def main():
                         "clocks": b["clocks"],
                         "gpu_launches": b["launches"]}
         line["gpu_launches"] += b["launches"]
+    if not args.no_variants:
+        pr = prefill_run(args, torch, dev, local, seed, world)
+        t_p = max_over_ranks(pr["t_ms"], world, dev)
+        fl = prefill_flops()
+        us_l = t_p * 1000.0 / pr["launches"]
+        tf = world * fl * pr["launches"] / (t_p / 1000.0) / 1e12
+        line["prefill"] = {"metric": "prefill attn TFLOP/s (2K tok)", "value": tf,
+                           "unit": "TFLOP/s", "us_per_layer": us_l,
+                           "flops_per_layer": fl, "steps": pr["steps"],
+                           "roofline": {"bound": "tensor", "achieved": tf / world,
+                                        "peak": tf_sus, "unit": "TFLOP/s",
+                                        "frac": tf / world / tf_sus,
+                                        "frac_of_burst_peak": tf / world / tf_peak,
+                                        "peak_source": f"{peak_src} bf16_tflops_sustained "
+                                                       "(MEASURED_PEAKS.json)",
+                                        "kernel": "q3a::prefill_kernel",
+                                        "traffic": profile_traffic("prefill_2k")},
+                           "workload": "configs[2]: causal prefill S=2048, Hq=32, Hkv=8, "
+                                       "d=128, bf16 Q/K/V, bf16 out, 36 layers per step",
+                           "clocks": pr["clocks"], "gpu_launches": pr["launches"]}
+        line["gpu_launches"] += pr["launches"]
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = cpu_reference_sample(n_calls_max=400, budget_s=15.0)
         line["cpu_baseline"] = {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")}

@@ -277,10 +277,10 @@ extern "C" int q3a_create(q3a_ctx** out, const q3a_cfg* cfg_in) {
         rc = make_map_2d(&c->tmV, c->vcache, c->bf16, HD, (uint64_t)c->total_rows, HD, DEC_BOX,
                          CU_TENSOR_MAP_SWIZZLE_NONE);
     if (rc == Q3A_OK && c->bf16) {
-        rc = make_map_2d(&c->tmKp, c->kcache, true, HD, (uint64_t)c->total_rows, 64, 128,
+        rc = make_map_2d(&c->tmKp, c->kcache, true, HD, (uint64_t)c->total_rows, 64, 64,
                          CU_TENSOR_MAP_SWIZZLE_128B);
         if (rc == Q3A_OK)
-            rc = make_map_2d(&c->tmVp, c->vcache, true, HD, (uint64_t)c->total_rows, 64, 128,
+            rc = make_map_2d(&c->tmVp, c->vcache, true, HD, (uint64_t)c->total_rows, 64, 64,
                              CU_TENSOR_MAP_SWIZZLE_128B);
     }
     if (rc != Q3A_OK) {
@@ -926,5 +926,54 @@ extern "C" int q3a_prefill_attn(q3a_ctx* c, void* out, int out_dtype, const void
     if (layer < 0 || layer >= c->cfg.n_layers) return fail(Q3A_ERR_INVALID, "layer %d", layer);
     if (n_tok <= 0 || pos0 < 0 || (long long)pos0 + n_tok > c->cfg.max_seq)
         return fail(Q3A_ERR_INVALID, "rows [%d, +%d) outside [0, %d)", pos0, n_tok, c->cfg.max_seq);
-    return fail(Q3A_ERR_UNSUPPORTED, "the tensor-core prefill kernel is not built yet");
+    int rc = ensure_device(c);
+    if (rc) return rc;
+    const size_t qd = (size_t)n_tok * c->cfg.n_heads * HD;
+    const size_t out_bytes = qd * (out_dtype == Q3A_OUT_BF16 ? 2 : 4);
+    const void* dq = q_bf16;
+    void* dout = out;
+    if (c->cfg.ptr_mode == Q3A_PTR_HOST) {
+        rc = grow_scratch(c, qd * 2 + 256 + out_bytes);
+        if (rc) return rc;
+        uint8_t* s = reinterpret_cast<uint8_t*>(c->d_scratch);
+        CUDA_TRY(cudaMemcpyAsync(s, q_bf16, qd * 2, cudaMemcpyHostToDevice, c->stream));
+        dq = s;
+        dout = s + ((qd * 2 + 255) & ~(size_t)255);
+    }
+    // Q [n_tok][n_heads][128] bf16: 3-D map (d, head, row), box 64 x 1 x 128,
+    // 128-byte swizzle -- one head's 128 rows x 64 dims per load
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return fail(Q3A_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
+    CUtensorMap tq;
+    cuuint64_t dims[3] = {(cuuint64_t)HD, (cuuint64_t)c->cfg.n_heads, (cuuint64_t)n_tok};
+    cuuint64_t strides[2] = {(cuuint64_t)HD * 2, (cuuint64_t)c->cfg.n_heads * HD * 2};
+    cuuint32_t box[3] = {64, 1, 128};
+    cuuint32_t estr[3] = {1, 1, 1};
+    if (fn(&tq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(dq), dims, strides, box, estr,
+           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return fail(Q3A_ERR_CUDA, "prefill q tensor map");
+    PrefillParams pp;
+    memset(&pp, 0, sizeof(pp));
+    pp.out_f32 = out_dtype == Q3A_OUT_F32 ? reinterpret_cast<float*>(dout) : nullptr;
+    pp.out_bf16 = out_dtype == Q3A_OUT_BF16 ? reinterpret_cast<__nv_bfloat16*>(dout) : nullptr;
+    pp.n_tok = n_tok;
+    pp.pos0 = pos0;
+    pp.hq_total = c->cfg.n_heads;
+    pp.nkv = c->nkv;
+    pp.kv0 = c->kv0;
+    pp.layer = layer;
+    pp.slot = seq;
+    pp.pages_per_seq = c->pages_per_seq;
+    pp.page_tokens = c->cfg.page_tokens;
+    pp.n_pages = c->n_pages;
+    pp.scale_log2e = (float)(1.4426950408889634 / sqrt((double)HD));
+    pp.err = c->err;
+    CUDA_TRY(launch_prefill(pp, tq, c->tmKp, c->tmVp, c->stream));
+    c->launches++;
+    if (c->cfg.ptr_mode == Q3A_PTR_HOST) {
+        CUDA_TRY(cudaMemcpyAsync(out, dout, out_bytes, cudaMemcpyDeviceToHost, c->stream));
+        CUDA_TRY(cudaStreamSynchronize(c->stream));
+    }
+    return Q3A_OK;
 }

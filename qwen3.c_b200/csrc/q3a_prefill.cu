@@ -1,0 +1,581 @@
+// q3a_prefill.cu -- causal prefill attention on the sm_100a tensor cores.
+//
+// The reference processes a prompt one token at a time through the decode
+// path (qwen3-8b/cpu/main.c:1481-1499), so prompt row s attends to cache
+// positions 0..pos0+s.  Here all rows of a prompt run as one causal flash
+// attention with tcgen05.mma (kind::f16: bf16 operands, fp32 accumulators in
+// tensor memory):
+//
+//  * Work item = (KV head g, pair of query heads 4g+2p, 4g+2p+1, 128 query
+//    rows).  The two query heads of an item share every K/V tile (GQA), and
+//    their MMAs alternate so that one head's softmax overlaps the other's
+//    tensor-core work.  Items are dealt to a persistent grid in a snake
+//    order of decreasing length (longest causal rows first).
+//  * Warp 0 streams Q (3-D TMA, 128B swizzle) and 64-key K/V tiles of the
+//    paged bf16 cache (2-D TMA, 128B swizzle) through a 2-stage ring.
+//    Warp 1 issues all MMAs from one lane: S = Q.K^T (M128 N64 K128) into a
+//    double-buffered tensor-memory tile per head, O += P.V (M128 N128 K64)
+//    into a tensor-memory accumulator per head; tcgen05.commit signals the
+//    mbarriers.  Warps 4-7 and 8-11 are the softmax warpgroups of the two
+//    heads: thread r owns query row r, reads its 64 scores with one
+//    tcgen05.ld, applies the causal mask and an online softmax in log2 units
+//    (the reference scale 1/sqrt(128) folded with log2 e), writes P as bf16
+//    into shared memory in the 128B-swizzled K-major layout the MMA reads,
+//    (two P buffers per head, so the softmax of tile j+1 does not wait for
+//    the MMA of tile j), and rescales O in tensor memory only when its running maximum grows by
+//    more than 2^8 (otherwise the stale maximum stays the reference; the
+//    final division uses the same reference, so the result is exact).
+//  * The epilogue divides O by the row sum and stores the row (fp32 or bf16).
+// Tensor memory: 512 columns per CTA (S 2x2x64, O 2x128), one CTA per SM.
+#include "q3a_common.cuh"
+#include "q3a_internal.h"
+
+namespace q3a {
+
+namespace pf {
+
+constexpr int QT = 128;        // query rows per head tile
+constexpr int KT = 64;         // keys per K/V tile
+constexpr int STAGES = 2;
+constexpr int NTHREADS = 384;  // 12 warps
+constexpr int Q_TILE_BYTES = QT * HD * 2;          // 32 KB (2 K-blocks of 128 rows x 128 B)
+constexpr int KV_TILE_BYTES = KT * HD * 2;         // 16 KB (2 blocks of 64 rows x 128 B)
+constexpr int P_TILE_BYTES = QT * KT * 2;          // 16 KB (128 rows x 128 B)
+constexpr int OFF_Q = 0;                           // [2 heads][32 KB]
+constexpr int OFF_K = OFF_Q + 2 * Q_TILE_BYTES;    // [STAGES][16 KB]
+constexpr int OFF_V = OFF_K + STAGES * KV_TILE_BYTES;
+constexpr int OFF_P = OFF_V + STAGES * KV_TILE_BYTES;  // [2 heads][2 bufs][16 KB]
+constexpr int OFF_BAR = OFF_P + 4 * P_TILE_BYTES;
+// barriers (8 bytes each)
+constexpr int B_QFULL = 0, B_QEMPTY = 1;
+constexpr int B_KFULL = 2, B_KEMPTY = B_KFULL + STAGES;
+constexpr int B_VFULL = B_KEMPTY + STAGES, B_VEMPTY = B_VFULL + STAGES;
+constexpr int B_SFULL = B_VEMPTY + STAGES;  // [head][buf]
+constexpr int B_SFREE = B_SFULL + 4;
+constexpr int B_PFULL = B_SFREE + 4;        // [head][buf]
+constexpr int B_PFREE = B_PFULL + 4;        // [head][buf]
+constexpr int B_OFREE = B_PFREE + 4;        // [head]
+constexpr int NBAR = B_OFREE + 2;
+constexpr int OFF_MISC = OFF_BAR + NBAR * 8;  // tmem address, abort flag
+constexpr int SMEM = OFF_MISC + 64 + 1024;    // + slack for 1024-byte alignment
+static_assert(SMEM <= 232448, "prefill shared memory exceeds the sm_100 limit");
+
+constexpr uint32_t TMEM_COLS = 512;
+constexpr uint32_t COL_S = 0;      // S[head][buf] at head*128 + buf*64
+constexpr uint32_t COL_O = 256;    // O[head] at 256 + head*128
+
+// instruction descriptors (kind::f16): c=F32 (bit 4), a=BF16 (bits 7-9),
+// b=BF16 (bits 10-12), b_major bit 16, N>>3 at bit 17, M>>4 at bit 24
+constexpr uint32_t IDESC_S = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(KT >> 3) << 17) |
+                             ((uint32_t)(QT >> 4) << 24);
+constexpr uint32_t IDESC_PV = (1u << 4) | (1u << 7) | (1u << 10) | (1u << 16) |
+                              ((uint32_t)(HD >> 3) << 17) | ((uint32_t)(QT >> 4) << 24);
+
+}  // namespace pf
+
+// Shared-memory matrix descriptor, 128B swizzle, descriptor version 1.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+    return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
+           ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) | (2ull << 61);
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                       uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n\t}" ::"r"(
+            d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(0u)
+        : "memory");
+}
+
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                     smem_u32(bar))
+                 : "memory");
+}
+
+#define Q3A_TC_LD32(taddr, r, base)                                                               \
+    asm volatile(                                                                                 \
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14," \
+        "%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"           \
+        : "=r"(r[base + 0]), "=r"(r[base + 1]), "=r"(r[base + 2]), "=r"(r[base + 3]),            \
+          "=r"(r[base + 4]), "=r"(r[base + 5]), "=r"(r[base + 6]), "=r"(r[base + 7]),            \
+          "=r"(r[base + 8]), "=r"(r[base + 9]), "=r"(r[base + 10]), "=r"(r[base + 11]),          \
+          "=r"(r[base + 12]), "=r"(r[base + 13]), "=r"(r[base + 14]), "=r"(r[base + 15]),        \
+          "=r"(r[base + 16]), "=r"(r[base + 17]), "=r"(r[base + 18]), "=r"(r[base + 19]),        \
+          "=r"(r[base + 20]), "=r"(r[base + 21]), "=r"(r[base + 22]), "=r"(r[base + 23]),        \
+          "=r"(r[base + 24]), "=r"(r[base + 25]), "=r"(r[base + 26]), "=r"(r[base + 27]),        \
+          "=r"(r[base + 28]), "=r"(r[base + 29]), "=r"(r[base + 30]), "=r"(r[base + 31])         \
+        : "r"(taddr))
+
+#define Q3A_TC_ST32(taddr, r, base)                                                               \
+    asm volatile(                                                                                 \
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13," \
+        "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(    \
+            taddr),                                                                               \
+        "r"(r[base + 0]), "r"(r[base + 1]), "r"(r[base + 2]), "r"(r[base + 3]), "r"(r[base + 4]), \
+        "r"(r[base + 5]), "r"(r[base + 6]), "r"(r[base + 7]), "r"(r[base + 8]), "r"(r[base + 9]), \
+        "r"(r[base + 10]), "r"(r[base + 11]), "r"(r[base + 12]), "r"(r[base + 13]),               \
+        "r"(r[base + 14]), "r"(r[base + 15]), "r"(r[base + 16]), "r"(r[base + 17]),               \
+        "r"(r[base + 18]), "r"(r[base + 19]), "r"(r[base + 20]), "r"(r[base + 21]),               \
+        "r"(r[base + 22]), "r"(r[base + 23]), "r"(r[base + 24]), "r"(r[base + 25]),               \
+        "r"(r[base + 26]), "r"(r[base + 27]), "r"(r[base + 28]), "r"(r[base + 29]),               \
+        "r"(r[base + 30]), "r"(r[base + 31])                                                     \
+        : "memory")
+
+__device__ __forceinline__ void tc_wait_ld() {
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tc_wait_st() {
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// 2^x by the hardware approximation (MUFU ex2, flush-to-zero): softmax
+// weights p = 2^(s - m) <= 2^8 need no denormal handling.
+__device__ __forceinline__ float exp2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// Bounded wait that also gives up as soon as another thread of the CTA has
+// given up (the shared abort word), so a stalled pipeline unwinds in about
+// one wait limit instead of one per remaining wait.
+__device__ __forceinline__ bool pf_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                        int* err) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const long long t0 = clock64();
+    while (!mbar_try_wait(bar, parity)) {
+        if (*abort_flag || clock64() - t0 > WAIT_LIMIT_CYCLES) {
+            if (!*abort_flag) atomicExch(err, DEV_ERR_TIMEOUT);
+            *abort_flag = 1;
+            return false;
+        }
+    }
+    return true;
+}
+
+// Work item i of n (i in decreasing-length order) -> (qt, g, hp).
+struct PfItem {
+    int qt, g, hp, nj;
+};
+
+__device__ __forceinline__ PfItem pf_item(const PrefillParams& P, int i) {
+    const int per_qt = P.nkv * 2;
+    const int n_qt = (P.n_tok + pf::QT - 1) / pf::QT;
+    PfItem it;
+    it.qt = n_qt - 1 - i / per_qt;
+    const int rem = i % per_qt;
+    it.g = rem / 2;
+    it.hp = rem % 2;
+    const int last_q = min(P.pos0 + (it.qt + 1) * pf::QT, P.pos0 + P.n_tok) - 1;  // absolute
+    it.nj = last_q / pf::KT + 1;
+    return it;
+}
+
+// The i-th item of CTA c in snake order over `nitems` items.
+__device__ __forceinline__ int pf_item_index(int c, int r, int G) {
+    return r * G + ((r & 1) ? (G - 1 - c) : c);
+}
+
+__global__ void __launch_bounds__(pf::NTHREADS, 1)
+    prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                   const __grid_constant__ CUtensorMap tmV, const __grid_constant__ PrefillParams P) {
+    using namespace pf;
+    extern __shared__ uint8_t smem_raw[];
+    // 1024-byte alignment for the 128B-swizzle atoms
+    uint8_t* smem = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
+    volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(smem + OFF_MISC);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + OFF_MISC + 8);
+    const uint32_t s_base = smem_u32(smem);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int c = blockIdx.x, G = gridDim.x;
+    const int n_qt = (P.n_tok + QT - 1) / QT;
+    const int n_items = n_qt * P.nkv * 2;
+
+    if (tid == 0) {
+        mbar_init(&bars[B_QFULL], 1);
+        mbar_init(&bars[B_QEMPTY], 1);
+        for (int s = 0; s < STAGES; s++) {
+            mbar_init(&bars[B_KFULL + s], 1);
+            mbar_init(&bars[B_KEMPTY + s], 1);
+            mbar_init(&bars[B_VFULL + s], 1);
+            mbar_init(&bars[B_VEMPTY + s], 1);
+        }
+        for (int i = 0; i < 4; i++) {
+            mbar_init(&bars[B_SFULL + i], 1);
+            mbar_init(&bars[B_SFREE + i], 4);
+        }
+        for (int i = 0; i < 4; i++) {
+            mbar_init(&bars[B_PFULL + i], 4);
+            mbar_init(&bars[B_PFREE + i], 1);
+        }
+        for (int t = 0; t < 2; t++) mbar_init(&bars[B_OFREE + t], 4);
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         smem_u32((const void*)tmem_slot)),
+                     "r"(TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    if (warp == 0 && lane == 0) {
+        tma_prefetch_desc(&tmQ);
+        tma_prefetch_desc(&tmK);
+        tma_prefetch_desc(&tmV);
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        // ============================================ TMA producer
+        if (lane == 0) {
+            const uint64_t pol_q = l2_policy_evict_first();
+            const uint64_t pol_kv = l2_policy_evict_last();  // K/V of a head are re-read by 16 items
+            int kv_it = 0, item_it = 0;
+            for (int r = 0;; r++) {
+                const int i = pf_item_index(c, r, G);
+                if (i >= n_items) break;
+                const PfItem it = pf_item(P, i);
+                if (item_it > 0 && !pf_wait(&bars[B_QEMPTY], (item_it - 1) & 1, abort_flag, P.err))
+                    break;
+                mbar_arrive_expect_tx(&bars[B_QFULL], 2u * Q_TILE_BYTES);
+                for (int t = 0; t < 2; t++) {
+                    const int h = (P.kv0 + it.g) * GQA + 2 * it.hp + t;
+                    uint8_t* dq = smem + OFF_Q + t * Q_TILE_BYTES;
+                    tma_load_3d(dq, &tmQ, &bars[B_QFULL], 0, h, it.qt * QT, pol_q);
+                    tma_load_3d(dq + QT * 128, &tmQ, &bars[B_QFULL], 64, h, it.qt * QT, pol_q);
+                }
+                bool dead = false;
+                for (int j = 0; j < it.nj; j++, kv_it++) {
+                    const int st = kv_it % STAGES;
+                    const uint32_t ph = (uint32_t)(kv_it / STAGES) & 1u;
+                    const int pt = P.page_tokens;
+                    const int t0 = j * KT;
+                    const long long phys = (long long)P.slot * P.pages_per_seq + t0 / pt;
+                    const int row = (int)((((long long)P.layer * P.nkv + it.g) * P.n_pages + phys) * pt +
+                                          (t0 % pt));
+                    if (kv_it >= STAGES && !pf_wait(&bars[B_KEMPTY + st], ph ^ 1u, abort_flag, P.err)) {
+                        dead = true;
+                        break;
+                    }
+                    uint8_t* dk = smem + OFF_K + st * KV_TILE_BYTES;
+                    mbar_arrive_expect_tx(&bars[B_KFULL + st], (uint32_t)KV_TILE_BYTES);
+                    tma_load_2d(dk, &tmK, &bars[B_KFULL + st], 0, row, pol_kv);
+                    tma_load_2d(dk + KT * 128, &tmK, &bars[B_KFULL + st], 64, row, pol_kv);
+                    if (kv_it >= STAGES && !pf_wait(&bars[B_VEMPTY + st], ph ^ 1u, abort_flag, P.err)) {
+                        dead = true;
+                        break;
+                    }
+                    uint8_t* dv = smem + OFF_V + st * KV_TILE_BYTES;
+                    mbar_arrive_expect_tx(&bars[B_VFULL + st], (uint32_t)KV_TILE_BYTES);
+                    tma_load_2d(dv, &tmV, &bars[B_VFULL + st], 0, row, pol_kv);
+                    tma_load_2d(dv + KT * 128, &tmV, &bars[B_VFULL + st], 64, row, pol_kv);
+                }
+                if (dead) break;
+                item_it++;
+            }
+        }
+    } else if (warp == 1) {
+        // ============================================ MMA issuer
+        if (lane == 0) {
+            int kv_it = 0, item_it = 0, s_it = 0, pv_it = 0;
+            bool dead = false;
+            for (int r = 0; !dead; r++) {
+                const int i = pf_item_index(c, r, G);
+                if (i >= n_items) break;
+                const PfItem it = pf_item(P, i);
+                if (!pf_wait(&bars[B_QFULL], item_it & 1, abort_flag, P.err)) break;
+                if (item_it > 0) {
+                    // the previous item's epilogue has read O
+                    if (!pf_wait(&bars[B_OFREE + 0], (item_it - 1) & 1, abort_flag, P.err) ||
+                        !pf_wait(&bars[B_OFREE + 1], (item_it - 1) & 1, abort_flag, P.err))
+                        break;
+                }
+                tc_fence_after();
+                // S(j) for both heads into buffer s_it&1, then release K(j)
+                auto issue_s = [&](int j) -> bool {
+                    const int st = (kv_it + j) % STAGES;
+                    const uint32_t ph = (uint32_t)((kv_it + j) / STAGES) & 1u;
+                    if (!pf_wait(&bars[B_KFULL + st], ph, abort_flag, P.err)) return false;
+                    const int buf = s_it & 1;
+                    if (s_it >= 2 &&
+                        (!pf_wait(&bars[B_SFREE + 0 * 2 + buf], ((s_it >> 1) - 1) & 1, abort_flag, P.err) ||
+                         !pf_wait(&bars[B_SFREE + 1 * 2 + buf], ((s_it >> 1) - 1) & 1, abort_flag, P.err)))
+                        return false;
+                    tc_fence_after();
+                    const uint32_t kb = s_base + OFF_K + st * KV_TILE_BYTES;
+                    for (int t = 0; t < 2; t++) {
+                        const uint32_t qb = s_base + OFF_Q + t * Q_TILE_BYTES;
+                        const uint32_t d = tmem + COL_S + t * 128 + buf * 64;
+#pragma unroll
+                        for (int kk = 0; kk < HD / 16; kk++) {
+                            const uint32_t koff = (kk & 3) * 32;  // 16 bf16 along K in the 128 B row
+                            const uint64_t da = smem_desc(qb + (kk >> 2) * (QT * 128) + koff, 16, 1024);
+                            const uint64_t db = smem_desc(kb + (kk >> 2) * (KT * 128) + koff, 16, 1024);
+                            tc_mma(d, da, db, IDESC_S, kk > 0 ? 1u : 0u);
+                        }
+                        tc_commit(&bars[B_SFULL + t * 2 + buf]);
+                    }
+                    tc_commit(&bars[B_KEMPTY + st]);
+                    s_it++;
+                    return true;
+                };
+                if (!issue_s(0)) break;
+                for (int j = 0; j < it.nj; j++) {
+                    if (j + 1 < it.nj && !issue_s(j + 1)) {
+                        dead = true;
+                        break;
+                    }
+                    const int st = (kv_it + j) % STAGES;
+                    const uint32_t ph = (uint32_t)((kv_it + j) / STAGES) & 1u;
+                    if (!pf_wait(&bars[B_VFULL + st], ph, abort_flag, P.err)) {
+                        dead = true;
+                        break;
+                    }
+                    const uint32_t vb = s_base + OFF_V + st * KV_TILE_BYTES;
+                    const int pbuf = pv_it & 1;
+                    for (int t = 0; t < 2; t++) {
+                        if (!pf_wait(&bars[B_PFULL + t * 2 + pbuf], (pv_it >> 1) & 1, abort_flag,
+                                     P.err)) {
+                            dead = true;
+                            break;
+                        }
+                        tc_fence_after();
+                        const uint32_t pb = s_base + OFF_P + (t * 2 + pbuf) * P_TILE_BYTES;
+                        const uint32_t d = tmem + COL_O + t * 128;
+#pragma unroll
+                        for (int kk = 0; kk < KT / 16; kk++) {
+                            const uint64_t da = smem_desc(pb + kk * 32, 16, 1024);
+                            const uint64_t db = smem_desc(vb + kk * 16 * 128, KT * 128, 1024);
+                            tc_mma(d, da, db, IDESC_PV, (j > 0 || kk > 0) ? 1u : 0u);
+                        }
+                        // completes when this PV (and every earlier MMA) is done
+                        tc_commit(&bars[B_PFREE + t * 2 + pbuf]);
+                    }
+                    if (dead) break;
+                    tc_commit(&bars[B_VEMPTY + st]);
+                    pv_it++;
+                }
+                if (dead) break;
+                tc_commit(&bars[B_QEMPTY]);
+                kv_it += it.nj;
+                item_it++;
+            }
+        }
+    } else if (warp >= 4) {
+        // ============================================ softmax warpgroups
+        const int t = (warp - 4) >> 2;            // head of the pair
+        const int rw = warp & 3;                  // TMEM lane quarter
+        const int row = rw * 32 + lane;           // query row within the tile
+        const uint32_t lane_base = (uint32_t)(rw * 32) << 16;
+        const float2 sc2 = make_float2(P.scale_log2e, P.scale_log2e);
+        int s_it = 0, pv_it = 0, item_it = 0;
+        for (int r = 0;; r++) {
+            const int i = pf_item_index(c, r, G);
+            if (i >= n_items) break;
+            const PfItem it = pf_item(P, i);
+            const int q_abs = P.pos0 + it.qt * QT + row;  // this row's position
+            float m_ref = -INFINITY, l_sum = 0.0f;
+            bool dead = false;
+            for (int j = 0; j < it.nj; j++) {
+                const int buf = s_it & 1;
+                if (!pf_wait(&bars[B_SFULL + t * 2 + buf], (s_it >> 1) & 1, abort_flag, P.err)) {
+                    dead = true;
+                    break;
+                }
+                tc_fence_after();
+                uint32_t sr[64];
+                const uint32_t sa = tmem + lane_base + COL_S + t * 128 + buf * 64;
+                Q3A_TC_LD32(sa, sr, 0);
+                Q3A_TC_LD32(sa + 32, sr, 32);
+                tc_wait_ld();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&bars[B_SFREE + t * 2 + buf]);
+                s_it++;
+                // causal mask: only rows the diagonal crosses in this tile
+                const int k0 = j * KT;
+                if (k0 + KT - 1 > q_abs) {
+#pragma unroll
+                    for (int cc = 0; cc < 64; cc++)
+                        if (k0 + cc > q_abs) sr[cc] = __float_as_uint(-INFINITY);
+                }
+                // running maximum on raw scores (the scale is positive), tree
+                float mx8[8];
+#pragma unroll
+                for (int u = 0; u < 8; u++) mx8[u] = __uint_as_float(sr[u]);
+#pragma unroll
+                for (int cc = 8; cc < 64; cc++) mx8[cc & 7] = fmaxf(mx8[cc & 7], __uint_as_float(sr[cc]));
+                const float mt = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                                       fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]))) *
+                                 P.scale_log2e;
+                float alpha = 1.0f;
+                bool rescale = false;
+                if (mt > m_ref + 8.0f) {  // includes the first tile (m_ref = -inf)
+                    alpha = (m_ref == -INFINITY) ? 0.0f : exp2_approx(m_ref - mt);
+                    rescale = (m_ref != -INFINITY);
+                    m_ref = mt;
+                }
+                // p = 2^(s*scale - m_ref), packed fp32x2 math, 4 partial sums
+                const float2 nm2 = make_float2(-m_ref, -m_ref);
+                float2 ps2[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f),
+                                 make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+                uint32_t pk[32];
+#pragma unroll
+                for (int cc = 0; cc < 64; cc += 2) {
+                    const float2 x = __ffma2_rn(
+                        make_float2(__uint_as_float(sr[cc]), __uint_as_float(sr[cc + 1])), sc2, nm2);
+                    const float2 pp = make_float2(exp2_approx(x.x), exp2_approx(x.y));
+                    ps2[(cc >> 1) & 3] = __fadd2_rn(ps2[(cc >> 1) & 3], pp);
+                    __nv_bfloat162 b2 = __floats2bfloat162_rn(pp.x, pp.y);
+                    pk[cc >> 1] = *reinterpret_cast<uint32_t*>(&b2);
+                }
+                const float2 s01 = __fadd2_rn(ps2[0], ps2[1]), s23 = __fadd2_rn(ps2[2], ps2[3]);
+                const float2 s4 = __fadd2_rn(s01, s23);
+                l_sum = l_sum * alpha + (s4.x + s4.y);
+                // P(j) goes to buffer pv_it&1 once the PV that last read it is done
+                const int pbuf = pv_it & 1;
+                if (pv_it >= 2 &&
+                    !pf_wait(&bars[B_PFREE + t * 2 + pbuf], ((pv_it >> 1) - 1) & 1, abort_flag,
+                             P.err)) {
+                    dead = true;
+                    break;
+                }
+                if (rescale && j > 0) {
+                    // O must be complete up to PV(j-1) before it is rescaled:
+                    // wait for that PV's commit on its P buffer (a barrier is
+                    // only ever awaited one phase ahead of what it completed)
+                    if (!pf_wait(&bars[B_PFREE + t * 2 + ((pv_it - 1) & 1)], ((pv_it - 1) >> 1) & 1,
+                                 abort_flag, P.err)) {
+                        dead = true;
+                        break;
+                    }
+                    tc_fence_after();
+                    uint32_t orr[64];
+                    for (int half = 0; half < 2; half++) {
+                        const uint32_t oa = tmem + lane_base + COL_O + t * 128 + half * 64;
+                        Q3A_TC_LD32(oa, orr, 0);
+                        Q3A_TC_LD32(oa + 32, orr, 32);
+                        tc_wait_ld();
+#pragma unroll
+                        for (int cc = 0; cc < 64; cc++)
+                            orr[cc] = __float_as_uint(__uint_as_float(orr[cc]) * alpha);
+                        Q3A_TC_ST32(oa, orr, 0);
+                        Q3A_TC_ST32(oa + 32, orr, 32);
+                    }
+                    tc_wait_st();
+                }
+                tc_fence_after();
+                // P row -> shared memory, 128B-swizzled K-major layout
+                uint8_t* prow = smem + OFF_P + (t * 2 + pbuf) * P_TILE_BYTES + row * 128;
+#pragma unroll
+                for (int ch = 0; ch < 8; ch++) {
+                    const int pch = ch ^ (row & 7);
+                    *reinterpret_cast<uint4*>(prow + pch * 16) =
+                        make_uint4(pk[4 * ch], pk[4 * ch + 1], pk[4 * ch + 2], pk[4 * ch + 3]);
+                }
+                fence_proxy_async_smem();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&bars[B_PFULL + t * 2 + pbuf]);
+                pv_it++;
+            }
+            if (dead) break;
+            // epilogue: O / l once the item's last PV (hence every PV) is done
+            if (!pf_wait(&bars[B_PFREE + t * 2 + ((pv_it - 1) & 1)], ((pv_it - 1) >> 1) & 1,
+                         abort_flag, P.err))
+                break;
+            tc_fence_after();
+            const int srow = it.qt * QT + row;  // prompt row
+            const int h = (P.kv0 + it.g) * GQA + 2 * it.hp + t;
+            const float inv = 1.0f / l_sum;
+            for (int half = 0; half < 2; half++) {
+                uint32_t orr[64];
+                const uint32_t oa = tmem + lane_base + COL_O + t * 128 + half * 64;
+                Q3A_TC_LD32(oa, orr, 0);
+                Q3A_TC_LD32(oa + 32, orr, 32);
+                tc_wait_ld();
+                if (srow < P.n_tok) {
+                    const size_t o = ((size_t)srow * P.hq_total + h) * HD + half * 64;
+                    if (P.out_f32) {
+                        float4* dst = reinterpret_cast<float4*>(P.out_f32 + o);
+#pragma unroll
+                        for (int q4 = 0; q4 < 16; q4++)
+                            dst[q4] = make_float4(__uint_as_float(orr[4 * q4]) * inv,
+                                                  __uint_as_float(orr[4 * q4 + 1]) * inv,
+                                                  __uint_as_float(orr[4 * q4 + 2]) * inv,
+                                                  __uint_as_float(orr[4 * q4 + 3]) * inv);
+                    } else {
+                        uint4* dst = reinterpret_cast<uint4*>(P.out_bf16 + o);
+#pragma unroll
+                        for (int q8 = 0; q8 < 8; q8++) {
+                            uint32_t w[4];
+#pragma unroll
+                            for (int e = 0; e < 4; e++) {
+                                __nv_bfloat162 b2 = __floats2bfloat162_rn(
+                                    __uint_as_float(orr[8 * q8 + 2 * e]) * inv,
+                                    __uint_as_float(orr[8 * q8 + 2 * e + 1]) * inv);
+                                w[e] = *reinterpret_cast<uint32_t*>(&b2);
+                            }
+                            dst[q8] = make_uint4(w[0], w[1], w[2], w[3]);
+                        }
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bars[B_OFREE + t]);
+            item_it++;
+        }
+    }
+    // teardown: every warp meets here; the allocating warp frees tensor memory
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) {
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                     "r"(TMEM_COLS)
+                     : "memory");
+    }
+}
+
+cudaError_t launch_prefill(const PrefillParams& p, const CUtensorMap& tmQ, const CUtensorMap& tmK,
+                           const CUtensorMap& tmV, cudaStream_t st) {
+    static bool attr_set = false;
+    if (!attr_set) {
+        cudaError_t e = cudaFuncSetAttribute(prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             pf::SMEM);
+        if (e != cudaSuccess) return e;
+        attr_set = true;
+    }
+    const int n_qt = (p.n_tok + pf::QT - 1) / pf::QT;
+    const int n_items = n_qt * p.nkv * 2;
+    int nsm = 0;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+    const int grid = n_items < nsm ? n_items : nsm;
+    prefill_kernel<<<grid, pf::NTHREADS, pf::SMEM, st>>>(tmQ, tmK, tmV, p);
+    return cudaGetLastError();
+}
+
+int prefill_smem_bytes() { return pf::SMEM; }
+
+}  // namespace q3a
