@@ -7,26 +7,32 @@
 // tensor memory):
 //
 //  * Work item = (KV head g, pair of query heads 4g+2p, 4g+2p+1, 128 query
-//    rows).  The two query heads of an item share every K/V tile (GQA), and
-//    their MMAs alternate so that one head's softmax overlaps the other's
-//    tensor-core work.  Items are dealt to a persistent grid in a snake
-//    order of decreasing length (longest causal rows first).
-//  * Warp 0 streams Q (3-D TMA, 128B swizzle) and 64-key K/V tiles of the
-//    paged bf16 cache (2-D TMA, 128B swizzle) through a 2-stage ring.
-//    Warp 1 issues all MMAs from one lane: S = Q.K^T (M128 N64 K128) into a
-//    double-buffered tensor-memory tile per head, O += P.V (M128 N128 K64)
-//    into a tensor-memory accumulator per head; tcgen05.commit signals the
-//    mbarriers.  Warps 4-7 and 8-11 are the softmax warpgroups of the two
-//    heads: thread r owns query row r, reads its 64 scores with one
-//    tcgen05.ld, applies the causal mask and an online softmax in log2 units
-//    (the reference scale 1/sqrt(128) folded with log2 e), writes P as bf16
-//    into shared memory in the 128B-swizzled K-major layout the MMA reads,
-//    (two P buffers per head, so the softmax of tile j+1 does not wait for
-//    the MMA of tile j), and rescales O in tensor memory only when its running maximum grows by
-//    more than 2^8 (otherwise the stale maximum stays the reference; the
-//    final division uses the same reference, so the result is exact).
+//    rows).  The two query heads of an item share every K/V tile (GQA).
+//    Items are dealt to a persistent grid (one CTA per SM) in a snake order
+//    of decreasing causal length.
+//  * Warp 0 streams Q (3-D TMA, 128B swizzle) and 128-key K/V tiles of the
+//    paged bf16 cache (2-D TMA boxes of 64 keys x 64 dims, 128B swizzle)
+//    through a 2-stage ring.
+//  * Warp 1 issues every MMA from one lane.  Per head t and key tile j:
+//    S_t = Q_t.K_j^T (M128 N128 K128, both operands in shared memory) into
+//    the head's 128 tensor-memory columns; once the softmax has replaced S_t
+//    by P_t (bf16, packed into the first 64 of those columns),
+//    O_t += P_t.V_j (M128 N128 K128, A read from tensor memory, B = V from
+//    shared memory).  S_t(j+1) overwrites P_t(j), so it is issued once
+//    PV_t(j) has completed; the two heads alternate on the tensor core while
+//    the other head runs its softmax.
+//  * Warps 4-7 / 8-11 are the softmax warpgroups of the two heads: thread r
+//    owns query row r, reads its 128 scores with tcgen05.ld, applies the
+//    causal mask and an online softmax in log2 units (the reference scale
+//    1/sqrt(128) folded with log2 e), writes P back with tcgen05.st, and
+//    rescales O in tensor memory only when the running maximum grows by more
+//    than 2^8 (the final division uses the same reference maximum, so the
+//    result is exact).
 //  * The epilogue divides O by the row sum and stores the row (fp32 or bf16).
-// Tensor memory: 512 columns per CTA (S 2x2x64, O 2x128), one CTA per SM.
+// Per key tile and head the tensor core reads 64 KB of Q+K and 32 KB of V
+// from shared memory for 8.4 MFLOP (N = 128 on both MMAs keeps the
+// shared-memory read rate within its bandwidth); P never touches shared
+// memory.  Tensor memory: 512 columns (per head 128 S/P + 128 O).
 #include "q3a_common.cuh"
 #include "q3a_internal.h"
 
@@ -35,34 +41,33 @@ namespace q3a {
 namespace pf {
 
 constexpr int QT = 128;        // query rows per head tile
-constexpr int KT = 64;         // keys per K/V tile
+constexpr int KT = 128;        // keys per K/V tile
 constexpr int STAGES = 2;
 constexpr int NTHREADS = 384;  // 12 warps
-constexpr int Q_TILE_BYTES = QT * HD * 2;          // 32 KB (2 K-blocks of 128 rows x 128 B)
-constexpr int KV_TILE_BYTES = KT * HD * 2;         // 16 KB (2 blocks of 64 rows x 128 B)
-constexpr int P_TILE_BYTES = QT * KT * 2;          // 16 KB (128 rows x 128 B)
+constexpr int Q_TILE_BYTES = QT * HD * 2;          // 32 KB: 2 dim-blocks of [128 rows][128 B]
+constexpr int KV_TILE_BYTES = KT * HD * 2;         // 32 KB: 2 dim-blocks of [128 keys][128 B]
+constexpr int DBLK = KT * 128;                     // bytes of one 64-dim block of a K/V tile
 constexpr int OFF_Q = 0;                           // [2 heads][32 KB]
-constexpr int OFF_K = OFF_Q + 2 * Q_TILE_BYTES;    // [STAGES][16 KB]
+constexpr int OFF_K = OFF_Q + 2 * Q_TILE_BYTES;    // [STAGES][32 KB]
 constexpr int OFF_V = OFF_K + STAGES * KV_TILE_BYTES;
-constexpr int OFF_P = OFF_V + STAGES * KV_TILE_BYTES;  // [2 heads][2 bufs][16 KB]
-constexpr int OFF_BAR = OFF_P + 4 * P_TILE_BYTES;
+constexpr int OFF_BAR = OFF_V + STAGES * KV_TILE_BYTES;
 // barriers (8 bytes each)
 constexpr int B_QFULL = 0, B_QEMPTY = 1;
 constexpr int B_KFULL = 2, B_KEMPTY = B_KFULL + STAGES;
 constexpr int B_VFULL = B_KEMPTY + STAGES, B_VEMPTY = B_VFULL + STAGES;
-constexpr int B_SFULL = B_VEMPTY + STAGES;  // [head][buf]
-constexpr int B_SFREE = B_SFULL + 4;
-constexpr int B_PFULL = B_SFREE + 4;        // [head][buf]
-constexpr int B_PFREE = B_PFULL + 4;        // [head][buf]
-constexpr int B_OFREE = B_PFREE + 4;        // [head]
-constexpr int NBAR = B_OFREE + 2;
+constexpr int B_SFULL = B_VEMPTY + STAGES;  // [head] S in tensor memory
+constexpr int B_PFULL = B_SFULL + 2;        // [head] P written (4 warps)
+constexpr int B_PVDONE = B_PFULL + 2;       // [head] PV complete, P consumed
+constexpr int B_OFULL = B_PVDONE + 2;       // [head] last PV of an item complete
+constexpr int B_DRAIN = B_OFULL + 2;        // every issued MMA complete (exit)
+constexpr int NBAR = B_DRAIN + 1;
 constexpr int OFF_MISC = OFF_BAR + NBAR * 8;  // tmem address, abort flag
 constexpr int SMEM = OFF_MISC + 64 + 1024;    // + slack for 1024-byte alignment
 static_assert(SMEM <= 232448, "prefill shared memory exceeds the sm_100 limit");
 
 constexpr uint32_t TMEM_COLS = 512;
-constexpr uint32_t COL_S = 0;      // S[head][buf] at head*128 + buf*64
-constexpr uint32_t COL_O = 256;    // O[head] at 256 + head*128
+constexpr uint32_t HEAD_COLS = 256;  // head t: S/P at t*256, O at t*256 + 128
+constexpr uint32_t COL_O = 128;
 
 // instruction descriptors (kind::f16): c=F32 (bit 4), a=BF16 (bits 7-9),
 // b=BF16 (bits 10-12), b_major bit 16, N>>3 at bit 17, M>>4 at bit 24
@@ -86,14 +91,27 @@ __device__ __forceinline__ void tc_fence_after() {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
 
-__device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
-                                       uint32_t idesc, uint32_t accumulate) {
+// D (tensor memory) (+)= A (shared-memory descriptor) . B (shared-memory descriptor)
+__device__ __forceinline__ void tc_mma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                          uint32_t idesc, uint32_t accumulate) {
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
         "setp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n\t}" ::"r"(
             d_tmem),
         "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(0u)
+        : "memory");
+}
+
+// D (tensor memory) (+)= A (tensor memory) . B (shared-memory descriptor)
+__device__ __forceinline__ void tc_mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                          uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %5, %5, %5}, p;\n\t}" ::"r"(
+            d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(0u)
         : "memory");
 }
 
@@ -164,7 +182,7 @@ __device__ __forceinline__ bool pf_wait(uint64_t* bar, uint32_t parity, volatile
     return true;
 }
 
-// Work item i of n (i in decreasing-length order) -> (qt, g, hp).
+// Work item i (in decreasing-length order) -> (query tile, kv head, pair).
 struct PfItem {
     int qt, g, hp, nj;
 };
@@ -182,7 +200,7 @@ __device__ __forceinline__ PfItem pf_item(const PrefillParams& P, int i) {
     return it;
 }
 
-// The i-th item of CTA c in snake order over `nitems` items.
+// The r-th item of CTA c in snake order.
 __device__ __forceinline__ int pf_item_index(int c, int r, int G) {
     return r * G + ((r & 1) ? (G - 1 - c) : c);
 }
@@ -214,15 +232,13 @@ __global__ void __launch_bounds__(pf::NTHREADS, 1)
             mbar_init(&bars[B_VFULL + s], 1);
             mbar_init(&bars[B_VEMPTY + s], 1);
         }
-        for (int i = 0; i < 4; i++) {
-            mbar_init(&bars[B_SFULL + i], 1);
-            mbar_init(&bars[B_SFREE + i], 4);
+        for (int t = 0; t < 2; t++) {
+            mbar_init(&bars[B_SFULL + t], 1);
+            mbar_init(&bars[B_PFULL + t], 4);
+            mbar_init(&bars[B_PVDONE + t], 1);
+            mbar_init(&bars[B_OFULL + t], 1);
         }
-        for (int i = 0; i < 4; i++) {
-            mbar_init(&bars[B_PFULL + i], 4);
-            mbar_init(&bars[B_PFREE + i], 1);
-        }
-        for (int t = 0; t < 2; t++) mbar_init(&bars[B_OFREE + t], 4);
+        mbar_init(&bars[B_DRAIN], 1);
         *abort_flag = 0;
         fence_mbar_init();
     }
@@ -248,8 +264,9 @@ __global__ void __launch_bounds__(pf::NTHREADS, 1)
         if (lane == 0) {
             const uint64_t pol_q = l2_policy_evict_first();
             const uint64_t pol_kv = l2_policy_evict_last();  // K/V of a head are re-read by 16 items
-            int kv_it = 0, item_it = 0;
-            for (int r = 0;; r++) {
+            int kv_it = 0, item_it = 0, k_issued = 0, v_issued = 0;
+            bool dead = false;
+            for (int r = 0; !dead; r++) {
                 const int i = pf_item_index(c, r, G);
                 if (i >= n_items) break;
                 const PfItem it = pf_item(P, i);
@@ -262,131 +279,166 @@ __global__ void __launch_bounds__(pf::NTHREADS, 1)
                     tma_load_3d(dq, &tmQ, &bars[B_QFULL], 0, h, it.qt * QT, pol_q);
                     tma_load_3d(dq + QT * 128, &tmQ, &bars[B_QFULL], 64, h, it.qt * QT, pol_q);
                 }
-                bool dead = false;
+                item_it++;
                 for (int j = 0; j < it.nj; j++, kv_it++) {
                     const int st = kv_it % STAGES;
                     const uint32_t ph = (uint32_t)(kv_it / STAGES) & 1u;
-                    const int pt = P.page_tokens;
-                    const int t0 = j * KT;
-                    const long long phys = (long long)P.slot * P.pages_per_seq + t0 / pt;
-                    const int row = (int)((((long long)P.layer * P.nkv + it.g) * P.n_pages + phys) * pt +
-                                          (t0 % pt));
+                    // a 128-key tile is two 64-key runs, each inside one page
+                    // (pages hold a multiple of 64 tokens)
+                    int rows[2];
+                    for (int hf = 0; hf < 2; hf++) {
+                        const int t0 = j * KT + hf * 64;
+                        const int pt = P.page_tokens;
+                        const long long phys = (long long)P.slot * P.pages_per_seq + t0 / pt;
+                        rows[hf] = (int)((((long long)P.layer * P.nkv + it.g) * P.n_pages + phys) * pt +
+                                         (t0 % pt));
+                    }
                     if (kv_it >= STAGES && !pf_wait(&bars[B_KEMPTY + st], ph ^ 1u, abort_flag, P.err)) {
                         dead = true;
                         break;
                     }
                     uint8_t* dk = smem + OFF_K + st * KV_TILE_BYTES;
                     mbar_arrive_expect_tx(&bars[B_KFULL + st], (uint32_t)KV_TILE_BYTES);
-                    tma_load_2d(dk, &tmK, &bars[B_KFULL + st], 0, row, pol_kv);
-                    tma_load_2d(dk + KT * 128, &tmK, &bars[B_KFULL + st], 64, row, pol_kv);
+                    for (int hf = 0; hf < 2; hf++)
+                        for (int db = 0; db < 2; db++)
+                            tma_load_2d(dk + db * DBLK + hf * 64 * 128, &tmK, &bars[B_KFULL + st], db * 64,
+                                        rows[hf], pol_kv);
+                    k_issued = kv_it + 1;
                     if (kv_it >= STAGES && !pf_wait(&bars[B_VEMPTY + st], ph ^ 1u, abort_flag, P.err)) {
                         dead = true;
                         break;
                     }
                     uint8_t* dv = smem + OFF_V + st * KV_TILE_BYTES;
                     mbar_arrive_expect_tx(&bars[B_VFULL + st], (uint32_t)KV_TILE_BYTES);
-                    tma_load_2d(dv, &tmV, &bars[B_VFULL + st], 0, row, pol_kv);
-                    tma_load_2d(dv + KT * 128, &tmV, &bars[B_VFULL + st], 64, row, pol_kv);
+                    for (int hf = 0; hf < 2; hf++)
+                        for (int db = 0; db < 2; db++)
+                            tma_load_2d(dv + db * DBLK + hf * 64 * 128, &tmV, &bars[B_VFULL + st], db * 64,
+                                        rows[hf], pol_kv);
+                    v_issued = kv_it + 1;
                 }
-                if (dead) break;
-                item_it++;
             }
+            // drain: the CTA may not exit with bulk copies still writing its
+            // shared memory (only matters after an abort; a no-op otherwise)
+            if (item_it > 0) mbar_wait(&bars[B_QFULL], (uint32_t)(item_it - 1) & 1u);
+            for (int k = (k_issued > STAGES ? k_issued - STAGES : 0); k < k_issued; k++)
+                mbar_wait(&bars[B_KFULL + k % STAGES], (uint32_t)(k / STAGES) & 1u);
+            for (int k = (v_issued > STAGES ? v_issued - STAGES : 0); k < v_issued; k++)
+                mbar_wait(&bars[B_VFULL + k % STAGES], (uint32_t)(k / STAGES) & 1u);
         }
     } else if (warp == 1) {
         // ============================================ MMA issuer
         if (lane == 0) {
-            int kv_it = 0, item_it = 0, s_it = 0, pv_it = 0;
+            int kv_base = 0, item_it = 0;
+            uint32_t pv_n[2] = {0u, 0u};  // PVs issued per head
             bool dead = false;
+            auto issue_s = [&](int t, int st) {
+                const uint32_t kb = s_base + OFF_K + st * KV_TILE_BYTES;
+                const uint32_t qb = s_base + OFF_Q + t * Q_TILE_BYTES;
+                const uint32_t d = tmem + t * HEAD_COLS;
+#pragma unroll
+                for (int kk = 0; kk < HD / 16; kk++) {
+                    const uint32_t koff = (kk & 3) * 32;  // 16 bf16 along K in a 128-byte row
+                    const uint64_t da = smem_desc(qb + (kk >> 2) * (QT * 128) + koff, 16, 1024);
+                    const uint64_t db = smem_desc(kb + (kk >> 2) * DBLK + koff, 16, 1024);
+                    tc_mma_ss(d, da, db, IDESC_S, kk > 0 ? 1u : 0u);
+                }
+                tc_commit(&bars[B_SFULL + t]);
+            };
             for (int r = 0; !dead; r++) {
                 const int i = pf_item_index(c, r, G);
                 if (i >= n_items) break;
                 const PfItem it = pf_item(P, i);
+                const int nj = it.nj;
                 if (!pf_wait(&bars[B_QFULL], item_it & 1, abort_flag, P.err)) break;
-                if (item_it > 0) {
-                    // the previous item's epilogue has read O
-                    if (!pf_wait(&bars[B_OFREE + 0], (item_it - 1) & 1, abort_flag, P.err) ||
-                        !pf_wait(&bars[B_OFREE + 1], (item_it - 1) & 1, abort_flag, P.err))
+                {
+                    // S(0) of both heads; head t's columns still hold P of the
+                    // previous item until its last PV has completed
+                    const int st = kv_base % STAGES;
+                    if (!pf_wait(&bars[B_KFULL + st], (uint32_t)(kv_base / STAGES) & 1u, abort_flag, P.err))
                         break;
-                }
-                tc_fence_after();
-                // S(j) for both heads into buffer s_it&1, then release K(j)
-                auto issue_s = [&](int j) -> bool {
-                    const int st = (kv_it + j) % STAGES;
-                    const uint32_t ph = (uint32_t)((kv_it + j) / STAGES) & 1u;
-                    if (!pf_wait(&bars[B_KFULL + st], ph, abort_flag, P.err)) return false;
-                    const int buf = s_it & 1;
-                    if (s_it >= 2 &&
-                        (!pf_wait(&bars[B_SFREE + 0 * 2 + buf], ((s_it >> 1) - 1) & 1, abort_flag, P.err) ||
-                         !pf_wait(&bars[B_SFREE + 1 * 2 + buf], ((s_it >> 1) - 1) & 1, abort_flag, P.err)))
-                        return false;
-                    tc_fence_after();
-                    const uint32_t kb = s_base + OFF_K + st * KV_TILE_BYTES;
-                    for (int t = 0; t < 2; t++) {
-                        const uint32_t qb = s_base + OFF_Q + t * Q_TILE_BYTES;
-                        const uint32_t d = tmem + COL_S + t * 128 + buf * 64;
-#pragma unroll
-                        for (int kk = 0; kk < HD / 16; kk++) {
-                            const uint32_t koff = (kk & 3) * 32;  // 16 bf16 along K in the 128 B row
-                            const uint64_t da = smem_desc(qb + (kk >> 2) * (QT * 128) + koff, 16, 1024);
-                            const uint64_t db = smem_desc(kb + (kk >> 2) * (KT * 128) + koff, 16, 1024);
-                            tc_mma(d, da, db, IDESC_S, kk > 0 ? 1u : 0u);
-                        }
-                        tc_commit(&bars[B_SFULL + t * 2 + buf]);
-                    }
-                    tc_commit(&bars[B_KEMPTY + st]);
-                    s_it++;
-                    return true;
-                };
-                if (!issue_s(0)) break;
-                for (int j = 0; j < it.nj; j++) {
-                    if (j + 1 < it.nj && !issue_s(j + 1)) {
-                        dead = true;
-                        break;
-                    }
-                    const int st = (kv_it + j) % STAGES;
-                    const uint32_t ph = (uint32_t)((kv_it + j) / STAGES) & 1u;
-                    if (!pf_wait(&bars[B_VFULL + st], ph, abort_flag, P.err)) {
-                        dead = true;
-                        break;
-                    }
-                    const uint32_t vb = s_base + OFF_V + st * KV_TILE_BYTES;
-                    const int pbuf = pv_it & 1;
-                    for (int t = 0; t < 2; t++) {
-                        if (!pf_wait(&bars[B_PFULL + t * 2 + pbuf], (pv_it >> 1) & 1, abort_flag,
-                                     P.err)) {
+                    for (int t = 0; t < 2 && !dead; t++) {
+                        if (pv_n[t] > 0 &&
+                            !pf_wait(&bars[B_PVDONE + t], (pv_n[t] - 1) & 1u, abort_flag, P.err)) {
                             dead = true;
                             break;
                         }
                         tc_fence_after();
-                        const uint32_t pb = s_base + OFF_P + (t * 2 + pbuf) * P_TILE_BYTES;
-                        const uint32_t d = tmem + COL_O + t * 128;
-#pragma unroll
-                        for (int kk = 0; kk < KT / 16; kk++) {
-                            const uint64_t da = smem_desc(pb + kk * 32, 16, 1024);
-                            const uint64_t db = smem_desc(vb + kk * 16 * 128, KT * 128, 1024);
-                            tc_mma(d, da, db, IDESC_PV, (j > 0 || kk > 0) ? 1u : 0u);
-                        }
-                        // completes when this PV (and every earlier MMA) is done
-                        tc_commit(&bars[B_PFREE + t * 2 + pbuf]);
+                        issue_s(t, st);
                     }
                     if (dead) break;
-                    tc_commit(&bars[B_VEMPTY + st]);
-                    pv_it++;
+                    tc_commit(&bars[B_KEMPTY + st]);
+                    if (nj == 1) tc_commit(&bars[B_QEMPTY]);
+                }
+                for (int j = 0; j < nj && !dead; j++) {
+                    const int kj = kv_base + j;
+                    const int st = kj % STAGES;
+                    if (!pf_wait(&bars[B_VFULL + st], (uint32_t)(kj / STAGES) & 1u, abort_flag, P.err)) {
+                        dead = true;
+                        break;
+                    }
+                    const int kn = kj + 1;
+                    const int stn = kn % STAGES;
+                    const uint32_t vb = s_base + OFF_V + st * KV_TILE_BYTES;
+                    for (int t = 0; t < 2; t++) {
+                        // O_t += P_t . V_j once the softmax has written P_t
+                        // (its arrive also orders the epilogue's reads of the
+                        // previous item's O before this overwrite)
+                        if (!pf_wait(&bars[B_PFULL + t], pv_n[t] & 1u, abort_flag, P.err)) {
+                            dead = true;
+                            break;
+                        }
+                        tc_fence_after();
+                        const uint32_t d = tmem + t * HEAD_COLS + COL_O;
+                        const uint32_t pa = tmem + t * HEAD_COLS;
+#pragma unroll
+                        for (int kk = 0; kk < KT / 16; kk++) {
+                            // A = P columns [8kk, 8kk+8) (16 keys, bf16 pairs);
+                            // B = V rows [16kk, 16kk+16), MN-major, the two
+                            // 64-dim blocks DBLK apart
+                            const uint64_t db = smem_desc(vb + kk * 16 * 128, DBLK, 1024);
+                            tc_mma_ts(d, pa + kk * 8, db, IDESC_PV, (j > 0 || kk > 0) ? 1u : 0u);
+                        }
+                        tc_commit(&bars[B_PVDONE + t]);
+                        pv_n[t]++;
+                        if (j == nj - 1) tc_commit(&bars[B_OFULL + t]);
+                        if (t == 1) tc_commit(&bars[B_VEMPTY + st]);
+                        if (j + 1 < nj) {
+                            // S_t(j+1) overwrites P_t(j): wait for that PV
+                            if (!pf_wait(&bars[B_PVDONE + t], (pv_n[t] - 1) & 1u, abort_flag, P.err)) {
+                                dead = true;
+                                break;
+                            }
+                            if (t == 0 &&
+                                !pf_wait(&bars[B_KFULL + stn], (uint32_t)(kn / STAGES) & 1u, abort_flag,
+                                         P.err)) {
+                                dead = true;
+                                break;
+                            }
+                            tc_fence_after();
+                            issue_s(t, stn);
+                            if (t == 1) {
+                                tc_commit(&bars[B_KEMPTY + stn]);
+                                if (j + 2 == nj) tc_commit(&bars[B_QEMPTY]);
+                            }
+                        }
+                    }
                 }
                 if (dead) break;
-                tc_commit(&bars[B_QEMPTY]);
-                kv_it += it.nj;
+                kv_base += nj;
                 item_it++;
             }
+            // drain: tensor memory is freed only after every issued MMA is done
+            tc_commit(&bars[B_DRAIN]);
+            mbar_wait(&bars[B_DRAIN], 0u);
         }
     } else if (warp >= 4) {
         // ============================================ softmax warpgroups
         const int t = (warp - 4) >> 2;            // head of the pair
-        const int rw = warp & 3;                  // TMEM lane quarter
+        const int rw = warp & 3;                  // tensor-memory lane quarter
         const int row = rw * 32 + lane;           // query row within the tile
-        const uint32_t lane_base = (uint32_t)(rw * 32) << 16;
+        const uint32_t tl = tmem + ((uint32_t)(rw * 32) << 16) + t * HEAD_COLS;  // this row, head t
         const float2 sc2 = make_float2(P.scale_log2e, P.scale_log2e);
-        int s_it = 0, pv_it = 0, item_it = 0;
+        int s_it = 0, item_it = 0;
         for (int r = 0;; r++) {
             const int i = pf_item_index(c, r, G);
             if (i >= n_items) break;
@@ -395,26 +447,23 @@ __global__ void __launch_bounds__(pf::NTHREADS, 1)
             float m_ref = -INFINITY, l_sum = 0.0f;
             bool dead = false;
             for (int j = 0; j < it.nj; j++) {
-                const int buf = s_it & 1;
-                if (!pf_wait(&bars[B_SFULL + t * 2 + buf], (s_it >> 1) & 1, abort_flag, P.err)) {
+                if (!pf_wait(&bars[B_SFULL + t], (uint32_t)s_it & 1u, abort_flag, P.err)) {
                     dead = true;
                     break;
                 }
-                tc_fence_after();
-                uint32_t sr[64];
-                const uint32_t sa = tmem + lane_base + COL_S + t * 128 + buf * 64;
-                Q3A_TC_LD32(sa, sr, 0);
-                Q3A_TC_LD32(sa + 32, sr, 32);
-                tc_wait_ld();
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&bars[B_SFREE + t * 2 + buf]);
                 s_it++;
+                tc_fence_after();
+                uint32_t sr[128];
+                Q3A_TC_LD32(tl, sr, 0);
+                Q3A_TC_LD32(tl + 32, sr, 32);
+                Q3A_TC_LD32(tl + 64, sr, 64);
+                Q3A_TC_LD32(tl + 96, sr, 96);
+                tc_wait_ld();
                 // causal mask: only rows the diagonal crosses in this tile
                 const int k0 = j * KT;
                 if (k0 + KT - 1 > q_abs) {
 #pragma unroll
-                    for (int cc = 0; cc < 64; cc++)
+                    for (int cc = 0; cc < 128; cc++)
                         if (k0 + cc > q_abs) sr[cc] = __float_as_uint(-INFINITY);
                 }
                 // running maximum on raw scores (the scale is positive), tree
@@ -422,7 +471,8 @@ __global__ void __launch_bounds__(pf::NTHREADS, 1)
 #pragma unroll
                 for (int u = 0; u < 8; u++) mx8[u] = __uint_as_float(sr[u]);
 #pragma unroll
-                for (int cc = 8; cc < 64; cc++) mx8[cc & 7] = fmaxf(mx8[cc & 7], __uint_as_float(sr[cc]));
+                for (int cc = 8; cc < 128; cc++)
+                    mx8[cc & 7] = fmaxf(mx8[cc & 7], __uint_as_float(sr[cc]));
                 const float mt = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
                                        fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]))) *
                                  P.scale_log2e;
@@ -433,91 +483,69 @@ __global__ void __launch_bounds__(pf::NTHREADS, 1)
                     rescale = (m_ref != -INFINITY);
                     m_ref = mt;
                 }
-                // p = 2^(s*scale - m_ref), packed fp32x2 math, 4 partial sums
+                // p = 2^(s*scale - m_ref) with packed fp32x2 math, in two
+                // halves of 64 keys; each half is packed to bf16 pairs
+                // (column c: keys 2c, 2c+1) and stored over the first 64
+                // columns of this row's S
                 const float2 nm2 = make_float2(-m_ref, -m_ref);
                 float2 ps2[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f),
                                  make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
-                uint32_t pk[32];
 #pragma unroll
-                for (int cc = 0; cc < 64; cc += 2) {
-                    const float2 x = __ffma2_rn(
-                        make_float2(__uint_as_float(sr[cc]), __uint_as_float(sr[cc + 1])), sc2, nm2);
-                    const float2 pp = make_float2(exp2_approx(x.x), exp2_approx(x.y));
-                    ps2[(cc >> 1) & 3] = __fadd2_rn(ps2[(cc >> 1) & 3], pp);
-                    __nv_bfloat162 b2 = __floats2bfloat162_rn(pp.x, pp.y);
-                    pk[cc >> 1] = *reinterpret_cast<uint32_t*>(&b2);
+                for (int hf = 0; hf < 2; hf++) {
+                    uint32_t pk[32];
+#pragma unroll
+                    for (int cc = 0; cc < 64; cc += 2) {
+                        const float2 x = __ffma2_rn(make_float2(__uint_as_float(sr[hf * 64 + cc]),
+                                                                __uint_as_float(sr[hf * 64 + cc + 1])),
+                                                    sc2, nm2);
+                        const float2 pp = make_float2(exp2_approx(x.x), exp2_approx(x.y));
+                        ps2[(cc >> 1) & 3] = __fadd2_rn(ps2[(cc >> 1) & 3], pp);
+                        __nv_bfloat162 b2 = __floats2bfloat162_rn(pp.x, pp.y);
+                        pk[cc >> 1] = *reinterpret_cast<uint32_t*>(&b2);
+                    }
+                    Q3A_TC_ST32(tl + hf * 32, pk, 0);
                 }
                 const float2 s01 = __fadd2_rn(ps2[0], ps2[1]), s23 = __fadd2_rn(ps2[2], ps2[3]);
                 const float2 s4 = __fadd2_rn(s01, s23);
                 l_sum = l_sum * alpha + (s4.x + s4.y);
-                // P(j) goes to buffer pv_it&1 once the PV that last read it is done
-                const int pbuf = pv_it & 1;
-                if (pv_it >= 2 &&
-                    !pf_wait(&bars[B_PFREE + t * 2 + pbuf], ((pv_it >> 1) - 1) & 1, abort_flag,
-                             P.err)) {
-                    dead = true;
-                    break;
-                }
-                if (rescale && j > 0) {
-                    // O must be complete up to PV(j-1) before it is rescaled:
-                    // wait for that PV's commit on its P buffer (a barrier is
-                    // only ever awaited one phase ahead of what it completed)
-                    if (!pf_wait(&bars[B_PFREE + t * 2 + ((pv_it - 1) & 1)], ((pv_it - 1) >> 1) & 1,
-                                 abort_flag, P.err)) {
-                        dead = true;
-                        break;
-                    }
-                    tc_fence_after();
-                    uint32_t orr[64];
-                    for (int half = 0; half < 2; half++) {
-                        const uint32_t oa = tmem + lane_base + COL_O + t * 128 + half * 64;
-                        Q3A_TC_LD32(oa, orr, 0);
-                        Q3A_TC_LD32(oa + 32, orr, 32);
+                if (rescale) {
+                    // S_t(j) was issued after PV_t(j-1) completed, so O holds
+                    // every tile before j and no MMA writes it until P_t(j)
+                    // is signalled below
+#pragma unroll 1
+                    for (int q = 0; q < 4; q++) {
+                        uint32_t orr[32];
+                        Q3A_TC_LD32(tl + COL_O + 32 * q, orr, 0);
                         tc_wait_ld();
 #pragma unroll
-                        for (int cc = 0; cc < 64; cc++)
+                        for (int cc = 0; cc < 32; cc++)
                             orr[cc] = __float_as_uint(__uint_as_float(orr[cc]) * alpha);
-                        Q3A_TC_ST32(oa, orr, 0);
-                        Q3A_TC_ST32(oa + 32, orr, 32);
+                        Q3A_TC_ST32(tl + COL_O + 32 * q, orr, 0);
                     }
-                    tc_wait_st();
                 }
-                tc_fence_after();
-                // P row -> shared memory, 128B-swizzled K-major layout
-                uint8_t* prow = smem + OFF_P + (t * 2 + pbuf) * P_TILE_BYTES + row * 128;
-#pragma unroll
-                for (int ch = 0; ch < 8; ch++) {
-                    const int pch = ch ^ (row & 7);
-                    *reinterpret_cast<uint4*>(prow + pch * 16) =
-                        make_uint4(pk[4 * ch], pk[4 * ch + 1], pk[4 * ch + 2], pk[4 * ch + 3]);
-                }
-                fence_proxy_async_smem();
+                tc_wait_st();
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&bars[B_PFULL + t * 2 + pbuf]);
-                pv_it++;
+                if (lane == 0) mbar_arrive(&bars[B_PFULL + t]);
             }
             if (dead) break;
-            // epilogue: O / l once the item's last PV (hence every PV) is done
-            if (!pf_wait(&bars[B_PFREE + t * 2 + ((pv_it - 1) & 1)], ((pv_it - 1) >> 1) & 1,
-                         abort_flag, P.err))
-                break;
+            // epilogue: O / l once the item's last PV is done
+            if (!pf_wait(&bars[B_OFULL + t], (uint32_t)item_it & 1u, abort_flag, P.err)) break;
             tc_fence_after();
             const int srow = it.qt * QT + row;  // prompt row
             const int h = (P.kv0 + it.g) * GQA + 2 * it.hp + t;
             const float inv = 1.0f / l_sum;
-            for (int half = 0; half < 2; half++) {
-                uint32_t orr[64];
-                const uint32_t oa = tmem + lane_base + COL_O + t * 128 + half * 64;
-                Q3A_TC_LD32(oa, orr, 0);
-                Q3A_TC_LD32(oa + 32, orr, 32);
+#pragma unroll 1
+            for (int q = 0; q < 4; q++) {
+                uint32_t orr[32];
+                Q3A_TC_LD32(tl + COL_O + 32 * q, orr, 0);
                 tc_wait_ld();
                 if (srow < P.n_tok) {
-                    const size_t o = ((size_t)srow * P.hq_total + h) * HD + half * 64;
+                    const size_t o = ((size_t)srow * P.hq_total + h) * HD + q * 32;
                     if (P.out_f32) {
                         float4* dst = reinterpret_cast<float4*>(P.out_f32 + o);
 #pragma unroll
-                        for (int q4 = 0; q4 < 16; q4++)
+                        for (int q4 = 0; q4 < 8; q4++)
                             dst[q4] = make_float4(__uint_as_float(orr[4 * q4]) * inv,
                                                   __uint_as_float(orr[4 * q4 + 1]) * inv,
                                                   __uint_as_float(orr[4 * q4 + 2]) * inv,
@@ -525,7 +553,7 @@ __global__ void __launch_bounds__(pf::NTHREADS, 1)
                     } else {
                         uint4* dst = reinterpret_cast<uint4*>(P.out_bf16 + o);
 #pragma unroll
-                        for (int q8 = 0; q8 < 8; q8++) {
+                        for (int q8 = 0; q8 < 4; q8++) {
                             uint32_t w[4];
 #pragma unroll
                             for (int e = 0; e < 4; e++) {
@@ -539,9 +567,10 @@ __global__ void __launch_bounds__(pf::NTHREADS, 1)
                     }
                 }
             }
+            // the next item's first PFULL arrive (after this code in program
+            // order, behind wait::ld and a before_thread_sync fence) is what
+            // lets the issuer overwrite O
             tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&bars[B_OFREE + t]);
             item_it++;
         }
     }
