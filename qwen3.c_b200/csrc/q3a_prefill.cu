@@ -50,14 +50,17 @@ constexpr int DBLK = KT * 128;                     // bytes of one 64-dim block 
 constexpr int OFF_Q = 0;                           // [2 heads][32 KB]
 constexpr int OFF_K = OFF_Q + 2 * Q_TILE_BYTES;    // [STAGES][32 KB]
 constexpr int OFF_V = OFF_K + STAGES * KV_TILE_BYTES;
-constexpr int OFF_BAR = OFF_V + STAGES * KV_TILE_BYTES;
+constexpr int STG_BYTES = 32 * 128;                 // per softmax warp: 32 rows x 128 B
+constexpr int OFF_STG = OFF_V + STAGES * KV_TILE_BYTES;  // [8 warps] epilogue staging
+constexpr int OFF_BAR = OFF_STG + 8 * STG_BYTES;
 // barriers (8 bytes each)
 constexpr int B_QFULL = 0, B_QEMPTY = 1;
 constexpr int B_KFULL = 2, B_KEMPTY = B_KFULL + STAGES;
 constexpr int B_VFULL = B_KEMPTY + STAGES, B_VEMPTY = B_VFULL + STAGES;
 constexpr int B_SFULL = B_VEMPTY + STAGES;  // [head] S in tensor memory
-constexpr int B_PFULL = B_SFULL + 2;        // [head] P written (4 warps)
-constexpr int B_PVDONE = B_PFULL + 2;       // [head] PV complete, P consumed
+constexpr int B_PLO = B_SFULL + 2;          // [head] P of keys 0-63 written (4 warps)
+constexpr int B_PHI = B_PLO + 2;            // [head] P of keys 64-127 written (4 warps)
+constexpr int B_PVDONE = B_PHI + 2;         // [head] PV complete, P consumed
 constexpr int B_OFULL = B_PVDONE + 2;       // [head] last PV of an item complete
 constexpr int B_DRAIN = B_OFULL + 2;        // every issued MMA complete (exit)
 constexpr int NBAR = B_DRAIN + 1;
@@ -165,6 +168,41 @@ __device__ __forceinline__ float exp2_approx(float x) {
     return y;
 }
 
+constexpr uint32_t NEG_INF_BITS = 0xff800000u;
+
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+
+// One pair in EXP2_POLY_EVERY of the softmax weights is computed by
+// exp2_poly2, which runs on the FMA pipe and so adds throughput next to the
+// MUFU unit (16 results per clock per SM).
+constexpr int EXP2_POLY_EVERY = 4;
+
+// 2^x for a pair, x <= 9: round x to j = nearest integer by the 1.5 * 2^23
+// addition (the integer lands in the low mantissa bits of t), evaluate a
+// cubic for 2^f on f = x - j in [-1/2, 1/2], and add j to the exponent
+// field.  The cubic is a least-squares fit of 2^f on Chebyshev nodes
+// weighted for relative error; its maximum relative error on
+// [-1/2, 1/2] is 7.5e-5, far below the bf16 rounding P receives.  x is
+// clamped at -126 so the exponent sum cannot wrap (values below 2^-126
+// come out as tiny denormals, not zero).
+__device__ __forceinline__ float2 exp2_poly2(float2 x) {
+    x.x = fmaxf(x.x, -126.0f);
+    x.y = fmaxf(x.y, -126.0f);
+    const float2 t = __fadd2_rn(x, make_float2(12582912.0f, 12582912.0f));
+    const float2 jf = __fadd2_rn(t, make_float2(-12582912.0f, -12582912.0f));
+    const float2 f = __fadd2_rn(x, make_float2(-jf.x, -jf.y));
+    float2 p = __ffma2_rn(make_float2(0.05517168715596199f, 0.05517168715596199f), f,
+                          make_float2(0.2426111400127411f, 0.2426111400127411f));
+    p = __ffma2_rn(p, f, make_float2(0.6932609677314758f, 0.6932609677314758f));
+    p = __ffma2_rn(p, f, make_float2(0.9999280571937561f, 0.9999280571937561f));
+    return make_float2(__int_as_float(__float_as_int(p.x) + (__float_as_int(t.x) << 23)),
+                       __int_as_float(__float_as_int(p.y) + (__float_as_int(t.y) << 23)));
+}
+
 // Bounded wait that also gives up as soon as another thread of the CTA has
 // given up (the shared abort word), so a stalled pipeline unwinds in about
 // one wait limit instead of one per remaining wait.
@@ -234,7 +272,8 @@ __global__ void __launch_bounds__(pf::NTHREADS, 1)
         }
         for (int t = 0; t < 2; t++) {
             mbar_init(&bars[B_SFULL + t], 1);
-            mbar_init(&bars[B_PFULL + t], 4);
+            mbar_init(&bars[B_PLO + t], 4);
+            mbar_init(&bars[B_PHI + t], 4);
             mbar_init(&bars[B_PVDONE + t], 1);
             mbar_init(&bars[B_OFULL + t], 1);
         }
@@ -380,24 +419,29 @@ __global__ void __launch_bounds__(pf::NTHREADS, 1)
                     const int stn = kn % STAGES;
                     const uint32_t vb = s_base + OFF_V + st * KV_TILE_BYTES;
                     for (int t = 0; t < 2; t++) {
-                        // O_t += P_t . V_j once the softmax has written P_t
-                        // (its arrive also orders the epilogue's reads of the
+                        // O_t += P_t . V_j, each half of the keys as soon as the
+                        // softmax has written its half of P_t (the first
+                        // arrive also orders the epilogue's reads of the
                         // previous item's O before this overwrite)
-                        if (!pf_wait(&bars[B_PFULL + t], pv_n[t] & 1u, abort_flag, P.err)) {
-                            dead = true;
-                            break;
-                        }
-                        tc_fence_after();
                         const uint32_t d = tmem + t * HEAD_COLS + COL_O;
                         const uint32_t pa = tmem + t * HEAD_COLS;
+                        for (int hf = 0; hf < 2; hf++) {
+                            if (!pf_wait(&bars[(hf ? B_PHI : B_PLO) + t], pv_n[t] & 1u, abort_flag, P.err)) {
+                                dead = true;
+                                break;
+                            }
+                            tc_fence_after();
 #pragma unroll
-                        for (int kk = 0; kk < KT / 16; kk++) {
-                            // A = P columns [8kk, 8kk+8) (16 keys, bf16 pairs);
-                            // B = V rows [16kk, 16kk+16), MN-major, the two
-                            // 64-dim blocks DBLK apart
-                            const uint64_t db = smem_desc(vb + kk * 16 * 128, DBLK, 1024);
-                            tc_mma_ts(d, pa + kk * 8, db, IDESC_PV, (j > 0 || kk > 0) ? 1u : 0u);
+                            for (int k4 = 0; k4 < KT / 32; k4++) {
+                                // A = P columns [8kk, 8kk+8) (16 keys, bf16
+                                // pairs); B = V rows [16kk, 16kk+16),
+                                // MN-major, the two 64-dim blocks DBLK apart
+                                const int kk = hf * (KT / 32) + k4;
+                                const uint64_t db = smem_desc(vb + kk * 16 * 128, DBLK, 1024);
+                                tc_mma_ts(d, pa + kk * 8, db, IDESC_PV, (j > 0 || kk > 0) ? 1u : 0u);
+                            }
                         }
+                        if (dead) break;
                         tc_commit(&bars[B_PVDONE + t]);
                         pv_n[t]++;
                         if (j == nj - 1) tc_commit(&bars[B_OFULL + t]);
@@ -459,23 +503,26 @@ __global__ void __launch_bounds__(pf::NTHREADS, 1)
                 Q3A_TC_LD32(tl + 64, sr, 64);
                 Q3A_TC_LD32(tl + 96, sr, 96);
                 tc_wait_ld();
-                // causal mask: only rows the diagonal crosses in this tile
-                const int k0 = j * KT;
-                if (k0 + KT - 1 > q_abs) {
+                // causal mask: keys after this row's position, only in tiles
+                // the diagonal crosses
+                const int lim = q_abs - j * KT;  // last visible key of this tile
+                if (lim < KT - 1) {
 #pragma unroll
                     for (int cc = 0; cc < 128; cc++)
-                        if (k0 + cc > q_abs) sr[cc] = __float_as_uint(-INFINITY);
+                        sr[cc] = (cc > lim) ? NEG_INF_BITS : sr[cc];
                 }
-                // running maximum on raw scores (the scale is positive), tree
-                float mx8[8];
+                // running maximum on raw scores (the scale is positive)
+                float mx4[4];
 #pragma unroll
-                for (int u = 0; u < 8; u++) mx8[u] = __uint_as_float(sr[u]);
+                for (int u = 0; u < 4; u++) mx4[u] = max3f(__uint_as_float(sr[u]), __uint_as_float(sr[4 + u]), __uint_as_float(sr[8 + u]));
 #pragma unroll
-                for (int cc = 8; cc < 128; cc++)
-                    mx8[cc & 7] = fmaxf(mx8[cc & 7], __uint_as_float(sr[cc]));
-                const float mt = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                                       fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]))) *
-                                 P.scale_log2e;
+                for (int cc = 12; cc < 124; cc += 8)
+#pragma unroll
+                    for (int u = 0; u < 4; u++)
+                        mx4[u] = max3f(mx4[u], __uint_as_float(sr[cc + u]), __uint_as_float(sr[cc + 4 + u]));
+#pragma unroll
+                for (int u = 0; u < 4; u++) mx4[u] = fmaxf(mx4[u], __uint_as_float(sr[124 + u]));
+                const float mt = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * P.scale_log2e;
                 float alpha = 1.0f;
                 bool rescale = false;
                 if (mt > m_ref + 8.0f) {  // includes the first tile (m_ref = -inf)
@@ -485,8 +532,11 @@ __global__ void __launch_bounds__(pf::NTHREADS, 1)
                 }
                 // p = 2^(s*scale - m_ref) with packed fp32x2 math, in two
                 // halves of 64 keys; each half is packed to bf16 pairs
-                // (column c: keys 2c, 2c+1) and stored over the first 64
-                // columns of this row's S
+                // (column c: keys 2c, 2c+1), stored over the first 64 columns
+                // of this row's S and signalled on its own barrier, so the
+                // first half of PV runs while the second half is computed.
+                // One pair in EXP2_POLY_EVERY takes the polynomial 2^x on the
+                // FMA pipe instead of the MUFU unit.
                 const float2 nm2 = make_float2(-m_ref, -m_ref);
                 float2 ps2[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f),
                                  make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
@@ -498,76 +548,102 @@ __global__ void __launch_bounds__(pf::NTHREADS, 1)
                         const float2 x = __ffma2_rn(make_float2(__uint_as_float(sr[hf * 64 + cc]),
                                                                 __uint_as_float(sr[hf * 64 + cc + 1])),
                                                     sc2, nm2);
-                        const float2 pp = make_float2(exp2_approx(x.x), exp2_approx(x.y));
+                        float2 pp;
+                        if (EXP2_POLY_EVERY > 0 && (cc >> 1) % EXP2_POLY_EVERY == EXP2_POLY_EVERY - 1)
+                            pp = exp2_poly2(x);
+                        else
+                            pp = make_float2(exp2_approx(x.x), exp2_approx(x.y));
                         ps2[(cc >> 1) & 3] = __fadd2_rn(ps2[(cc >> 1) & 3], pp);
                         __nv_bfloat162 b2 = __floats2bfloat162_rn(pp.x, pp.y);
                         pk[cc >> 1] = *reinterpret_cast<uint32_t*>(&b2);
                     }
                     Q3A_TC_ST32(tl + hf * 32, pk, 0);
+                    if (hf == 0 && rescale) {
+                        // O *= alpha before the first half of PV(j) adds to
+                        // it.  S_t(j) was issued after PV_t(j-1) completed,
+                        // so O holds every tile before j, and no MMA writes
+                        // it before P_t(j) is signalled below.
+#pragma unroll 1
+                        for (int q = 0; q < 4; q++) {
+                            uint32_t orr[32];
+                            Q3A_TC_LD32(tl + COL_O + 32 * q, orr, 0);
+                            tc_wait_ld();
+#pragma unroll
+                            for (int cc = 0; cc < 32; cc++)
+                                orr[cc] = __float_as_uint(__uint_as_float(orr[cc]) * alpha);
+                            Q3A_TC_ST32(tl + COL_O + 32 * q, orr, 0);
+                        }
+                    }
+                    tc_wait_st();
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&bars[(hf ? B_PHI : B_PLO) + t]);
                 }
                 const float2 s01 = __fadd2_rn(ps2[0], ps2[1]), s23 = __fadd2_rn(ps2[2], ps2[3]);
                 const float2 s4 = __fadd2_rn(s01, s23);
                 l_sum = l_sum * alpha + (s4.x + s4.y);
-                if (rescale) {
-                    // S_t(j) was issued after PV_t(j-1) completed, so O holds
-                    // every tile before j and no MMA writes it until P_t(j)
-                    // is signalled below
-#pragma unroll 1
-                    for (int q = 0; q < 4; q++) {
-                        uint32_t orr[32];
-                        Q3A_TC_LD32(tl + COL_O + 32 * q, orr, 0);
-                        tc_wait_ld();
-#pragma unroll
-                        for (int cc = 0; cc < 32; cc++)
-                            orr[cc] = __float_as_uint(__uint_as_float(orr[cc]) * alpha);
-                        Q3A_TC_ST32(tl + COL_O + 32 * q, orr, 0);
-                    }
-                }
-                tc_wait_st();
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&bars[B_PFULL + t]);
             }
             if (dead) break;
-            // epilogue: O / l once the item's last PV is done
+            // epilogue: O / l once the item's last PV is done.  Each warp
+            // stages 32 rows x 32 columns at a time in its own shared-memory
+            // buffer (16-byte chunks XOR-swizzled by row) and writes them
+            // back row-contiguous, so every global store fills whole sectors.
             if (!pf_wait(&bars[B_OFULL + t], (uint32_t)item_it & 1u, abort_flag, P.err)) break;
             tc_fence_after();
-            const int srow = it.qt * QT + row;  // prompt row
+            const int srow0 = it.qt * QT + rw * 32;  // prompt row of lane 0
             const int h = (P.kv0 + it.g) * GQA + 2 * it.hp + t;
             const float inv = 1.0f / l_sum;
+            uint8_t* stg = smem + OFF_STG + (warp - 4) * STG_BYTES;
 #pragma unroll 1
             for (int q = 0; q < 4; q++) {
                 uint32_t orr[32];
                 Q3A_TC_LD32(tl + COL_O + 32 * q, orr, 0);
                 tc_wait_ld();
-                if (srow < P.n_tok) {
-                    const size_t o = ((size_t)srow * P.hq_total + h) * HD + q * 32;
-                    if (P.out_f32) {
-                        float4* dst = reinterpret_cast<float4*>(P.out_f32 + o);
+                if (P.out_f32) {
+                    // row: 32 fp32 = 8 chunks of 16 B
 #pragma unroll
-                        for (int q4 = 0; q4 < 8; q4++)
-                            dst[q4] = make_float4(__uint_as_float(orr[4 * q4]) * inv,
-                                                  __uint_as_float(orr[4 * q4 + 1]) * inv,
-                                                  __uint_as_float(orr[4 * q4 + 2]) * inv,
-                                                  __uint_as_float(orr[4 * q4 + 3]) * inv);
-                    } else {
-                        uint4* dst = reinterpret_cast<uint4*>(P.out_bf16 + o);
+                    for (int c4 = 0; c4 < 8; c4++)
+                        *reinterpret_cast<float4*>(stg + lane * 128 + ((c4 ^ (lane & 7)) << 4)) =
+                            make_float4(__uint_as_float(orr[4 * c4]) * inv, __uint_as_float(orr[4 * c4 + 1]) * inv,
+                                        __uint_as_float(orr[4 * c4 + 2]) * inv,
+                                        __uint_as_float(orr[4 * c4 + 3]) * inv);
+                    __syncwarp();
 #pragma unroll
-                        for (int q8 = 0; q8 < 4; q8++) {
-                            uint32_t w[4];
+                    for (int k = 0; k < 8; k++) {
+                        const int rr = 4 * k + (lane >> 3), c4 = lane & 7;
+                        const float4 v =
+                            *reinterpret_cast<const float4*>(stg + rr * 128 + ((c4 ^ (rr & 7)) << 4));
+                        if (srow0 + rr < P.n_tok)
+                            *reinterpret_cast<float4*>(P.out_f32 + ((size_t)(srow0 + rr) * P.hq_total + h) * HD +
+                                                       q * 32 + c4 * 4) = v;
+                    }
+                } else {
+                    // row: 32 bf16 = 4 chunks of 16 B
 #pragma unroll
-                            for (int e = 0; e < 4; e++) {
-                                __nv_bfloat162 b2 = __floats2bfloat162_rn(
-                                    __uint_as_float(orr[8 * q8 + 2 * e]) * inv,
-                                    __uint_as_float(orr[8 * q8 + 2 * e + 1]) * inv);
-                                w[e] = *reinterpret_cast<uint32_t*>(&b2);
-                            }
-                            dst[q8] = make_uint4(w[0], w[1], w[2], w[3]);
+                    for (int c8 = 0; c8 < 4; c8++) {
+                        uint32_t w[4];
+#pragma unroll
+                        for (int e = 0; e < 4; e++) {
+                            __nv_bfloat162 b2 = __floats2bfloat162_rn(__uint_as_float(orr[8 * c8 + 2 * e]) * inv,
+                                                                      __uint_as_float(orr[8 * c8 + 2 * e + 1]) * inv);
+                            w[e] = *reinterpret_cast<uint32_t*>(&b2);
                         }
+                        *reinterpret_cast<uint4*>(stg + lane * 128 + ((c8 ^ (lane & 7)) << 4)) =
+                            make_uint4(w[0], w[1], w[2], w[3]);
+                    }
+                    __syncwarp();
+#pragma unroll
+                    for (int k = 0; k < 4; k++) {
+                        const int rr = 8 * k + (lane >> 2), c8 = lane & 3;
+                        const uint4 v = *reinterpret_cast<const uint4*>(stg + rr * 128 + ((c8 ^ (rr & 7)) << 4));
+                        if (srow0 + rr < P.n_tok)
+                            *reinterpret_cast<uint4*>(P.out_bf16 + ((size_t)(srow0 + rr) * P.hq_total + h) * HD +
+                                                      q * 32 + c8 * 8) = v;
                     }
                 }
+                __syncwarp();  // the staging buffer is rewritten by the next chunk
             }
-            // the next item's first PFULL arrive (after this code in program
+            // the next item's first P arrive (after this code in program
             // order, behind wait::ld and a before_thread_sync fence) is what
             // lets the issuer overwrite O
             tc_fence_before();
