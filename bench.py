@@ -42,6 +42,9 @@ L_CTX = 8192
 POS = L_CTX - 1
 METRIC = "decode attn µs/layer + HBM GB/s (KV 8K); prefill attn TFLOP/s (2K tok)"
 PREFILL_S = 2048
+LONG_L = 131072          # configs[3]: sequence-sharded long-context decode
+RAGGED_B = 64            # configs[4]: ragged batch, KV lengths U[512, 32768]
+RAGGED_LO, RAGGED_HI = 512, 32768
 
 
 def algo_bytes_per_layer(esize: int) -> int:
@@ -161,7 +164,8 @@ def barrier(world):
 # ------------------------------------------------------------------ our arm
 def fill_cache(ctx, torch, dev, seed, n_layers, pos, stream):
     """Layer l: k_t, v_t ~ N(0,1) (streams l*16+1, l*16+2), k normed and
-    rotated at t by the library's own append kernel, rows 0..pos-1."""
+    rotated at t by the library's own append kernel, rows 0..pos-1 (full
+    rows of all 8 KV heads; a KV-head-sharded context keeps its own)."""
     import q3attn
     kraw = torch.empty(pos * KV_DIM, device=dev)
     vraw = torch.empty(pos * KV_DIM, device=dev)
@@ -249,16 +253,22 @@ def decode_run(args, torch, dev, local, kv_dtype, seed, world, with_e2e, with_cp
     return res
 
 
-def prefill_run(args, torch, dev, local, seed, world):
+def prefill_run(args, torch, dev, local, seed, world, rank=0):
     """causal prefill of S=2048 prompt rows per layer, 36 layers,
     bf16 Q/K/V (post QK-norm + RoPE), fp32 softmax and accumulation, bf16
     output.  One step = 36 launches of q3a_prefill_attn (the attention of
-    each layer over its cache), timed as one CUDA graph between two events."""
+    each layer over its cache), timed as one CUDA graph between two events.
+    With N > 1 ranks each rank holds 8/N KV heads (and their query heads) and
+    one NCCL all-gather of the output head slices per layer rebuilds the
+    output on every rank (strong scaling)."""
     import q3attn
+    import shard
     S = PREFILL_S
+    h0, nh = shard.kv_heads(HKV, world, rank)
     stream = torch.cuda.Stream(device=dev)
     ctx = q3attn.Context(n_layers=N_LAYERS, max_seq=S, kv_dtype=q3attn.KV_BF16,
-                         ptr_mode=q3attn.PTR_DEVICE, device=local)
+                         ptr_mode=q3attn.PTR_DEVICE, device=local, kv_head_begin=h0,
+                         kv_head_count=nh)
     ctx.set_stream(stream.cuda_stream)
     fill_cache(ctx, torch, dev, seed, N_LAYERS, S, stream)
     qf = torch.empty(S * HQ * HD, device=dev)
@@ -271,10 +281,14 @@ def prefill_run(args, torch, dev, local, seed, world):
         qs.append(qf.to(torch.bfloat16).view(S, HQ * HD).contiguous())
     out = torch.empty(N_LAYERS, S, HQ * HD, dtype=torch.bfloat16, device=dev)
     stream.synchronize()
+    gather = shard.HeadSliceGather(torch, world=world, rank=rank, rows=S, device=dev,
+                                   dtype=torch.bfloat16) if world > 1 else None
 
     def step():
         for l in range(N_LAYERS):
             ctx.prefill_attn(out[l], q3attn.OUT_BF16, qs[l], 0, l, 0, S)
+            if gather is not None:
+                gather(out[l])
 
     with torch.cuda.stream(stream):
         for _ in range(args.warmup):
@@ -307,6 +321,140 @@ def prefill_run(args, torch, dev, local, seed, world):
     ctx.close()
     return {"t_ms": t_ms, "launches": launches, "kernel_us": 1000.0 * t_ms / launches,
             "clocks": cs.report(), "steps": K}
+
+
+def time_graph(torch, dev, local, stream, step, K, world):
+    """K steps captured as one CUDA graph between two events on `stream`
+    (collectives included), replayed once untimed and once timed."""
+    e0 = torch.cuda.Event(enable_timing=True, external=True)
+    e1 = torch.cuda.Event(enable_timing=True, external=True)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        e0.record(stream)
+        for _ in range(K):
+            step()
+        e1.record(stream)
+    with torch.cuda.stream(stream):
+        g.replay()
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    with ClockSampler(local) as cs:
+        with torch.cuda.stream(stream):
+            g.replay()
+        torch.cuda.synchronize(dev)
+    barrier(world)
+    t_ms = e0.elapsed_time(e1)
+    del g
+    return t_ms, cs.report()
+
+
+def long_ctx_run(args, torch, dev, local, world, rank):
+    """one new token attending to a 131072-token bf16 cache, 36
+    layers, the sequence split into contiguous chunks over the ranks.  Per
+    layer: q3a_attn_partial over the local chunk into a packed (o, lse) row,
+    one NCCL all-gather (N > 1), q3a_lse_combine_packed into xb on every
+    rank.  Strong scaling: the total work is fixed as N grows."""
+    import q3attn
+    import shard
+    t0, t1 = shard.seq_chunk(LONG_L, world, rank)
+    n_loc = t1 - t0
+    stream = torch.cuda.Stream(device=dev)
+    ctx = q3attn.Context(n_layers=N_LAYERS, max_seq=n_loc, kv_dtype=q3attn.KV_BF16,
+                         ptr_mode=q3attn.PTR_DEVICE, device=local)
+    ctx.set_stream(stream.cuda_stream)
+    # each rank's chunk from its own streams; q is the same on every rank
+    fill_cache(ctx, torch, dev, 4242 + 7919 * rank, N_LAYERS, n_loc, stream)
+    q = torch.empty(N_LAYERS, HQ * HD, device=dev)
+    for l in range(N_LAYERS):
+        ctx.randn(q[l], q3attn.OUT_F32, HQ * HD, 4242, l * 16 + 3)
+    xb = torch.zeros(N_LAYERS, HQ * HD, device=dev)
+    stream.synchronize()
+    dec = shard.SeqShardDecode(torch, ctx, world=world, rank=rank, device=dev)
+
+    def step():
+        for l in range(N_LAYERS):
+            dec(xb[l], q[l], 0, l, n_loc)
+
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            step()
+    stream.synchronize()
+    ctx.check_device_error()
+    K = max(2, args.steps // 10)
+    n0 = ctx.launch_count()
+    t_ms, clocks = time_graph(torch, dev, local, stream, step, K, world)
+    launches = (ctx.launch_count() - n0)
+    ctx.check_device_error()
+    ctx.close()
+    return {"t_ms": t_ms, "steps": K, "clocks": clocks, "launches": launches,
+            "rows_local": n_loc}
+
+
+def ragged_lengths():
+    """configs[4] KV lengths: 64 draws from U[512, 32768] (numpy PCG64, seed
+    2024); sequence b attends rows 0..L_b-1, the last being its new token."""
+    import numpy as np
+    return np.random.default_rng(2024).integers(RAGGED_LO, RAGGED_HI + 1, size=RAGGED_B)
+
+
+def ragged_run(args, torch, dev, local, world, rank):
+    """64 sequences, one new token each, bf16 caches, one fused
+    batched launch (QK-norm, RoPE, append, attention) per step; rank r holds
+    KV heads kv_heads(8, N, r) of every sequence, writes its query heads'
+    columns of xb, and one NCCL all-gather of the slices rebuilds xb."""
+    import q3attn
+    import shard
+    lens = ragged_lengths()
+    h0, nh = shard.kv_heads(HKV, world, rank)
+    stream = torch.cuda.Stream(device=dev)
+    ctx = q3attn.Context(n_layers=1, max_seq=RAGGED_HI, n_seqs=RAGGED_B,
+                         kv_dtype=q3attn.KV_BF16, ptr_mode=q3attn.PTR_DEVICE, device=local,
+                         kv_head_begin=h0, kv_head_count=nh)
+    ctx.set_stream(stream.cuda_stream)
+    ones = torch.ones(HD, device=dev)
+    kraw = torch.empty(RAGGED_HI * KV_DIM, device=dev)
+    vraw = torch.empty(RAGGED_HI * KV_DIM, device=dev)
+    for b, L in enumerate(lens):
+        n = int(L) - 1
+        # full rows of every sequence on every rank; each keeps its heads
+        ctx.randn(kraw, q3attn.OUT_F32, n * KV_DIM, 5151, 1000 + 2 * b)
+        ctx.randn(vraw, q3attn.OUT_F32, n * KV_DIM, 5151, 1001 + 2 * b)
+        ctx.kv_append(b, 0, 0, n, kraw, vraw, ones)
+    del kraw, vraw
+    q = torch.empty(RAGGED_B, HQ * HD, device=dev)
+    k = torch.empty(RAGGED_B, KV_DIM, device=dev)
+    v = torch.empty(RAGGED_B, KV_DIM, device=dev)
+    ctx.randn(q, q3attn.OUT_F32, q.numel(), 5151, 3)
+    ctx.randn(k, q3attn.OUT_F32, k.numel(), 5151, 4)
+    ctx.randn(v, q3attn.OUT_F32, v.numel(), 5151, 5)
+    xb = torch.zeros(RAGGED_B, HQ * HD, device=dev)
+    stream.synchronize()
+    seq_ids = list(range(RAGGED_B))
+    pos = [int(L) - 1 for L in lens]
+    gather = shard.HeadSliceGather(torch, world=world, rank=rank, rows=RAGGED_B,
+                                   device=dev) if world > 1 else None
+
+    def step():
+        ctx.attn_layer_batched(xb, q, k, v, ones, ones, 0, seq_ids, pos)
+        if gather is not None:
+            gather(xb)
+
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            step()
+    stream.synchronize()
+    ctx.check_device_error()
+    K = max(3, args.steps // 5)
+    n0 = ctx.launch_count()
+    t_ms, clocks = time_graph(torch, dev, local, stream, step, K, world)
+    launches = ctx.launch_count() - n0
+    ctx.check_device_error()
+    ctx.close()
+    # all ranks together read every row of K and V once (the new row is
+    # written, then read from shared memory)
+    total_bytes = int(sum(2 * (int(L) - 1) * KV_DIM * 2 + 2 * KV_DIM * 2 for L in lens))
+    return {"t_ms": t_ms, "steps": K, "clocks": clocks, "launches": launches,
+            "bytes_per_step": total_bytes, "mean_len": float(lens.mean())}
 
 
 def e2e_run(args, torch, dev, local, kv_dtype, seed, q_raw, k_raw, v_in, dctx, stream):
@@ -571,11 +719,13 @@ def main():
                         "gpu_launches": b["launches"]}
         line["gpu_launches"] += b["launches"]
     if not args.no_variants:
-        pr = prefill_run(args, torch, dev, local, seed, world)
+        pr = prefill_run(args, torch, dev, local, seed, world, rank)
         t_p = max_over_ranks(pr["t_ms"], world, dev)
         fl = prefill_flops()
+        # each launch is one layer (N = 1) or one rank's 8/N KV heads of a
+        # layer (N > 1): the job computes launches layers in t_p
         us_l = t_p * 1000.0 / pr["launches"]
-        tf = world * fl * pr["launches"] / (t_p / 1000.0) / 1e12
+        tf = fl * pr["launches"] / (t_p / 1000.0) / 1e12
         line["prefill"] = {"metric": "prefill attn TFLOP/s (2K tok)", "value": tf,
                            "unit": "TFLOP/s", "us_per_layer": us_l,
                            "flops_per_layer": fl, "steps": pr["steps"],
@@ -589,8 +739,45 @@ def main():
                                         "traffic": profile_traffic("prefill_2k")},
                            "workload": "configs[2]: causal prefill S=2048, Hq=32, Hkv=8, "
                                        "d=128, bf16 Q/K/V, bf16 out, 36 layers per step",
+                           "parallelism": f"kvhead{world}" if world > 1 else "single",
+                           "scaling": "strong",
                            "clocks": pr["clocks"], "gpu_launches": pr["launches"]}
         line["gpu_launches"] += pr["launches"]
+    if not args.no_variants:
+        lc = long_ctx_run(args, torch, dev, local, world, rank)
+        t_l = max_over_ranks(lc["t_ms"], world, dev)
+        bpl_l = 2 * LONG_L * KV_DIM * 2
+        n_lay = lc["steps"] * N_LAYERS
+        us_l = t_l * 1000.0 / n_lay
+        line["long_ctx"] = {"metric": "decode attn µs/layer (KV 128K, sequence-sharded)",
+                            "value": bpl_l * n_lay / (t_l / 1000.0) / 1e9, "unit": "GB/s",
+                            "us_per_layer": us_l, "n_gpus": world, "scaling": "strong",
+                            "parallelism": f"seq{world}" if world > 1 else "single",
+                            "workload": "configs[3]: KV 131072 bf16, batch 1, Hq=32, Hkv=8, "
+                                        "d=128, 36 layers per step; per layer q3a_attn_partial "
+                                        "over the local chunk, one NCCL all-gather of the "
+                                        "packed (o, lse) rows, q3a_lse_combine_packed",
+                            "bytes_per_layer": bpl_l, "rows_per_gpu": lc["rows_local"],
+                            "hbm_frac_per_gpu": bpl_l / world / (us_l * 1e-6) / 1e9 / hbm_peak,
+                            "clocks": lc["clocks"], "gpu_launches": lc["launches"]}
+        line["gpu_launches"] += lc["launches"]
+        rg = ragged_run(args, torch, dev, local, world, rank)
+        t_r = max_over_ranks(rg["t_ms"], world, dev)
+        us_s = t_r * 1000.0 / rg["steps"]
+        line["ragged_batch"] = {"metric": "batched ragged decode attn µs/step (64 seqs)",
+                                "value": rg["bytes_per_step"] * rg["steps"] / (t_r / 1000.0) / 1e9,
+                                "unit": "GB/s", "us_per_step": us_s, "n_gpus": world,
+                                "scaling": "strong",
+                                "parallelism": f"kvhead{world}" if world > 1 else "single",
+                                "workload": "configs[4]: 64 sequences, KV lengths U[512, 32768] "
+                                            f"(mean {rg['mean_len']:.0f}), bf16, one fused "
+                                            "q3a_attn_layer_batched launch per step + NCCL "
+                                            "all-gather of the xb head slices",
+                                "bytes_per_step": rg["bytes_per_step"],
+                                "hbm_frac_per_gpu": rg["bytes_per_step"] / world / (us_s * 1e-6)
+                                / 1e9 / hbm_peak,
+                                "clocks": rg["clocks"], "gpu_launches": rg["launches"]}
+        line["gpu_launches"] += rg["launches"]
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = cpu_reference_sample(n_calls_max=400, budget_s=15.0)
         line["cpu_baseline"] = {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")}

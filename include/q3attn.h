@@ -196,6 +196,13 @@ int q3a_attn_partial(q3a_ctx *ctx, float *o, float *lse, const float *q, int seq
 int q3a_lse_combine(q3a_ctx *ctx, float *xb, const float *o_parts,
                     const float *lse_parts, int n_parts);
 
+/* Sequence-sharded decode, step 2 in the layout one all-gather produces:
+ * parts [n_parts][n_heads*hd + n_heads], part j = rank j's o followed by its
+ * lse (what q3a_attn_partial writes when given o = part, lse = part +
+ * n_heads*hd).  Same merge as q3a_lse_combine; the reference has no
+ * multi-GPU path, so this replaces nothing in it. */
+int q3a_lse_combine_packed(q3a_ctx *ctx, float *xb, const float *parts, int n_parts);
+
 /* Seeded N(0,1) fill of n elements (fp32 or bf16 by out_dtype): element i is
  * the Box-Muller transform of uniforms u(2j), u(2j+1), j = (offset+i)/2, with
  * u from a splitmix64-hashed counter passed through the xorshift64* output

@@ -716,7 +716,7 @@ extern "C" int q3a_lse_combine(q3a_ctx* c, float* xb, const float* o_parts, cons
     const int nh = c->cfg.n_heads;
     const size_t qd = (size_t)nh * HD;
     if (c->cfg.ptr_mode == Q3A_PTR_DEVICE) {
-        CUDA_TRY(launch_lse_combine(xb, o_parts, lse_parts, n_parts, nh, c->stream));
+        CUDA_TRY(launch_lse_combine(xb, o_parts, qd, lse_parts, nh, n_parts, nh, c->stream));
         c->launches++;
         return Q3A_OK;
     }
@@ -726,7 +726,31 @@ extern "C" int q3a_lse_combine(q3a_ctx* c, float* xb, const float* o_parts, cons
     float *d_o = s, *d_l = s + (size_t)n_parts * qd, *d_x = d_l + (size_t)n_parts * nh;
     CUDA_TRY(cudaMemcpyAsync(d_o, o_parts, (size_t)n_parts * qd * 4, cudaMemcpyHostToDevice, c->stream));
     CUDA_TRY(cudaMemcpyAsync(d_l, lse_parts, (size_t)n_parts * nh * 4, cudaMemcpyHostToDevice, c->stream));
-    CUDA_TRY(launch_lse_combine(d_x, d_o, d_l, n_parts, nh, c->stream));
+    CUDA_TRY(launch_lse_combine(d_x, d_o, qd, d_l, nh, n_parts, nh, c->stream));
+    c->launches++;
+    CUDA_TRY(cudaMemcpyAsync(xb, d_x, qd * 4, cudaMemcpyDeviceToHost, c->stream));
+    CUDA_TRY(cudaStreamSynchronize(c->stream));
+    return Q3A_OK;
+}
+
+extern "C" int q3a_lse_combine_packed(q3a_ctx* c, float* xb, const float* parts, int n_parts) {
+    g_err[0] = 0;
+    if (!c || !xb || !parts || n_parts <= 0) return fail(Q3A_ERR_INVALID, "bad argument");
+    int rc = ensure_device(c);
+    if (rc) return rc;
+    const int nh = c->cfg.n_heads;
+    const size_t qd = (size_t)nh * HD, pw = qd + nh;
+    if (c->cfg.ptr_mode == Q3A_PTR_DEVICE) {
+        CUDA_TRY(launch_lse_combine(xb, parts, pw, parts + qd, pw, n_parts, nh, c->stream));
+        c->launches++;
+        return Q3A_OK;
+    }
+    rc = grow_scratch(c, ((size_t)n_parts * pw + qd) * 4);
+    if (rc) return rc;
+    float* s = reinterpret_cast<float*>(c->d_scratch);
+    float *d_p = s, *d_x = s + (size_t)n_parts * pw;
+    CUDA_TRY(cudaMemcpyAsync(d_p, parts, (size_t)n_parts * pw * 4, cudaMemcpyHostToDevice, c->stream));
+    CUDA_TRY(launch_lse_combine(d_x, d_p, pw, d_p + qd, pw, n_parts, nh, c->stream));
     c->launches++;
     CUDA_TRY(cudaMemcpyAsync(xb, d_x, qd * 4, cudaMemcpyDeviceToHost, c->stream));
     CUDA_TRY(cudaStreamSynchronize(c->stream));

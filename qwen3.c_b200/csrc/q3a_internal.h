@@ -132,8 +132,9 @@ cudaError_t launch_kv_read(const AppendParams& p, float* k_out, float* v_out, cu
 cudaError_t launch_prep_rows(const PrepParams& p, cudaStream_t st);
 cudaError_t launch_randn(void* dst, int out_bf16, size_t n, uint64_t key, uint64_t offset,
                          cudaStream_t st);
-cudaError_t launch_lse_combine(float* xb, const float* o_parts, const float* lse_parts,
-                               int n_parts, int n_heads, cudaStream_t st);
+cudaError_t launch_lse_combine(float* xb, const float* o_parts, size_t o_stride,
+                               const float* lse_parts, size_t lse_stride, int n_parts, int n_heads,
+                               cudaStream_t st);
 
 struct PrefillParams {
     float* out_f32;

@@ -151,18 +151,22 @@ __global__ void randn_kernel(void* dst, int out_bf16, size_t n, uint64_t key, ui
 
 // ---------------------------------------------------------------- combine
 // One block per head: xb[h] = sum_j 2^(lse_j - M) o_j[h] / sum_j 2^(lse_j - M).
+// Part j's output o_j [n_heads][128] starts at o_parts + j * o_stride and its
+// log2-sum-exp lse_j [n_heads] at lse_parts + j * lse_stride (dense arrays:
+// strides n_heads*128 and n_heads; the one-buffer layout of an all-gather:
+// both n_heads*129, lse_parts = o_parts + n_heads*128).
 __global__ void lse_combine_kernel(float* __restrict__ xb, const float* __restrict__ o_parts,
-                                   const float* __restrict__ lse_parts, int n_parts,
-                                   int n_heads) {
+                                   size_t o_stride, const float* __restrict__ lse_parts,
+                                   size_t lse_stride, int n_parts, int n_heads) {
     const int h = blockIdx.x, d = threadIdx.x;
     float M = -INFINITY;
-    for (int j = 0; j < n_parts; j++) M = fmaxf(M, lse_parts[(size_t)j * n_heads + h]);
+    for (int j = 0; j < n_parts; j++) M = fmaxf(M, lse_parts[(size_t)j * lse_stride + h]);
     float W = 0.0f, acc = 0.0f;
     for (int j = 0; j < n_parts; j++) {
-        const float l = lse_parts[(size_t)j * n_heads + h];
+        const float l = lse_parts[(size_t)j * lse_stride + h];
         const float w = (l == -INFINITY) ? 0.0f : exp2f(l - M);
         W += w;
-        acc = fmaf(w, o_parts[((size_t)j * n_heads + h) * HD + d], acc);
+        acc = fmaf(w, o_parts[(size_t)j * o_stride + (size_t)h * HD + d], acc);
     }
     xb[(size_t)h * HD + d] = acc / W;
 }
@@ -206,9 +210,11 @@ cudaError_t launch_randn(void* dst, int out_bf16, size_t n, uint64_t key, uint64
     return cudaGetLastError();
 }
 
-cudaError_t launch_lse_combine(float* xb, const float* o_parts, const float* lse_parts,
-                               int n_parts, int n_heads, cudaStream_t st) {
-    lse_combine_kernel<<<n_heads, HD, 0, st>>>(xb, o_parts, lse_parts, n_parts, n_heads);
+cudaError_t launch_lse_combine(float* xb, const float* o_parts, size_t o_stride,
+                               const float* lse_parts, size_t lse_stride, int n_parts, int n_heads,
+                               cudaStream_t st) {
+    lse_combine_kernel<<<n_heads, HD, 0, st>>>(xb, o_parts, o_stride, lse_parts, lse_stride, n_parts,
+                                               n_heads);
     return cudaGetLastError();
 }
 

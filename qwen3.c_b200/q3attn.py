@@ -23,7 +23,8 @@ EXPORTS = [
     "q3a_cfg_default", "q3a_create", "q3a_destroy", "q3a_last_error", "q3a_set_stream",
     "q3a_sync", "q3a_check_device_error", "q3a_attn_layer", "q3a_attn_decode",
     "q3a_attn_layer_batched", "q3a_kv_append", "q3a_kv_load", "q3a_kv_read", "q3a_prefill",
-    "q3a_prefill_attn", "q3a_attn_partial", "q3a_lse_combine", "q3a_randn",
+    "q3a_prefill_attn", "q3a_attn_partial", "q3a_lse_combine", "q3a_lse_combine_packed",
+    "q3a_randn",
     "q3a_launch_count", "q3a_attn_decode_noalloc",
 ]
 
@@ -75,6 +76,7 @@ def load():
         L.q3a_prefill_attn.argtypes = [_P, _P, _I, _P, _I, _I, _I, _I]
         L.q3a_attn_partial.argtypes = [_P, _P, _P, _P, _I, _I, _I, _I]
         L.q3a_lse_combine.argtypes = [_P, _P, _P, _P, _I]
+        L.q3a_lse_combine_packed.argtypes = [_P, _P, _P, _I]
         L.q3a_randn.argtypes = [_P, _P, _I, _SZ, _U64, _U64, _U64]
         L.q3a_attn_decode_noalloc.argtypes = [_P, _P, _P, _P, _SZ, _I, _I, _I, _I, _I, _I, _P]
         L.q3a_launch_count.argtypes = [_P]
@@ -191,6 +193,9 @@ class Context:
 
     def lse_combine(self, xb, o_parts, lse_parts, n_parts):
         check(self.lib.q3a_lse_combine(self.h, ptr(xb), ptr(o_parts), ptr(lse_parts), n_parts))
+
+    def lse_combine_packed(self, xb, parts, n_parts):
+        check(self.lib.q3a_lse_combine_packed(self.h, ptr(xb), ptr(parts), n_parts))
 
     def randn(self, dst, out_dtype, n, seed, stream_id, offset=0):
         check(self.lib.q3a_randn(self.h, ptr(dst), out_dtype, n, seed, stream_id, offset))
