@@ -171,7 +171,10 @@ int q3a_kv_read(q3a_ctx *ctx, int seq, int layer, int pos0, int n, float *k, flo
  * q [n_tok][n_heads*hd] raw (left unmodified), k, v [n_tok][n_kv*hd] raw; out
  * [n_tok][n_heads*hd] in out_dtype (Q3A_OUT_F32 / Q3A_OUT_BF16).  Requires a
  * bf16 cache (the tensor-core operands are bf16, softmax and accumulation
- * fp32). */
+ * fp32).  A context created with kv_head_begin/kv_head_count (KV-head
+ * sharding) takes the same full-width q, k, v rows, keeps its own KV heads
+ * and writes only its query heads' columns of out; the other columns are
+ * left as the caller had them. */
 int q3a_prefill(q3a_ctx *ctx, void *out, int out_dtype, const float *q, const float *k,
                 const float *v, const float *q_norm_w, const float *k_norm_w, int seq,
                 int layer, int pos0, int n_tok);

@@ -872,8 +872,6 @@ extern "C" int q3a_prefill(q3a_ctx* c, void* out, int out_dtype, const float* q,
     g_err[0] = 0;
     if (!c || !out || !q || !k || !v || !qw || !kw) return fail(Q3A_ERR_INVALID, "null argument");
     if (!c->bf16) return fail(Q3A_ERR_UNSUPPORTED, "prefill needs a bf16 cache");
-    if (c->nkv != c->cfg.n_kv_heads)
-        return fail(Q3A_ERR_INVALID, "q3a_prefill needs a context holding all KV heads");
     if (n_tok <= 0) return fail(Q3A_ERR_INVALID, "n_tok %d", n_tok);
     int rc = ensure_device(c);
     if (rc) return rc;
@@ -902,6 +900,8 @@ extern "C" int q3a_prefill(q3a_ctx* c, void* out, int out_dtype, const float* q,
         CUDA_TRY(cudaMemcpyAsync(fv, v, kd * 4, cudaMemcpyHostToDevice, c->stream));
         CUDA_TRY(cudaMemcpyAsync(fqw, qw, HD * 4, cudaMemcpyHostToDevice, c->stream));
         CUDA_TRY(cudaMemcpyAsync(fkw, kw, HD * 4, cudaMemcpyHostToDevice, c->stream));
+        if (c->nkv != c->cfg.n_kv_heads)  // sharded: keep the caller's other heads' columns
+            CUDA_TRY(cudaMemcpyAsync(fo, out, out_bytes, cudaMemcpyHostToDevice, c->stream));
         dq = fq; dk = fk; dv = fv; dqw = fqw; dkw = fkw; dout = fo;
     }
     PrepParams pp;
@@ -911,8 +911,8 @@ extern "C" int q3a_prefill(q3a_ctx* c, void* out, int out_dtype, const float* q,
     pp.w = dqw;
     pp.eps = c->cfg.norm_eps;
     pp.n = n_tok;
-    pp.nheads = c->cfg.n_heads;
-    pp.head0 = 0;
+    pp.nheads = c->nkv * GQA;  // this context's query heads
+    pp.head0 = c->kv0 * GQA;
     pp.nheads_total = c->cfg.n_heads;
     pp.pos0 = pos0;
     pp.do_norm_rope = 1;
@@ -944,8 +944,6 @@ extern "C" int q3a_prefill_attn(q3a_ctx* c, void* out, int out_dtype, const void
     if (!c->bf16) return fail(Q3A_ERR_UNSUPPORTED, "prefill needs a bf16 cache");
     if (out_dtype != Q3A_OUT_F32 && out_dtype != Q3A_OUT_BF16)
         return fail(Q3A_ERR_INVALID, "out_dtype %d", out_dtype);
-    if (c->nkv != c->cfg.n_kv_heads)
-        return fail(Q3A_ERR_INVALID, "q3a_prefill_attn needs a context holding all KV heads");
     if (seq < 0 || seq >= c->cfg.n_seqs) return fail(Q3A_ERR_INVALID, "seq %d", seq);
     if (layer < 0 || layer >= c->cfg.n_layers) return fail(Q3A_ERR_INVALID, "layer %d", layer);
     if (n_tok <= 0 || pos0 < 0 || (long long)pos0 + n_tok > c->cfg.max_seq)
@@ -963,6 +961,8 @@ extern "C" int q3a_prefill_attn(q3a_ctx* c, void* out, int out_dtype, const void
         CUDA_TRY(cudaMemcpyAsync(s, q_bf16, qd * 2, cudaMemcpyHostToDevice, c->stream));
         dq = s;
         dout = s + ((qd * 2 + 255) & ~(size_t)255);
+        if (c->nkv != c->cfg.n_kv_heads)  // sharded: keep the caller's other heads' columns
+            CUDA_TRY(cudaMemcpyAsync(dout, out, out_bytes, cudaMemcpyHostToDevice, c->stream));
     }
     // Q [n_tok][n_heads][128] bf16: 3-D map (d, head, row), box 64 x 1 x 128,
     // 128-byte swizzle -- one head's 128 rows x 64 dims per load

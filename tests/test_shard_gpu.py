@@ -140,6 +140,32 @@ def test_kv_head_shards_batched_ragged(bf16, world):
         check_close(xb[i], refs[i], bf16, f"seq {i} len {lens[i]}, {world} head shards")
 
 
+@pytest.mark.parametrize("world", [2, 4])
+def test_kv_head_shards_prefill(world):
+    """q3a_prefill on KV-head-sharded contexts: each writes its query heads'
+    columns (host mode keeps the rest); together they equal the oracle."""
+    S = 200
+    seed = 61
+    qraw = orc.randn(S * HQ * HD, seed, 3)
+    kc, vc, kraw, vraw = orc.make_cache(seed, 0, S, HKV, HD, S, bf16=True)
+    qw = np.ones(HD, np.float32)
+    q = qraw.copy()
+    for s_ in range(S):
+        row = q[s_ * HQ * HD:(s_ + 1) * HQ * HD]
+        orc.rmsnorm_head(row, qw, HQ, HD, EPS)
+        orc.rope(row, HQ, HD, s_, THETA)
+    ref = orc.prefill_causal(orc.bf16_round(q), kc, vc, 0, S, HQ, KV_MUL, HD, KV_DIM, S)
+    out = np.full((S, HQ * HD), np.nan, np.float32)
+    for r in range(world):
+        h0, nh = shard.kv_heads(HKV, world, r)
+        with q3attn.Context(n_layers=1, max_seq=S, kv_dtype=q3attn.KV_BF16,
+                            kv_head_begin=h0, kv_head_count=nh) as ctx:
+            ctx.prefill(out, q3attn.OUT_F32, qraw, kraw, vraw, qw, qw, 0, 0, 0, S)
+    assert np.all(np.isfinite(out))
+    err = float(np.abs(np.float64(out.reshape(-1)) - ref).max())
+    assert err <= TOL_BF16_ABS, f"{world} head shards: max-abs {err}"
+
+
 def _free_port():
     s = socket.socket()
     s.bind(("127.0.0.1", 0))
@@ -148,63 +174,20 @@ def _free_port():
     return port
 
 
-def _nccl_worker(rank, world, port, out_q):
-    try:
-        for p in (os.path.join(ROOT, "oracle"), os.path.join(ROOT, "qwen3.c_b200"),
-                  os.path.join(ROOT, "tests")):
-            sys.path.insert(0, p)
-        import datetime
-        import torch
-        import torch.distributed as dist
-        import q3a_oracle as orc
-        import q3attn
-        import shard
-        os.environ["MASTER_ADDR"] = "127.0.0.1"
-        os.environ["MASTER_PORT"] = str(port)
-        os.environ["NCCL_NVLS_ENABLE"] = "0"
-        dev = torch.device(f"cuda:{rank}")
-        torch.cuda.set_device(dev)
-        dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
-                                timeout=datetime.timedelta(seconds=60))
-        L = 20000
-        kc, vc, _, _ = orc.make_cache(123, 0, L, HKV, HD, L, bf16=True)
-        qv = orc.randn(HQ * HD, 123, 9)
-        t0, t1 = shard.seq_chunk(L, world, rank)
-        with q3attn.Context(n_layers=1, max_seq=t1 - t0, kv_dtype=q3attn.KV_BF16,
-                            ptr_mode=q3attn.PTR_DEVICE, device=rank) as ctx:
-            st = torch.cuda.current_stream(dev)
-            ctx.set_stream(st.cuda_stream)
-            ctx.kv_load(0, 0, 0, t1 - t0, torch.from_numpy(kc[t0 * KV_DIM:t1 * KV_DIM]).to(dev),
-                        torch.from_numpy(vc[t0 * KV_DIM:t1 * KV_DIM]).to(dev))
-            dec = shard.SeqShardDecode(torch, ctx, world=world, rank=rank, device=dev)
-            xb = torch.zeros(HQ * HD, device=dev)
-            dec(xb, torch.from_numpy(qv).to(dev), 0, 0, t1 - t0)
-            torch.cuda.synchronize(dev)
-            ctx.check_device_error()
-            got = xb.cpu().numpy()
-        dist.barrier()
-        dist.destroy_process_group()
-        ref = orc.attn_decode(qv, kc, vc, 0, L - 1, HQ, KV_MUL, HD, KV_DIM, L)
-        out_q.put((rank, float(np.abs(np.float64(got) - ref).max()), None))
-    except Exception as e:  # reported to the parent, which fails the test
-        out_q.put((rank, None, repr(e)))
-
-
-def test_sequence_shards_over_nccl_two_gpus():
+def test_sequence_shards_over_nccl_two_gpus(tmp_path):
+    """Two ranks launched the way bench.py --gpus 2 is (torchrun, one process
+    per GPU, NCCL over NVLink); each checks its combined xb against the
+    oracle and writes the error to a file."""
+    import subprocess
     import torch
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
-    import torch.multiprocessing as mp
-    ctx = mp.get_context("spawn")
-    q = ctx.Queue()
-    port = _free_port()
-    procs = [ctx.Process(target=_nccl_worker, args=(r, 2, port, q)) for r in range(2)]
-    for p in procs:
-        p.start()
-    res = [q.get(timeout=300) for _ in range(2)]
-    for p in procs:
-        p.join(timeout=60)
-    for rank, err, exc in res:
-        assert exc is None, f"rank {rank}: {exc}"
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", SHARD_TEST_OUT=str(tmp_path))
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2",
+           "--master-addr", "127.0.0.1", "--master-port", str(_free_port()),
+           os.path.join(ROOT, "tests", "nccl_seq_shard.py")]
+    r = subprocess.run(cmd, env=env, timeout=240, capture_output=True, text=True)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
+    for rank in range(2):
+        err = float(open(os.path.join(tmp_path, f"rank{rank}.txt")).read())
         assert err <= TOL_BF16_ABS, f"rank {rank}: max-abs {err}"
-
