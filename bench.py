@@ -296,40 +296,29 @@ def prefill_run(args, torch, dev, local, seed, world, rank=0):
     stream.synchronize()
     ctx.check_device_error()
     K = max(1, args.steps // 10)
-    e0 = torch.cuda.Event(enable_timing=True, external=True)
-    e1 = torch.cuda.Event(enable_timing=True, external=True)
-    g = torch.cuda.CUDAGraph()
     n0 = ctx.launch_count()
-    with torch.cuda.graph(g, stream=stream):
-        e0.record(stream)
-        for _ in range(K):
-            step()
-        e1.record(stream)
+    t_ms, clocks = time_graph(torch, dev, local, stream, step, K, world)
     launches = ctx.launch_count() - n0
-    with torch.cuda.stream(stream):
-        g.replay()
-    torch.cuda.synchronize(dev)
-    barrier(world)
-    with ClockSampler(local) as cs:
-        with torch.cuda.stream(stream):
-            g.replay()
-        torch.cuda.synchronize(dev)
-    barrier(world)
     ctx.check_device_error()
-    t_ms = e0.elapsed_time(e1)
-    del g
     ctx.close()
     return {"t_ms": t_ms, "launches": launches, "kernel_us": 1000.0 * t_ms / launches,
-            "clocks": cs.report(), "steps": K}
+            "clocks": clocks, "steps": K}
 
 
 def time_graph(torch, dev, local, stream, step, K, world):
     """K steps captured as one CUDA graph between two events on `stream`
-    (collectives included), replayed once untimed and once timed."""
+    (collectives included), replayed once untimed and once timed.  With
+    N > 1 a small all-reduce sits in the graph before the first event, so
+    every rank's timed region starts once all ranks are there (host launch
+    skew between ranks is not counted)."""
     e0 = torch.cuda.Event(enable_timing=True, external=True)
     e1 = torch.cuda.Event(enable_timing=True, external=True)
+    align = torch.zeros(1, device=dev)
     g = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g, stream=stream):
+        if world > 1:
+            import torch.distributed as dist
+            dist.all_reduce(align)
         e0.record(stream)
         for _ in range(K):
             step()

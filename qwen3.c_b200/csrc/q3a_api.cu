@@ -448,10 +448,26 @@ static int schedule(q3a_ctx* c, DecodeParams& p) {
     }
     p.total_units = acc;
     p.n_pieces = 0;
+    const int n_lin = (int)std::min<long long>(c->num_sms, acc);
     if ((long long)p.nb * p.nkv <= std::min(c->num_sms, MAX_PIECES)) {
         schedule_pieces(c, p);
+        // Piece mode gives every group whole CTAs.  With many groups of
+        // unequal length (ragged batches, few KV heads per context) the
+        // longest ranges can sit far above the even share of the linear
+        // list; then the linear list is used instead.
+        double piece_max = 0.0;
+        for (int i = 0; i < p.n_pieces; i++) {
+            const Piece& pc = p.pieces[i];
+            const double u = (pc.r1 - pc.r0) / (double)DEC_TILE + (p.fused && pc.i == pc.k - 1 ? 1 : 0);
+            piece_max = std::max(piece_max, u);
+        }
+        const double lin_max = std::ceil((double)acc / n_lin) + 1.0;
+        if (piece_max > 1.2 * lin_max) {
+            p.n_pieces = 0;
+            p.n_ctas = n_lin;
+        }
     } else {
-        p.n_ctas = (int)std::min<long long>(c->num_sms, acc);
+        p.n_ctas = n_lin;
     }
     const long long slots = (long long)p.n_ctas + (long long)p.nb * p.nkv;
     if (slots > c->part_slots) return fail(Q3A_ERR_INVALID, "decode scratch too small");
