@@ -340,9 +340,10 @@ def time_graph(torch, dev, local, stream, step, K, world):
 def long_ctx_run(args, torch, dev, local, world, rank):
     """one new token attending to a 131072-token bf16 cache, 36
     layers, the sequence split into contiguous chunks over the ranks.  Per
-    layer: q3a_attn_partial over the local chunk into a packed (o, lse) row,
-    one NCCL all-gather (N > 1), q3a_lse_combine_packed into xb on every
-    rank.  Strong scaling: the total work is fixed as N grows."""
+    layer one launch of q3a_attn_seqshard: split-KV decode of the local
+    chunk, each KV head's (o, lse) stored into every rank's receive buffer
+    over NVLink, merged on every rank once all have arrived.  Strong scaling:
+    the total work is fixed as N grows."""
     import q3attn
     import shard
     t0, t1 = shard.seq_chunk(LONG_L, world, rank)
@@ -358,7 +359,7 @@ def long_ctx_run(args, torch, dev, local, world, rank):
         ctx.randn(q[l], q3attn.OUT_F32, HQ * HD, 4242, l * 16 + 3)
     xb = torch.zeros(N_LAYERS, HQ * HD, device=dev)
     stream.synchronize()
-    dec = shard.SeqShardDecode(torch, ctx, world=world, rank=rank, device=dev)
+    dec = shard.SeqShardDecode(torch, ctx, world=world, rank=rank, device=dev, mode="peer")
 
     def step():
         for l in range(N_LAYERS):
@@ -743,9 +744,10 @@ def main():
                             "us_per_layer": us_l, "n_gpus": world, "scaling": "strong",
                             "parallelism": f"seq{world}" if world > 1 else "single",
                             "workload": "configs[3]: KV 131072 bf16, batch 1, Hq=32, Hkv=8, "
-                                        "d=128, 36 layers per step; per layer q3a_attn_partial "
-                                        "over the local chunk, one NCCL all-gather of the "
-                                        "packed (o, lse) rows, q3a_lse_combine_packed",
+                                        "d=128, 36 layers per step; per layer one "
+                                        "q3a_attn_seqshard launch: split-KV decode of the "
+                                        "local chunk, (o, lse) of each KV head stored into "
+                                        "every rank over NVLink, merged on every rank",
                             "bytes_per_layer": bpl_l, "rows_per_gpu": lc["rows_local"],
                             "hbm_frac_per_gpu": bpl_l / world / (us_l * 1e-6) / 1e9 / hbm_peak,
                             "clocks": lc["clocks"], "gpu_launches": lc["launches"]}

@@ -45,6 +45,9 @@ extern "C" {
 #define Q3A_PTR_HOST 0
 #define Q3A_PTR_DEVICE 1
 
+#define Q3A_MAX_PEERS 8         /* ranks of a peer-memory sequence shard */
+#define Q3A_IPC_HANDLE_BYTES 64 /* bytes of one exported buffer handle */
+
 #define Q3A_OUT_F32 0
 #define Q3A_OUT_BF16 1
 
@@ -205,6 +208,31 @@ int q3a_lse_combine(q3a_ctx *ctx, float *xb, const float *o_parts,
  * n_heads*hd).  Same merge as q3a_lse_combine; the reference has no
  * multi-GPU path, so this replaces nothing in it. */
 int q3a_lse_combine_packed(q3a_ctx *ctx, float *xb, const float *parts, int n_parts);
+
+/* Sequence-sharded decode over peer memory (NVLink), one launch per layer
+ * and no collective library: the alternative to q3a_attn_partial + an
+ * all-gather + q3a_lse_combine_packed.  The reference has no multi-GPU path;
+ * these three calls replace nothing in it.
+ *
+ * Set-up, once per context, in the same order on every rank (one process
+ * per GPU, contexts holding all KV heads, device-pointer mode):
+ *   q3a_peer_export(ctx, world, handle)  allocates this rank's receive
+ *       buffer (two parity halves of world packed (o, lse) rows and their
+ *       flags) and writes its IPC handle (Q3A_IPC_HANDLE_BYTES) to `handle`;
+ *   the caller exchanges the handles (any transport) and calls
+ *   q3a_peer_open(ctx, rank, world, handles)  with all ranks' handles in rank
+ *       order, mapping the peers' buffers.
+ * Per layer: q3a_attn_seqshard(ctx, xb, q, seq, layer, n_local) attends the
+ * prepared q [n_heads*hd] over rows [0, n_local) of this rank's cache; each
+ * KV head's result is stored into every rank's buffer, a flag is raised, and
+ * once every rank's result for that head has arrived (bounded wait, error
+ * Q3A_ERR_TIMEOUT after about a second) the log-sum-exp merge writes that
+ * head group of xb on every rank.  All ranks must make the same sequence of
+ * calls; a rank may run at most one call ahead of another. */
+int q3a_peer_export(q3a_ctx *ctx, int world, void *handle);
+int q3a_peer_open(q3a_ctx *ctx, int rank, int world, const void *handles);
+int q3a_attn_seqshard(q3a_ctx *ctx, float *xb, const float *q, int seq, int layer,
+                      int n_local);
 
 /* Seeded N(0,1) fill of n elements (fp32 or bf16 by out_dtype): element i is
  * the Box-Muller transform of uniforms u(2j), u(2j+1), j = (offset+i)/2, with

@@ -105,6 +105,12 @@ struct q3a_ctx {
     void* d_scratch = nullptr;
     size_t scratch_bytes = 0;
     uint64_t launches = 0;
+    // peer-memory sequence shards (q3a_peer_export / q3a_peer_open)
+    int peer_world = 0;
+    int peer_rank = -1;
+    float* peer_buf = nullptr;            // this rank's receive buffer
+    float* peer_ptrs[PEER_MAX] = {};      // every rank's buffer, mapped here
+    unsigned* peer_epoch = nullptr;       // call counter + finisher ticket
 };
 
 static int ensure_device(const q3a_ctx* c) {
@@ -170,6 +176,10 @@ int q3a::record_error(int code, const char* msg) { return fail(code, "%s", msg);
 static void destroy_ctx(q3a_ctx* c) {
     if (!c) return;
     if (c->stream) cudaStreamSynchronize(c->stream);
+    for (int r = 0; r < PEER_MAX; r++)
+        if (c->peer_ptrs[r] && c->peer_ptrs[r] != c->peer_buf) cudaIpcCloseMemHandle(c->peer_ptrs[r]);
+    cudaFree(c->peer_buf);
+    cudaFree(c->peer_epoch);
     cudaFree(c->kcache);
     cudaFree(c->vcache);
     cudaFree(c->partials);
@@ -747,6 +757,94 @@ extern "C" int q3a_lse_combine(q3a_ctx* c, float* xb, const float* o_parts, cons
     CUDA_TRY(cudaMemcpyAsync(xb, d_x, qd * 4, cudaMemcpyDeviceToHost, c->stream));
     CUDA_TRY(cudaStreamSynchronize(c->stream));
     return Q3A_OK;
+}
+
+// ------------------------------------------------ peer-memory sequence shards
+static size_t peer_row(const q3a_ctx* c) { return (size_t)c->cfg.n_heads * HD + c->cfg.n_heads; }
+
+extern "C" int q3a_peer_export(q3a_ctx* c, int world, void* handle) {
+    g_err[0] = 0;
+    if (!c || !handle) return fail(Q3A_ERR_INVALID, "null argument");
+    if (world < 1 || world > PEER_MAX) return fail(Q3A_ERR_INVALID, "world %d outside [1, %d]", world, PEER_MAX);
+    if (c->nkv != c->cfg.n_kv_heads || c->cfg.n_kv_heads > PEER_MAXG)
+        return fail(Q3A_ERR_INVALID, "peer shards need a context holding all (<= %d) KV heads", PEER_MAXG);
+    if (c->cfg.ptr_mode != Q3A_PTR_DEVICE) return fail(Q3A_ERR_UNSUPPORTED, "peer shards run in device-pointer mode");
+    if (c->peer_world && c->peer_world != world)
+        return fail(Q3A_ERR_INVALID, "already exported for %d ranks", c->peer_world);
+    int rc = ensure_device(c);
+    if (rc) return rc;
+    if (!c->peer_buf) {
+        // [2 parities][world][row] words of 8 bytes (value, call number)
+        const size_t bytes = (size_t)2 * world * peer_row(c) * 8;
+        if (cudaMalloc(&c->peer_buf, bytes) != cudaSuccess) return fail(Q3A_ERR_OOM, "peer buffer of %zu bytes", bytes);
+        if (cudaMalloc(&c->peer_epoch, PEER_MAXG * sizeof(unsigned)) != cudaSuccess)
+            return fail(Q3A_ERR_OOM, "peer counters");
+        CUDA_TRY(cudaMemset(c->peer_buf, 0, bytes));
+        CUDA_TRY(cudaMemset(c->peer_epoch, 0, PEER_MAXG * sizeof(unsigned)));
+        CUDA_TRY(cudaDeviceSynchronize());
+        c->peer_world = world;
+    }
+    cudaIpcMemHandle_t h;
+    CUDA_TRY(cudaIpcGetMemHandle(&h, c->peer_buf));
+    static_assert(sizeof(h) == Q3A_IPC_HANDLE_BYTES, "IPC handle size");
+    memcpy(handle, &h, sizeof(h));
+    return Q3A_OK;
+}
+
+extern "C" int q3a_peer_open(q3a_ctx* c, int rank, int world, const void* handles) {
+    g_err[0] = 0;
+    if (!c || !handles) return fail(Q3A_ERR_INVALID, "null argument");
+    if (!c->peer_buf || world != c->peer_world)
+        return fail(Q3A_ERR_INVALID, "q3a_peer_export(ctx, %d, ...) must come first", world);
+    if (rank < 0 || rank >= world) return fail(Q3A_ERR_INVALID, "rank %d of %d", rank, world);
+    if (c->peer_rank >= 0) return fail(Q3A_ERR_INVALID, "peers already open");
+    int rc = ensure_device(c);
+    if (rc) return rc;
+    const uint8_t* hs = reinterpret_cast<const uint8_t*>(handles);
+    for (int r = 0; r < world; r++) {
+        if (r == rank) {
+            c->peer_ptrs[r] = c->peer_buf;
+            continue;
+        }
+        cudaIpcMemHandle_t h;
+        memcpy(&h, hs + (size_t)r * Q3A_IPC_HANDLE_BYTES, sizeof(h));
+        void* p = nullptr;
+        if (cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+            cudaGetLastError();
+            return fail(Q3A_ERR_CUDA, "cannot map the buffer of rank %d", r);
+        }
+        c->peer_ptrs[r] = reinterpret_cast<float*>(p);
+    }
+    c->peer_rank = rank;
+    return Q3A_OK;
+}
+
+extern "C" int q3a_attn_seqshard(q3a_ctx* c, float* xb, const float* q, int seq, int layer,
+                                 int n_local) {
+    g_err[0] = 0;
+    if (!c || !xb || !q) return fail(Q3A_ERR_INVALID, "null argument");
+    if (c->peer_rank < 0) return fail(Q3A_ERR_INVALID, "q3a_peer_open must come first");
+    if (seq < 0 || seq >= c->cfg.n_seqs) return fail(Q3A_ERR_INVALID, "seq %d", seq);
+    if (layer < 0 || layer >= c->cfg.n_layers) return fail(Q3A_ERR_INVALID, "layer %d", layer);
+    if (n_local < 1 || n_local > c->cfg.max_seq)
+        return fail(Q3A_ERR_INVALID, "local chunk of %d rows outside [1, %d]", n_local, c->cfg.max_seq);
+    int rc = ensure_device(c);
+    if (rc) return rc;
+    DecodeParams p;
+    base_params(c, p, layer);
+    p.nb = 1;
+    p.fused = 0;
+    p.slot[0] = seq;
+    p.t_begin[0] = 0;
+    p.t_end[0] = n_local;
+    p.q = q;
+    p.xb = xb;
+    p.peer_world = c->peer_world;
+    p.peer_rank = c->peer_rank;
+    p.peer_row = (int)peer_row(c);
+    for (int r = 0; r < c->peer_world; r++) p.peer_recv[r] = c->peer_ptrs[r];
+    p.peer_epoch = c->peer_epoch;
+    return run_decode(c, p, c->tmK, c->tmV, c->bf16);
 }
 
 extern "C" int q3a_lse_combine_packed(q3a_ctx* c, float* xb, const float* parts, int n_parts) {

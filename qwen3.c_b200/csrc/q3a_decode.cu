@@ -430,6 +430,33 @@ __device__ __forceinline__ void store4(KV* dst, float4 v) {
     }
 }
 
+// ---- peer-memory exchange words: each 8-byte word carries a 32-bit value
+// and the call number it belongs to, stored and loaded as one naturally
+// aligned 64-bit access, so a reader that sees the call number also sees the
+// value -- no flag and no fence are needed on either side.
+__device__ __forceinline__ void st_word_sys(unsigned long long* p, float v, unsigned ep) {
+    const unsigned long long w = ((unsigned long long)ep << 32) | __float_as_uint(v);
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_word_sys(const unsigned long long* p) {
+    unsigned long long w;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+    return w;
+}
+// Bounded wait for the word of call `ep`; false on timeout.
+__device__ __forceinline__ bool wait_word(const unsigned long long* p, unsigned ep, float& v) {
+    unsigned long long w = ld_word_sys(p);
+    if ((unsigned)(w >> 32) != ep) {
+        const long long t0 = clock64();
+        do {
+            if (clock64() - t0 > WAIT_LIMIT_CYCLES) return false;
+            w = ld_word_sys(p);
+        } while ((unsigned)(w >> 32) != ep);
+    }
+    v = __uint_as_float((unsigned)w);
+    return true;
+}
+
 template <typename KV>
 __global__ void __launch_bounds__(DecCfg<KV>::NTHREADS, 1)
     decode_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
@@ -707,6 +734,70 @@ __global__ void __launch_bounds__(DecCfg<KV>::NTHREADS, 1)
                 lse = Mx + log2f(W);
                 if (tid == 0) P.counters[s.grp] = 0;
             }
+        }
+        if (write_out && P.peer_world > 0) {
+            // Sequence-shard exchange over peer memory.  This CTA holds this
+            // rank's result for KV head kvh.  Every value of it (o of the 4
+            // query heads, their lse) goes as a (value, call) word into row
+            // `rank` of every rank's receive buffer (the half of this call's
+            // parity; a rank is at most one call ahead); then each thread
+            // waits for its own words from every rank and merges them.
+            const int W = P.peer_world, R = P.peer_rank, row = P.peer_row;
+            const int gh = hq0 + h;
+            const unsigned ep = *reinterpret_cast<volatile const unsigned*>(P.peer_epoch + kvh) + 1u;
+            const int par = (int)(ep & 1u);
+            const size_t my_row = ((size_t)par * W + R) * row;
+            for (int r = 0; r < W; r++) {
+                unsigned long long* dst = reinterpret_cast<unsigned long long*>(P.peer_recv[r]) + my_row;
+                st_word_sys(dst + gh * HD + d, o0, ep);
+                st_word_sys(dst + gh * HD + d + 1, o1, ep);
+                if ((tid & 63) == 0) st_word_sys(dst + P.hq_total * HD + gh, lse, ep);
+            }
+            const unsigned long long* src =
+                reinterpret_cast<const unsigned long long*>(P.peer_recv[R]) + (size_t)par * W * row;
+            // loads for four ranks' words at a time are in flight together;
+            // words not there yet are polled (bounded)
+            float lr[PEER_MAX], x0[PEER_MAX], x1[PEER_MAX];
+            bool ok = true;
+            for (int r0 = 0; r0 < W; r0 += 4) {
+                unsigned long long wl[4], w0[4], w1[4];
+#pragma unroll
+                for (int u = 0; u < 4; u++) {
+                    if (r0 + u < W) {
+                        const unsigned long long* sr = src + (size_t)(r0 + u) * row;
+                        wl[u] = ld_word_sys(sr + P.hq_total * HD + gh);
+                        w0[u] = ld_word_sys(sr + gh * HD + d);
+                        w1[u] = ld_word_sys(sr + gh * HD + d + 1);
+                    }
+                }
+#pragma unroll
+                for (int u = 0; u < 4; u++) {
+                    const int r = r0 + u;
+                    if (r < W) {
+                        const unsigned long long* sr = src + (size_t)r * row;
+                        lr[r] = __uint_as_float((unsigned)wl[u]);
+                        x0[r] = __uint_as_float((unsigned)w0[u]);
+                        x1[r] = __uint_as_float((unsigned)w1[u]);
+                        if ((unsigned)(wl[u] >> 32) != ep) ok = ok && wait_word(sr + P.hq_total * HD + gh, ep, lr[r]);
+                        if ((unsigned)(w0[u] >> 32) != ep) ok = ok && wait_word(sr + gh * HD + d, ep, x0[r]);
+                        if ((unsigned)(w1[u] >> 32) != ep) ok = ok && wait_word(sr + gh * HD + d + 1, ep, x1[r]);
+                    }
+                }
+            }
+            if (!ok) atomicExch(P.err, DEV_ERR_TIMEOUT);
+            float Mx = -INFINITY;
+            for (int r = 0; r < W; r++) Mx = fmaxf(Mx, ok ? lr[r] : -INFINITY);
+            float Wt = 0.0f, a0 = 0.0f, a1 = 0.0f;
+            for (int r = 0; r < W; r++) {
+                const float wr = (!ok || lr[r] == -INFINITY) ? 0.0f : exp2f(lr[r] - Mx);
+                Wt += wr;
+                a0 = fmaf(wr, x0[r], a0);
+                a1 = fmaf(wr, x1[r], a1);
+            }
+            if (ok) *reinterpret_cast<float2*>(P.xb + (size_t)gh * HD + d) = make_float2(a0 / Wt, a1 / Wt);
+            named_bar_sync(1, C::NCONS);
+            if (tid == 0) *reinterpret_cast<volatile unsigned*>(P.peer_epoch + kvh) = ep;
+            write_out = false;
         }
         if (write_out) {
             float* xo = P.xb + (size_t)b * P.hq_total * HD + (size_t)(hq0 + h) * HD + d;

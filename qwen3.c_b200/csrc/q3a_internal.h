@@ -15,6 +15,8 @@ constexpr int DEC_TILE = 64;        // cache tokens per pipeline stage (decode)
 constexpr int DEC_BOX = 16;         // rows per TMA box; split points are multiples of it
 constexpr int MAX_PIECES = 160;     // piece-mode schedule capacity (>= SM count)
 constexpr int PART_STRIDE = 4 * 128 + 4;  // floats per partial slot: o[4][128], lse[4]
+constexpr int PEER_MAX = 8;         // ranks of a peer-memory sequence shard
+constexpr int PEER_MAXG = 16;       // KV heads (groups) per flag row
 
 // One contiguous range of cache rows of one (sequence, kv head) group, the
 // unit of work of a CTA in piece mode.  Pieces of a group are numbered
@@ -73,6 +75,11 @@ struct DecodeParams {
     int cache_mode;          // CacheMode
     int fused;               // 1: new token prepared + appended in-kernel
     int partial_out;         // 1: write normalised o + lse instead of xb
+    int peer_world;          // > 0: sequence-shard exchange over peer memory
+    int peer_rank;
+    int peer_row;            // 8-byte words per row: hq_total*128 + hq_total
+    float* peer_recv[PEER_MAX];      // every rank's receive buffer (this device's view)
+    unsigned* peer_epoch;    // this rank's call counter per KV head (device)
     long long total_units;
     int n_ctas;
     int n_pieces;            // > 0: piece mode with n_ctas == n_pieces

@@ -11,6 +11,8 @@ import os
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "lib", "libq3attn.so")
+IPC_HANDLE_BYTES = 64  # Q3A_IPC_HANDLE_BYTES
+MAX_PEERS = 8          # Q3A_MAX_PEERS
 
 OK, ERR_INVALID, ERR_CUDA, ERR_OOM, ERR_UNSUPPORTED, ERR_TIMEOUT = 0, 1, 2, 3, 4, 5
 KV_F32, KV_BF16 = 0, 1
@@ -24,6 +26,7 @@ EXPORTS = [
     "q3a_sync", "q3a_check_device_error", "q3a_attn_layer", "q3a_attn_decode",
     "q3a_attn_layer_batched", "q3a_kv_append", "q3a_kv_load", "q3a_kv_read", "q3a_prefill",
     "q3a_prefill_attn", "q3a_attn_partial", "q3a_lse_combine", "q3a_lse_combine_packed",
+    "q3a_peer_export", "q3a_peer_open", "q3a_attn_seqshard",
     "q3a_randn",
     "q3a_launch_count", "q3a_attn_decode_noalloc",
 ]
@@ -77,6 +80,9 @@ def load():
         L.q3a_attn_partial.argtypes = [_P, _P, _P, _P, _I, _I, _I, _I]
         L.q3a_lse_combine.argtypes = [_P, _P, _P, _P, _I]
         L.q3a_lse_combine_packed.argtypes = [_P, _P, _P, _I]
+        L.q3a_peer_export.argtypes = [_P, _I, _P]
+        L.q3a_peer_open.argtypes = [_P, _I, _I, _P]
+        L.q3a_attn_seqshard.argtypes = [_P, _P, _P, _I, _I, _I]
         L.q3a_randn.argtypes = [_P, _P, _I, _SZ, _U64, _U64, _U64]
         L.q3a_attn_decode_noalloc.argtypes = [_P, _P, _P, _P, _SZ, _I, _I, _I, _I, _I, _I, _P]
         L.q3a_launch_count.argtypes = [_P]
@@ -196,6 +202,21 @@ class Context:
 
     def lse_combine_packed(self, xb, parts, n_parts):
         check(self.lib.q3a_lse_combine_packed(self.h, ptr(xb), ptr(parts), n_parts))
+
+    def peer_export(self, world) -> bytes:
+        """This rank's receive-buffer handle (IPC_HANDLE_BYTES bytes)."""
+        buf = ctypes.create_string_buffer(IPC_HANDLE_BYTES)
+        check(self.lib.q3a_peer_export(self.h, world, buf))
+        return buf.raw
+
+    def peer_open(self, rank, world, handles):
+        """handles: every rank's peer_export() bytes, in rank order."""
+        blob = b"".join(handles)
+        buf = ctypes.create_string_buffer(blob, len(blob))
+        check(self.lib.q3a_peer_open(self.h, rank, world, buf))
+
+    def attn_seqshard(self, xb, q, seq, layer, n_local):
+        check(self.lib.q3a_attn_seqshard(self.h, ptr(xb), ptr(q), seq, layer, n_local))
 
     def randn(self, dst, out_dtype, n, seed, stream_id, offset=0):
         check(self.lib.q3a_randn(self.h, ptr(dst), out_dtype, n, seed, stream_id, offset))

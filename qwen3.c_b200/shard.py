@@ -7,11 +7,17 @@ issues are new, and all arithmetic stays in the library's kernels.
 
 * Sequence shards (long-context decode).  Rank r holds cache positions
   ``seq_chunk(L, world, r)`` of the sequence, stored compactly from row 0 of
-  its own context.  Each rank writes its chunk's normalised output and
-  log2-sum-exp into one packed row ``[n_heads*hd | n_heads]``
-  (``q3a_attn_partial``); one all-gather gives every rank all rows, and
-  ``q3a_lse_combine_packed`` merges them by log-sum-exp weights into the full
-  xb on every rank.
+  its own context.  Two exchanges are available:
+
+  - ``mode="peer"``: one launch per layer (``q3a_attn_seqshard``) whose
+    kernel stores each KV head's (o, lse) straight into every rank's receive
+    buffer over NVLink (buffers mapped once with ``q3a_peer_export`` /
+    ``q3a_peer_open``; the handles travel through one all_gather_object) and
+    merges once all ranks' rows have arrived;
+  - ``mode="nccl"``: each rank writes its chunk's normalised output and
+    log2-sum-exp into one packed row ``[n_heads*hd | n_heads]``
+    (``q3a_attn_partial``); one NCCL all-gather gives every rank all rows, and
+    ``q3a_lse_combine_packed`` merges them into the full xb on every rank.
 * KV-head shards (batched decode, prefill).  Rank r holds KV heads
   ``kv_heads(n_kv, world, r)`` and their query heads; attention needs no
   exchange, and one all-gather of the xb head slices rebuilds xb.
@@ -64,11 +70,22 @@ class SeqShardDecode:
     """
 
     def __init__(self, torch, ctx=None, *, world: int, rank: int, group=None,
-                 n_heads: int = 32, hd: int = 128, device=None,
+                 n_heads: int = 32, hd: int = 128, device=None, mode: str = "nccl",
                  partial: Optional[Callable] = None, combine: Optional[Callable] = None):
         import torch.distributed as dist
         self.dist = dist
         self.world, self.rank, self.group = world, rank, group
+        if mode not in ("nccl", "peer"):
+            raise ValueError(f"mode {mode!r}")
+        self.mode = mode
+        self.ctx = ctx
+        if mode == "peer":
+            handle = ctx.peer_export(world)
+            handles = [handle]
+            if world > 1:
+                handles = [None] * world
+                dist.all_gather_object(handles, handle, group=group)
+            ctx.peer_open(rank, world, handles)
         self.nq = n_heads * hd
         self.width = packed_width(n_heads, hd)
         self.send = torch.zeros(self.width, dtype=torch.float32, device=device)
@@ -79,6 +96,9 @@ class SeqShardDecode:
     def __call__(self, xb, q, seq: int, layer: int, n_local: int):
         """xb <- attention of q over all ranks' chunks; this rank's chunk is
         rows [0, n_local) of its own cache (slot ``seq``, layer ``layer``)."""
+        if self.mode == "peer":
+            self.ctx.attn_seqshard(xb, q, seq, layer, n_local)
+            return
         if self.world == 1:  # one shard: no exchange
             self.partial(self.recv[0, : self.nq], self.recv[0, self.nq:], q, seq, layer, 0, n_local)
         else:

@@ -1,7 +1,8 @@
 """Worker of test_shard_gpu.py::test_sequence_shards_over_nccl_two_gpus, run
 under torchrun (one process per GPU): a 20000-token bf16 sequence split over
 the ranks, one decode step through shard.SeqShardDecode (q3a_attn_partial,
-NCCL all-gather, q3a_lse_combine_packed), compared with the oracle's single
+NCCL all-gather, q3a_lse_combine_packed; or, with SHARD_MODE=peer, the
+peer-memory exchange of q3a_attn_seqshard), compared with the oracle's single
 pass (the reference's attention loop, cpu/main.c:1331-1353)."""
 import datetime
 import os
@@ -37,15 +38,20 @@ def main():
         ctx.set_stream(st.cuda_stream)
         ctx.kv_load(0, 0, 0, t1 - t0, torch.from_numpy(kc[t0 * KV_DIM:t1 * KV_DIM]).to(dev),
                     torch.from_numpy(vc[t0 * KV_DIM:t1 * KV_DIM]).to(dev))
-        dec = shard.SeqShardDecode(torch, ctx, world=world, rank=rank, device=dev)
-        xb = torch.zeros(HQ * HD, device=dev)
+        dec = shard.SeqShardDecode(torch, ctx, world=world, rank=rank, device=dev,
+                                   mode=os.environ.get("SHARD_MODE", "nccl"))
         q = torch.from_numpy(qv).to(dev)
-        torch.cuda.synchronize(dev)
-        with torch.cuda.stream(st):
-            dec(xb, q, 0, 0, t1 - t0)
-        st.synchronize()
-        ctx.check_device_error()
-        got = xb.cpu().numpy()
+        outs = []
+        for _ in range(3):  # repeated calls: the peer exchange alternates buffer halves
+            xb = torch.zeros(HQ * HD, device=dev)
+            torch.cuda.synchronize(dev)
+            with torch.cuda.stream(st):
+                dec(xb, q, 0, 0, t1 - t0)
+            st.synchronize()
+            ctx.check_device_error()
+            outs.append(xb.cpu().numpy())
+        got = outs[-1]
+        assert all(np.array_equal(o, got) for o in outs)
     dist.barrier()
     dist.destroy_process_group()
     ref = orc.attn_decode(qv, kc, vc, 0, L - 1, HQ, KV_MUL, HD, KV_DIM, L)

@@ -166,6 +166,36 @@ def test_kv_head_shards_prefill(world):
     assert err <= TOL_BF16_ABS, f"{world} head shards: max-abs {err}"
 
 
+@pytest.mark.parametrize("bf16", [False, True])
+def test_peer_seqshard_one_rank(bf16):
+    """The peer-memory path with one rank (no cross-GPU wait): partial decode,
+    store of the packed row into its own buffer, flag, merge; repeated calls
+    alternate the buffer halves and give the same result."""
+    import torch
+    dev = torch.device("cuda:0")
+    L = 5000
+    kc, vc, _, _ = orc.make_cache(808, 0, L, HKV, HD, L, bf16=bf16)
+    q = orc.randn(HQ * HD, 808, 9)
+    ref = orc.attn_decode(q, kc, vc, 0, L - 1, HQ, KV_MUL, HD, KV_DIM, L)
+    dt = q3attn.KV_BF16 if bf16 else q3attn.KV_F32
+    with q3attn.Context(n_layers=1, max_seq=L, kv_dtype=dt, ptr_mode=q3attn.PTR_DEVICE) as ctx:
+        ctx.kv_load(0, 0, 0, L, torch.from_numpy(kc).to(dev), torch.from_numpy(vc).to(dev))
+        h = ctx.peer_export(1)
+        assert len(h) == q3attn.IPC_HANDLE_BYTES
+        ctx.peer_open(0, 1, [h])
+        qd = torch.from_numpy(q).to(dev)
+        outs = []
+        for _ in range(3):
+            xb = torch.zeros(HQ * HD, device=dev)
+            ctx.attn_seqshard(xb, qd, 0, 0, L)
+            ctx.sync()
+            ctx.check_device_error()
+            outs.append(xb.cpu().numpy())
+        for o in outs:
+            check_close(o, ref, bf16, "peer seqshard, one rank")
+        assert all(np.array_equal(o, outs[0]) for o in outs)
+
+
 def _free_port():
     s = socket.socket()
     s.bind(("127.0.0.1", 0))
@@ -174,15 +204,17 @@ def _free_port():
     return port
 
 
-def test_sequence_shards_over_nccl_two_gpus(tmp_path):
+@pytest.mark.parametrize("mode", ["nccl", "peer"])
+def test_sequence_shards_over_nccl_two_gpus(tmp_path, mode):
     """Two ranks launched the way bench.py --gpus 2 is (torchrun, one process
-    per GPU, NCCL over NVLink); each checks its combined xb against the
-    oracle and writes the error to a file."""
+    per GPU); the exchange is an NCCL all-gather or the peer-memory stores of
+    q3a_attn_seqshard; each rank checks its combined xb against the oracle
+    and writes the error to a file."""
     import subprocess
     import torch
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
-    env = dict(os.environ, NCCL_NVLS_ENABLE="0", SHARD_TEST_OUT=str(tmp_path))
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", SHARD_TEST_OUT=str(tmp_path), SHARD_MODE=mode)
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2",
            "--master-addr", "127.0.0.1", "--master-port", str(_free_port()),
            os.path.join(ROOT, "tests", "nccl_seq_shard.py")]
