@@ -89,6 +89,8 @@ struct q3a_ctx {
     float* partials = nullptr;
     long long part_slots = 0;
     int* counters = nullptr;
+    unsigned long long* words = nullptr;  // spread-merge slots (tagged words)
+    unsigned* group_epoch = nullptr;      // spread-merge call number per group
     int* err = nullptr;
     cudaStream_t own_stream = nullptr;
     cudaStream_t stream = nullptr;
@@ -184,6 +186,8 @@ static void destroy_ctx(q3a_ctx* c) {
     cudaFree(c->vcache);
     cudaFree(c->partials);
     cudaFree(c->counters);
+    cudaFree(c->words);
+    cudaFree(c->group_epoch);
     cudaFree(c->err);
     cudaFree(c->d_inv_freq);
     cudaFree(c->d_stage);
@@ -261,6 +265,8 @@ extern "C" int q3a_create(q3a_ctx** out, const q3a_cfg* cfg_in) {
     c->part_slots = (long long)c->num_sms + max_groups;
     if (cudaMalloc(&c->partials, (size_t)c->part_slots * PART_STRIDE * 4) != cudaSuccess ||
         cudaMalloc(&c->counters, (size_t)max_groups * sizeof(int)) != cudaSuccess ||
+        cudaMalloc(&c->words, (size_t)MAX_PIECES * PART_STRIDE * 8) != cudaSuccess ||
+        cudaMalloc(&c->group_epoch, (size_t)MAX_PIECES * sizeof(unsigned)) != cudaSuccess ||
         cudaMalloc(&c->err, sizeof(int)) != cudaSuccess ||
         cudaMalloc(&c->d_inv_freq, sizeof(c->inv_freq)) != cudaSuccess) {
         destroy_ctx(c);
@@ -274,6 +280,9 @@ extern "C" int q3a_create(q3a_ctx** out, const q3a_cfg* cfg_in) {
     if (cudaMemsetAsync(c->kcache, 0, cache_bytes, c->stream) != cudaSuccess ||
         cudaMemsetAsync(c->vcache, 0, cache_bytes, c->stream) != cudaSuccess ||
         cudaMemsetAsync(c->counters, 0, (size_t)max_groups * sizeof(int), c->stream) != cudaSuccess ||
+        cudaMemsetAsync(c->words, 0, (size_t)MAX_PIECES * PART_STRIDE * 8, c->stream) != cudaSuccess ||
+        cudaMemsetAsync(c->group_epoch, 0, (size_t)MAX_PIECES * sizeof(unsigned), c->stream) !=
+            cudaSuccess ||
         cudaMemsetAsync(c->err, 0, sizeof(int), c->stream) != cudaSuccess ||
         cudaMemcpyAsync(c->d_inv_freq, c->inv_freq, sizeof(c->inv_freq), cudaMemcpyHostToDevice,
                         c->stream) != cudaSuccess ||
@@ -338,8 +347,11 @@ extern "C" int q3a_check_device_error(q3a_ctx* c) {
     if (h != 0) {
         const int max_groups = Q3A_MAX_BATCH * c->cfg.n_kv_heads;
         CUDA_TRY(cudaMemsetAsync(c->err, 0, sizeof(int), c->stream));
-        // an abandoned launch may have left arrival counters behind
+        // an abandoned launch may have left arrival counters behind, and
+        // spread-merge words of a call whose number was never advanced
         CUDA_TRY(cudaMemsetAsync(c->counters, 0, (size_t)max_groups * sizeof(int), c->stream));
+        CUDA_TRY(cudaMemsetAsync(c->words, 0, (size_t)MAX_PIECES * PART_STRIDE * 8, c->stream));
+        CUDA_TRY(cudaMemsetAsync(c->group_epoch, 0, (size_t)MAX_PIECES * sizeof(unsigned), c->stream));
         CUDA_TRY(cudaStreamSynchronize(c->stream));
         return fail(Q3A_ERR_TIMEOUT, "a bounded device wait expired (device error %d)", h);
     }
@@ -355,6 +367,9 @@ static void base_params(q3a_ctx* c, DecodeParams& p, int layer) {
     p.vcache = c->vcache;
     p.partials = c->partials;
     p.counters = c->counters;
+    p.words = c->words;
+    p.group_epoch = c->group_epoch;
+    p.spread = 1;
     p.err = c->err;
     p.eps = c->cfg.norm_eps;
     p.scale_log2e = (float)(1.4426950408889634 / sqrt((double)HD));
@@ -839,7 +854,8 @@ extern "C" int q3a_attn_seqshard(q3a_ctx* c, float* xb, const float* q, int seq,
     p.t_end[0] = n_local;
     p.q = q;
     p.xb = xb;
-    p.peer_world = c->peer_world;
+    // one rank: its own merge is the whole result, nothing to exchange
+    p.peer_world = c->peer_world > 1 ? c->peer_world : 0;
     p.peer_rank = c->peer_rank;
     p.peer_row = (int)peer_row(c);
     for (int r = 0; r < c->peer_world; r++) p.peer_recv[r] = c->peer_ptrs[r];

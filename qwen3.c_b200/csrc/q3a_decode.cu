@@ -457,7 +457,113 @@ __device__ __forceinline__ bool wait_word(const unsigned long long* p, unsigned 
     return true;
 }
 
-template <typename KV>
+// Same word format inside one GPU (the spread merge of split-KV ranges).
+__device__ __forceinline__ void st_word_gpu(unsigned long long* p, float v, unsigned tag) {
+    const unsigned long long w = ((unsigned long long)tag << 32) | __float_as_uint(v);
+    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+template <bool SYS>
+__device__ __forceinline__ unsigned long long ld_word(const unsigned long long* p) {
+    unsigned long long w;
+    if constexpr (SYS)
+        asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+    else
+        asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+    return w;
+}
+
+constexpr int SPREAD_MAXJ = 8;  // sources per thread in a spread gather
+
+// Log-sum-exp state (max, weight, weighted sum) of one output value; the
+// combination of two states is exact in the order it is applied.
+__device__ __forceinline__ void lse_fold(float& M, float& W, float& A, float m2, float w2, float a2) {
+    const float Mn = fmaxf(M, m2);
+    if (Mn == -INFINITY) return;
+    const float s1 = exp2f(M - Mn), s2 = exp2f(m2 - Mn);
+    W = W * s1 + w2 * s2;
+    A = A * s1 + a2 * s2;
+    M = Mn;
+}
+
+// Spread gather: this thread reads the (o, lse) word pairs of sources
+// j = sub, sub + tpv, ... < n at base + j*stride + off_o / off_l, waits
+// (bounded) until each carries `tag`, and folds them; then the tpv lanes of
+// its value (consecutive lanes of one warp) combine by shuffles.  Returns
+// false when a word did not arrive within the limit.
+template <bool SYS>
+__device__ __forceinline__ bool spread_gather(const unsigned long long* base, size_t stride, int n,
+                                              int sub, int tpv, bool active, size_t off_o,
+                                              size_t off_l, unsigned tag, float& M, float& W,
+                                              float& A) {
+    unsigned long long wo[SPREAD_MAXJ], wl[SPREAD_MAXJ];
+    unsigned pend = 0;
+#pragma unroll
+    for (int u = 0; u < SPREAD_MAXJ; u++) {
+        const int j = sub + u * tpv;
+        wo[u] = wl[u] = 0ull;
+        if (active && j < n) {
+            wo[u] = ld_word<SYS>(base + (size_t)j * stride + off_o);
+            wl[u] = ld_word<SYS>(base + (size_t)j * stride + off_l);
+            pend |= 1u << u;
+        }
+    }
+    bool ok = true;
+    const long long t0 = clock64();
+    while (true) {
+#pragma unroll
+        for (int u = 0; u < SPREAD_MAXJ; u++)
+            if (((pend >> u) & 1u) && (unsigned)(wo[u] >> 32) == tag && (unsigned)(wl[u] >> 32) == tag)
+                pend &= ~(1u << u);
+        if (pend == 0) break;
+        if (clock64() - t0 > WAIT_LIMIT_CYCLES) {
+            ok = false;
+            break;
+        }
+#pragma unroll
+        for (int u = 0; u < SPREAD_MAXJ; u++) {
+            if ((pend >> u) & 1u) {
+                const int j = sub + u * tpv;
+                wo[u] = ld_word<SYS>(base + (size_t)j * stride + off_o);
+                wl[u] = ld_word<SYS>(base + (size_t)j * stride + off_l);
+            }
+        }
+    }
+    M = -INFINITY;
+    W = 0.0f;
+    A = 0.0f;
+#pragma unroll
+    for (int u = 0; u < SPREAD_MAXJ; u++) {
+        const int j = sub + u * tpv;
+        if (ok && active && j < n)
+            lse_fold(M, W, A, __uint_as_float((unsigned)wl[u]), 1.0f, __uint_as_float((unsigned)wo[u]));
+    }
+    for (int o = 1; o < tpv; o <<= 1) {
+        const float m2 = __shfl_xor_sync(FULL, M, o);
+        const float w2 = __shfl_xor_sync(FULL, W, o);
+        const float a2 = __shfl_xor_sync(FULL, A, o);
+        lse_fold(M, W, A, m2, w2, a2);
+    }
+    return ok;
+}
+
+// Bounded wait of one warp until word base + j*stride carries `tag` for
+// every j < n (lane l takes j = l, l + 32, ...).  A timeout is left to the
+// gather that follows, which waits again and reports it.
+template <bool SYS>
+__device__ __forceinline__ void wait_sentinels(const unsigned long long* base, size_t stride, int n,
+                                               int lane, unsigned tag) {
+    const long long t0 = clock64();
+    for (int j = lane; j < n; j += 32) {
+        const unsigned long long* p = base + (size_t)j * stride;
+        while ((unsigned)(ld_word<SYS>(p) >> 32) != tag) {
+            if (clock64() - t0 > WAIT_LIMIT_CYCLES) return;
+        }
+    }
+}
+
+// SPREAD: piece-mode launch whose split groups merge by the spread merge
+// (a separate instantiation, so the linear-mode kernel keeps its own code).
+template <typename KV, bool SPREAD>
 __global__ void __launch_bounds__(DecCfg<KV>::NTHREADS, 1)
     decode_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                   const __grid_constant__ DecodeParams P) {
@@ -589,6 +695,13 @@ __global__ void __launch_bounds__(DecCfg<KV>::NTHREADS, 1)
             reinterpret_cast<float2*>(sQ)[tid] = qv;
             sRaw[tid] = wv;
             sRaw2[tid] = kv;
+            // call numbers of the spread merge, read before this range
+            // stores any word of the call
+            if (tid == 0 && (SPREAD && s.ncontrib > 1)) {
+                misc[1] = (int)*reinterpret_cast<volatile const unsigned*>(P.group_epoch + s.grp);
+                if (P.peer_world > 0)
+                    misc[2] = (int)*reinterpret_cast<volatile const unsigned*>(P.peer_epoch + kvh);
+            }
         }
         named_bar_sync(1, C::NCONS);
         if (P.fused) {
@@ -683,7 +796,84 @@ __global__ void __launch_bounds__(DecCfg<KV>::NTHREADS, 1)
         float lse = M + log2f(L);
 
         bool write_out = true;
-        if (s.ncontrib > 1) {
+        if ((SPREAD && s.ncontrib > 1)) {
+            // Spread merge.  Every range of the group stores its (o, lse) as
+            // tagged words into its own slot and then merges one slice of
+            // the group's 512 outputs from all slots: no ticket round trip,
+            // and no single CTA loads every partial.  Ranges wait for one
+            // another, which piece mode allows (one CTA per SM, all
+            // resident).  The tag is (call number of the group << 8 | group).
+            const unsigned gep = (unsigned)misc[1] + 1u;
+            const unsigned tag = (gep << 8) | ((unsigned)s.grp & 0xFFu);
+            unsigned long long* mine = P.words + (size_t)s.slot * PART_STRIDE;
+            st_word_gpu(mine + h * HD + d, o0, tag);
+            st_word_gpu(mine + h * HD + d + 1, o1, tag);
+            if ((tid & 63) == 0) st_word_gpu(mine + GQA * HD + h, lse, tag);
+            const int k = s.ncontrib, i = s.slot - s.slot0;
+            const int v0 = i * (GQA * HD) / k, nv = (i + 1) * (GQA * HD) / k - v0;
+            int tpv = 32;
+            while (tpv > 1 && tpv * nv > C::NCONS) tpv >>= 1;
+            const int vi = tid / tpv, sub = tid & (tpv - 1);
+            const bool act = vi < nv;
+            const int v = v0 + (act ? vi : 0), vh = v >> 7, vd = v & (HD - 1);
+            // one warp first waits for the last-stored word of every range
+            // (head 3's lse), so the full gather below is normally issued
+            // once instead of being polled by every thread
+            if (warp == 0)
+                wait_sentinels<false>(P.words + (size_t)s.slot0 * PART_STRIDE + GQA * HD + GQA - 1,
+                                      PART_STRIDE, k, lane, tag);
+            named_bar_sync(1, C::NCONS);
+            float Mv, Wv, Av;
+            bool ok = spread_gather<false>(P.words + (size_t)s.slot0 * PART_STRIDE, PART_STRIDE, k,
+                                           sub, tpv, act, v, GQA * HD + vh, tag, Mv, Wv, Av);
+            float ov = Av / Wv, lv = Mv + log2f(Wv);
+            const int gh = hq0 + vh;
+            unsigned pep = 0;
+            if (P.peer_world > 0) {
+                // then the same exchange across ranks, slice by slice: the
+                // owner of each value stores it (and the owner of a head's
+                // first value that head's lse) into row `rank` of every
+                // rank's receive buffer, and every slice merges its values
+                // from all ranks' rows
+                const int Wr = P.peer_world, R = P.peer_rank;
+                const size_t row = (size_t)P.peer_row;
+                pep = (unsigned)misc[2] + 1u;
+                const int par = (int)(pep & 1u);
+                if (ok && act && sub == 0) {
+                    for (int r = 0; r < Wr; r++) {
+                        unsigned long long* dst = reinterpret_cast<unsigned long long*>(P.peer_recv[r]) +
+                                                  ((size_t)par * Wr + R) * row;
+                        st_word_sys(dst + (size_t)gh * HD + vd, ov, pep);
+                        if (vd == 0) st_word_sys(dst + (size_t)P.hq_total * HD + gh, lv, pep);
+                    }
+                }
+                const unsigned long long* src =
+                    reinterpret_cast<const unsigned long long*>(P.peer_recv[R]) + (size_t)par * Wr * row;
+                if (warp == 0)
+                    wait_sentinels<true>(src + (size_t)P.hq_total * HD + hq0 + (v0 >> 7), row, Wr, lane,
+                                         pep);
+                named_bar_sync(1, C::NCONS);
+                ok = spread_gather<true>(src, row, Wr, sub, tpv, act && ok, (size_t)gh * HD + vd,
+                                         (size_t)P.hq_total * HD + gh, pep, Mv, Wv, Av) && ok;
+                ov = Av / Wv;
+                lv = Mv + log2f(Wv);
+            }
+            if (!ok) atomicExch(P.err, DEV_ERR_TIMEOUT);
+            if (ok && act && sub == 0) {
+                P.xb[(size_t)b * P.hq_total * HD + (size_t)gh * HD + vd] = ov;
+                if (P.lse_out && vd == 0) P.lse_out[(size_t)b * P.hq_total + gh] = lv;
+            }
+            // the rotated q goes back slice by slice once every range of
+            // the group has stored its words (so has read the raw q)
+            if (P.fused && P.q_out && P.peer_world == 0 && tid < nv)
+                P.q_out[(size_t)b * P.hq_total * HD + (size_t)hq0 * HD + v0 + tid] = sQ[v0 + tid];
+            if (i == 0 && tid == 0) {
+                // every range of the group has read the call numbers by now
+                *reinterpret_cast<volatile unsigned*>(P.group_epoch + s.grp) = gep;
+                if (P.peer_world > 0) *reinterpret_cast<volatile unsigned*>(P.peer_epoch + kvh) = pep;
+            }
+            write_out = false;
+        } else if (s.ncontrib > 1) {
             float* ps = P.partials + (long long)s.slot * PART_STRIDE;
             *reinterpret_cast<float2*>(ps + h * HD + d) = make_float2(o0, o1);
             if ((tid & 63) == 0) ps[GQA * HD + h] = lse;
@@ -812,25 +1002,30 @@ __global__ void __launch_bounds__(DecCfg<KV>::NTHREADS, 1)
     }
 }
 
-template <typename KV>
+template <typename KV, bool SPREAD>
 static cudaError_t launch_decode_t(const DecodeParams& p, const CUtensorMap& tmK,
                                    const CUtensorMap& tmV, cudaStream_t st) {
     using C = DecCfg<KV>;
     static bool attr_set = false;
     if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(decode_kernel<KV>,
+        cudaError_t e = cudaFuncSetAttribute(decode_kernel<KV, SPREAD>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
         if (e != cudaSuccess) return e;
         attr_set = true;
     }
-    decode_kernel<KV><<<p.n_ctas, C::NTHREADS, C::SMEM, st>>>(tmK, tmV, p);
+    decode_kernel<KV, SPREAD><<<p.n_ctas, C::NTHREADS, C::SMEM, st>>>(tmK, tmV, p);
     return cudaGetLastError();
 }
 
 cudaError_t launch_decode(const DecodeParams& p, const CUtensorMap& tmK, const CUtensorMap& tmV,
                           bool bf16, cudaStream_t st) {
-    return bf16 ? launch_decode_t<__nv_bfloat16>(p, tmK, tmV, st)
-                : launch_decode_t<float>(p, tmK, tmV, st);
+    // the spread merge needs every range resident at once: piece mode only
+    const bool spread = p.spread && p.n_pieces > 0;
+    if (bf16)
+        return spread ? launch_decode_t<__nv_bfloat16, true>(p, tmK, tmV, st)
+                      : launch_decode_t<__nv_bfloat16, false>(p, tmK, tmV, st);
+    return spread ? launch_decode_t<float, true>(p, tmK, tmV, st)
+                  : launch_decode_t<float, false>(p, tmK, tmV, st);
 }
 
 int decode_smem_bytes(bool bf16) {

@@ -83,6 +83,9 @@ struct DecodeParams {
     long long total_units;
     int n_ctas;
     int n_pieces;            // > 0: piece mode with n_ctas == n_pieces
+    int spread;              // 1: piece-mode groups merge by the spread merge
+    unsigned long long* words;   // spread merge: MAX_PIECES slots of PART_STRIDE tagged words
+    unsigned* group_epoch;   // spread merge: call number per group [MAX_PIECES]
     const float* inv_freq;   // [64] RoPE inverse frequencies (host powf, reference formula)
     Piece pieces[MAX_PIECES];
     int t_begin[MAX_B];      // first cache position attended per sequence
