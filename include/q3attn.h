@@ -81,7 +81,10 @@ typedef struct q3a_ctx q3a_ctx;
 void q3a_cfg_default(q3a_cfg *cfg);
 
 /* Allocates the device KV cache ([layer][kv head][page][token][128], pages
- * 128-byte aligned, zero-filled) and the context's scratch.  Replaces
+ * 128-byte aligned, zero-filled; a bf16 cache stores each block of 8 tokens
+ * as [2 dim-halves][8 tokens][64 dims] with the 128-byte swizzle of the
+ * tensor-core operands, so it is read through q3a_kv_read, not by address)
+ * and the context's scratch.  Replaces
  * alloc_state / alloc_state_gpu for the cache (qwen3-8b/cpu/main.c:1134-1148,
  * qwen3-8b/gpu/main.c:1287-1323); sizes are size_t, so 36 layers x 131072
  * positions do not overflow as the reference's int kv_cache_len does. */

@@ -96,7 +96,6 @@ struct q3a_ctx {
     cudaStream_t stream = nullptr;
     int num_sms = 148;
     CUtensorMap tmK, tmV;          // decode maps of the paged cache
-    CUtensorMap tmKp, tmVp;        // prefill maps (bf16, 128B swizzle)
     float inv_freq[64];
     float* d_inv_freq = nullptr;   // the same table in device memory
     // host-mode staging
@@ -295,13 +294,6 @@ extern "C" int q3a_create(q3a_ctx** out, const q3a_cfg* cfg_in) {
     if (rc == Q3A_OK)
         rc = make_map_2d(&c->tmV, c->vcache, c->bf16, HD, (uint64_t)c->total_rows, HD, DEC_BOX,
                          CU_TENSOR_MAP_SWIZZLE_NONE);
-    if (rc == Q3A_OK && c->bf16) {
-        rc = make_map_2d(&c->tmKp, c->kcache, true, HD, (uint64_t)c->total_rows, 64, 64,
-                         CU_TENSOR_MAP_SWIZZLE_128B);
-        if (rc == Q3A_OK)
-            rc = make_map_2d(&c->tmVp, c->vcache, true, HD, (uint64_t)c->total_rows, 64, 64,
-                             CU_TENSOR_MAP_SWIZZLE_128B);
-    }
     if (rc != Q3A_OK) {
         destroy_ctx(c);
         return rc;
@@ -503,6 +495,8 @@ static int run_decode(q3a_ctx* c, DecodeParams& p, const CUtensorMap& tk, const 
                       bool bf16) {
     int rc = schedule(c, p);
     if (rc) return rc;
+    // the context's bf16 paged cache is consumed on the tensor cores
+    p.tc = (bf16 && p.cache_mode == CACHE_PAGED) ? 1 : 0;
     CUDA_TRY(launch_decode(p, tk, tv, bf16, c->stream));
     c->launches++;
     return Q3A_OK;
@@ -1123,7 +1117,9 @@ extern "C" int q3a_prefill_attn(q3a_ctx* c, void* out, int out_dtype, const void
     pp.n_pages = c->n_pages;
     pp.scale_log2e = (float)(1.4426950408889634 / sqrt((double)HD));
     pp.err = c->err;
-    CUDA_TRY(launch_prefill(pp, tq, c->tmKp, c->tmVp, c->stream));
+    pp.kcache = reinterpret_cast<const __nv_bfloat16*>(c->kcache);
+    pp.vcache = reinterpret_cast<const __nv_bfloat16*>(c->vcache);
+    CUDA_TRY(launch_prefill(pp, tq, c->stream));
     c->launches++;
     if (c->cfg.ptr_mode == Q3A_PTR_HOST) {
         CUDA_TRY(cudaMemcpyAsync(out, dout, out_bytes, cudaMemcpyDeviceToHost, c->stream));

@@ -195,4 +195,22 @@ __device__ __forceinline__ void rope_pair(float& v0, float& v1, int pos, float i
     v1 = b;
 }
 
+// Element index of (row R, dim d) in a context's paged cache.  fp32 rows are
+// plain 128-float rows.  bf16 rows are kept in blocks of 8 rows (2 KB, the
+// same bytes the 8 rows would occupy row by row): [2 dim-halves][8 rows][64
+// dims], the 16-byte chunk c of row r stored at chunk c ^ (r % 8).  That is
+// the 128-byte-swizzled K-major operand layout of the tensor cores, so a run
+// of whole blocks is one contiguous bulk copy into shared memory, ready for
+// tcgen05.mma as K (K-major) and as V (MN-major).
+template <typename KV>
+__device__ __forceinline__ size_t kv_index(long long R, int d) {
+    if constexpr (sizeof(KV) == 2) {
+        const int r = (int)(R & 7);
+        return (size_t)(R >> 3) * 1024 +
+               (size_t)((d >> 6) * 512 + r * 64 + ((((d >> 3) & 7) ^ r) << 3) + (d & 7));
+    } else {
+        return (size_t)R * HD + d;
+    }
+}
+
 }  // namespace q3a

@@ -34,10 +34,11 @@
 //    log-sum-exp into xb.
 #include "q3a_common.cuh"
 #include "q3a_internal.h"
+#include "q3a_tcgen05.cuh"
 
 namespace q3a {
 
-template <typename KV>
+template <typename KV, bool TC = false>
 struct DecCfg {
     static constexpr int TILE = DEC_TILE;
     static constexpr int CWARPS = 8;
@@ -61,6 +62,78 @@ struct DecCfg {
     static constexpr int SMEM = OFF_MISC + 64;
     static_assert(SMEM <= 232448, "decode shared memory exceeds the sm_100 limit");
 };
+
+// Tensor-core consumer (bf16 paged caches).  Stages of 128 cache rows, K and
+// V each copied as is from the cache, whose 8-row blocks ([2 dim-halves][8
+// rows][128 B], 128-byte swizzle) are the MMA operand layout: S^T = K . Q^T
+// (A = K, K-major) and O^T = V^T . P^T (A = V read MN-major).  Q^T and P^T
+// are [16][128] bf16 operands of two [16 rows][128 B] halves (rows 0-3 the 4
+// query heads' high parts, rows 4-7 their low parts, rows 8-15 zero).
+template <>
+struct DecCfg<__nv_bfloat16, true> {
+    static constexpr int TILE = 128;
+    static constexpr int CWARPS = 8;
+    static constexpr int NCONS = CWARPS * 32;
+    static constexpr int NTHREADS = NCONS + 32;
+    static constexpr int STAGES = 3;
+    static constexpr int TILE_BYTES = TILE * HD * 2;        // one tensor of a stage
+    static constexpr int OPB_BYTES = 16 * HD * 2;           // a [16][128] bf16 operand
+    static constexpr int OFF_K = 0;
+    static constexpr int OFF_V = STAGES * TILE_BYTES;
+    static constexpr int OFF_QT = 2 * STAGES * TILE_BYTES;  // Q^T
+    static constexpr int OFF_PT = OFF_QT + OPB_BYTES;       // P^T, two buffers
+    static constexpr int OFF_QS = OFF_PT + 2 * OPB_BYTES;   // float [4][128]
+    static constexpr int OFF_RAW = OFF_QS + GQA * HD * 4;
+    static constexpr int OFF_RAW2 = OFF_RAW + 256 * 4;
+    static constexpr int OFF_NEWK = OFF_RAW2 + 256 * 4;
+    static constexpr int OFF_NEWV = OFF_NEWK + HD * 2;
+    static constexpr int OFF_P = OFF_NEWV + HD * 2;         // unused here
+    static constexpr int WST = 0;
+    // o[4][128], lse[4], tile maxima [2][4 warps][4], row sums [4 warps][4]
+    static constexpr int OFF_WST = OFF_P + 16;
+    static constexpr int W_LSE = GQA * HD, W_RED = W_LSE + GQA, W_LSUM = W_RED + 32;
+    static constexpr int OFF_BAR = OFF_WST + (W_LSUM + 16) * 4;
+    // full[3] empty[3] sfull[2] pfull[2] ofull[2] newrow drain
+    static constexpr int NBAR = 2 * STAGES + 8;
+    static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
+    static constexpr int SMEM = OFF_MISC + 64 + 1024;       // + slack for 1024-byte alignment
+    static_assert(OFF_QT % 1024 == 0 && OFF_PT % 1024 == 0 && OFF_BAR % 8 == 0, "layout");
+    static_assert(SMEM <= 232448, "decode shared memory exceeds the sm_100 limit");
+};
+
+// tensor memory columns of the tensor-core consumer: S^T double buffer,
+// O^T tile double buffer, 16 columns each
+constexpr uint32_t DTC_COLS = 64;
+constexpr uint32_t DTC_S_COL = 0, DTC_O_COL = 32;
+// instruction descriptors (kind::f16, M=128, N=16): c=F32 (bit 4), a=BF16
+// (bits 7-9), b=BF16 (bits 10-12), a_major bit 15, N>>3 at 17, M>>4 at 24
+constexpr uint32_t IDESC_DS = (1u << 4) | (1u << 7) | (1u << 10) | ((16u >> 3) << 17) | ((128u >> 4) << 24);
+constexpr uint32_t IDESC_DPV = IDESC_DS | (1u << 15);
+
+// Named barrier that also returns the AND of a predicate over its threads.
+__device__ __forceinline__ bool named_bar_red_and(int id, int nthreads, bool v) {
+    int r;
+    asm volatile(
+        "{\n\t.reg .pred pi, po;\n\t"
+        "setp.ne.b32 pi, %1, 0;\n\t"
+        "barrier.cta.red.and.pred po, %2, %3, pi;\n\t"
+        "selp.b32 %0, 1, 0, po;\n\t}"
+        : "=r"(r)
+        : "r"((int)v), "r"(id), "r"(nthreads)
+        : "memory");
+    return r != 0;
+}
+
+__device__ __forceinline__ void fence_proxy_async_global() {
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+// Byte offset of element (row n, k) in a [16][128] bf16 K-major operand with
+// 128-byte swizzle: two 64-element halves of [16 rows][128 B], the 16-byte
+// chunk index XORed with the row within its 8-row group.
+__device__ __forceinline__ uint32_t opb_offset(int n, int k) {
+    return (uint32_t)((k >> 6) * 2048 + n * 128 + ((((k & 63) >> 3) ^ (n & 7)) << 4) + (k & 7) * 2);
+}
 
 // One contiguous range of cache rows of one group, as processed by a CTA.
 struct SegInfo {
@@ -563,12 +636,17 @@ __device__ __forceinline__ void wait_sentinels(const unsigned long long* base, s
 
 // SPREAD: piece-mode launch whose split groups merge by the spread merge
 // (a separate instantiation, so the linear-mode kernel keeps its own code).
-template <typename KV, bool SPREAD>
-__global__ void __launch_bounds__(DecCfg<KV>::NTHREADS, 1)
+// TC: bf16 paged cache consumed on the tensor cores (tcgen05): warp 4 issues
+// S^T = K.Q^T and O^T = V^T.P^T per 128-row stage, warps 0-3 run the
+// softmax (one thread per cache row for S, one per dimension for O).
+template <typename KV, bool SPREAD, bool TC>
+__global__ void __launch_bounds__(DecCfg<KV, TC>::NTHREADS, 1)
     decode_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                   const __grid_constant__ DecodeParams P) {
-    using C = DecCfg<KV>;
-    extern __shared__ __align__(1024) uint8_t smem[];
+    using C = DecCfg<KV, TC>;
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem = smem_raw;
+    if constexpr (TC) smem += (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
     KV* sK = reinterpret_cast<KV*>(smem + C::OFF_K);
     KV* sV = reinterpret_cast<KV*>(smem + C::OFF_V);
     float* sQ = reinterpret_cast<float*>(smem + C::OFF_QS);
@@ -580,6 +658,12 @@ __global__ void __launch_bounds__(DecCfg<KV>::NTHREADS, 1)
     float* sW = reinterpret_cast<float*>(smem + C::OFF_WST);
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
     uint64_t* empty = full + C::STAGES;
+    // tensor-core path only
+    uint64_t* sfull = empty + C::STAGES;  // S^T of a stage in tensor memory
+    uint64_t* pfull = sfull + 2;          // P^T of a stage written (128 softmax threads)
+    uint64_t* ofull = pfull + 2;          // O^T tile of a stage in tensor memory
+    uint64_t* newrow = ofull + 2;         // the new token's row is in the cache
+    uint64_t* drain = newrow + 1;         // every issued MMA complete
     volatile int* misc = reinterpret_cast<volatile int*>(smem + C::OFF_MISC);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -593,7 +677,16 @@ __global__ void __launch_bounds__(DecCfg<KV>::NTHREADS, 1)
 #pragma unroll
             for (int s = 0; s < C::STAGES; s++) {
                 mbar_init(&full[s], 1);
-                mbar_init(&empty[s], C::CWARPS);
+                mbar_init(&empty[s], TC ? 1 : C::CWARPS);
+            }
+            if constexpr (TC) {
+                for (int t = 0; t < 2; t++) {
+                    mbar_init(&sfull[t], 1);
+                    mbar_init(&pfull[t], 128);
+                    mbar_init(&ofull[t], 1);
+                }
+                mbar_init(newrow, 2);
+                mbar_init(drain, 1);
             }
             fence_mbar_init();
             tma_prefetch_desc(&tmK);
@@ -607,6 +700,57 @@ __global__ void __launch_bounds__(DecCfg<KV>::NTHREADS, 1)
             bool dead = false;
             long long cur = 0;
             SegInfo s;
+            int nnew = 0;  // ranges with a new token so far (phase of `newrow`)
+            if constexpr (TC) {
+            while (!dead && next_seg(P, c, cur, s)) {
+                // 128-row stages; the cache's 8-row blocks are already in
+                // the operand layout, so rows [t0, hi) of a page are one
+                // bulk copy per tensor.  The range includes the new token's
+                // row, which the consumers append first (the stage holding
+                // it is loaded after `newrow`).
+                const int slot = P.slot[s.b];
+                const int r_end = s.r1 + (s.has_new ? 1 : 0);
+                const int lo_all = s.r0 & ~(DEC_BOX - 1);
+                const int hi_all = (r_end + DEC_BOX - 1) & ~(DEC_BOX - 1);
+                bool need_new = s.has_new != 0;
+                for (int t0 = lo_all; t0 < r_end; t0 += C::TILE) {
+                    const int stage = it % C::STAGES;
+                    const uint32_t ph = (uint32_t)(it / C::STAGES) & 1u;
+                    if (it >= C::STAGES && !mbar_wait(&empty[stage], ph ^ 1u)) {
+                        atomicExch(P.err, DEV_ERR_TIMEOUT);
+                        dead = true;
+                        break;
+                    }
+                    const int hi = min(t0 + C::TILE, hi_all);
+                    if (need_new && hi > s.r1) {
+                        if (!mbar_wait(newrow, (uint32_t)nnew & 1u)) {
+                            atomicExch(P.err, DEV_ERR_TIMEOUT);
+                            dead = true;
+                            break;
+                        }
+                        fence_proxy_async_global();
+                        need_new = false;
+                    }
+                    mbar_arrive_expect_tx(&full[stage], (uint32_t)(2 * (hi - t0) * HD * 2));
+                    uint8_t* kst = smem + C::OFF_K + stage * C::TILE_BYTES;
+                    uint8_t* vst = smem + C::OFF_V + stage * C::TILE_BYTES;
+                    for (int a = t0; a < hi;) {
+                        // a and the page ends are multiples of 16 rows
+                        const int e = min(hi, (a / P.page_tokens + 1) * P.page_tokens);
+                        const long long row = paged_row(P, slot, s.kvh, a);
+                        const uint32_t nb = (uint32_t)((e - a) * HD * 2);
+                        const int so = (a - t0) * HD * 2;
+                        bulk_load(kst + so, reinterpret_cast<const KV*>(P.kcache) + row * HD, nb,
+                                  &full[stage], pol);
+                        bulk_load(vst + so, reinterpret_cast<const KV*>(P.vcache) + row * HD, nb,
+                                  &full[stage], pol);
+                        a = e;
+                    }
+                    it++;
+                }
+                if (s.has_new) nnew++;
+            }
+            } else {
             while (!dead && next_seg(P, c, cur, s)) {
                 const int slot = P.slot[s.b];
                 // tiles start at the range's own 16-row-aligned start, so a
@@ -656,6 +800,7 @@ __global__ void __launch_bounds__(DecCfg<KV>::NTHREADS, 1)
                     it++;
                 }
             }
+            }
             // Drain: the CTA never exits with a bulk copy still writing its
             // shared memory (bounded, like every wait here).
             const int first = it > C::STAGES ? it - C::STAGES : 0;
@@ -675,6 +820,24 @@ __global__ void __launch_bounds__(DecCfg<KV>::NTHREADS, 1)
     long long cur = 0;
     SegInfo s;
     float2* pw = sP + warp * 32;
+    volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(misc + 4);
+    if constexpr (TC) {
+        if (warp == GQA) {
+            asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                             smem_u32((const void*)tmem_slot)),
+                         "r"(DTC_COLS)
+                         : "memory");
+            asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+        }
+        // rows 8-15 of Q^T and of both P^T buffers stay zero
+        for (int i = tid; i < 3 * 128; i += C::NCONS) {
+            const int op = i >> 7, hf = (i >> 6) & 1;
+            *reinterpret_cast<uint4*>(smem + C::OFF_QT + op * C::OPB_BYTES + hf * 2048 + 1024 +
+                                      (i & 63) * 16) = make_uint4(0u, 0u, 0u, 0u);
+        }
+        fence_proxy_async_smem();
+        tc_fence_before();
+    }
     while (next_seg(P, c, cur, s)) {
         const int b = s.b, kvh = s.kvh;
         const int hq0 = (P.kv0 + kvh) * GQA;
@@ -723,77 +886,294 @@ __global__ void __launch_bounds__(DecCfg<KV>::NTHREADS, 1)
                 }
                 store4<KV>(sNewK + 4 * lane, kr);
                 const long long row = paged_row(P, slot, kvh, pos);
-                store4<KV>(reinterpret_cast<KV*>(P.kcache) + row * HD + 4 * lane, kr);
+                store4<KV>(reinterpret_cast<KV*>(P.kcache) + kv_index<KV>(row, 4 * lane), kr);
+                if constexpr (TC) {
+                    // the producer loads this row with the range's last stage
+                    fence_proxy_async_global();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(newrow);
+                }
             } else if (warp == GQA + 1 && s.has_new) {
                 const float4 vv = reinterpret_cast<const float4*>(sRaw2 + HD)[lane];
                 store4<KV>(sNewV + 4 * lane, vv);
                 const long long row = paged_row(P, slot, kvh, P.pos[b]);
-                store4<KV>(reinterpret_cast<KV*>(P.vcache) + row * HD + 4 * lane, vv);
+                store4<KV>(reinterpret_cast<KV*>(P.vcache) + kv_index<KV>(row, 4 * lane), vv);
+                if constexpr (TC) {
+                    fence_proxy_async_global();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(newrow);
+                }
             }
             named_bar_sync(1, C::NCONS);
         }
 
-        float2 qr[GQA][8];
-        load_q_regs<KV>(sQ, lane, P.scale_log2e, qr);
-        float m[GQA] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-        float lpart = 0.0f;
-        float2 O[GQA][2];
-#pragma unroll
-        for (int h = 0; h < GQA; h++) O[h][0] = O[h][1] = make_float2(0.0f, 0.0f);
-
-        bool dead = false;
-        for (int t0 = s.r0 & ~(DEC_BOX - 1); t0 < s.r1; t0 += C::TILE) {
-            const int stage = it % C::STAGES;
-            const uint32_t ph = (uint32_t)(it / C::STAGES) & 1u;
-            if (!mbar_wait(&full[stage], ph)) {
-                atomicExch(P.err, DEV_ERR_TIMEOUT);
-                dead = true;
-                break;
-            }
-            const int lo = max(s.r0 - t0, 0);
-            const int hi = min(s.r1 - t0, C::TILE);
-            process_rows<KV>(sK + stage * C::TILE * HD, sV + stage * C::TILE * HD, lo, hi, warp,
-                             lane, qr, m, lpart, O, pw);
-            if (lane == 0) mbar_arrive(&empty[stage]);
-            it++;
-        }
-        if (dead) return;
-        if (s.has_new) process_rows<KV>(sNewK, sNewV, 0, 1, warp, lane, qr, m, lpart, O, pw);
-
-        // ---- merge the 8 warp states of this range
-        float lsum = lpart;
-        lsum += __shfl_xor_sync(FULL, lsum, 4);
-        lsum += __shfl_xor_sync(FULL, lsum, 8);
-        lsum += __shfl_xor_sync(FULL, lsum, 16);
-        {
-            float* ws = sW + warp * C::WST;
-#pragma unroll
-            for (int h = 0; h < GQA; h++)
-                *reinterpret_cast<float4*>(ws + h * HD + 4 * lane) =
-                    make_float4(O[h][0].x, O[h][0].y, O[h][1].x, O[h][1].y);
-            if (lane < 4) {
-                ws[GQA * HD + lane] = sel4(m, lane);
-                ws[GQA * HD + 4 + lane] = lsum;
-            }
-        }
-        named_bar_sync(1, C::NCONS);
         const int h = tid >> 6, d = 2 * (tid & 63);
-        float M = -INFINITY;
+        float o0, o1, lse;
+        if constexpr (TC) {
+            // ---- Q^T operand: q in log2 units split into bf16 high and low
+            // parts (rows h and h+4), so the scores carry fp32-accurate q
+            {
+                const int hq = tid >> 6, k = 2 * (tid & 63);
+                const float x0 = sQ[hq * HD + k] * P.scale_log2e;
+                const float x1 = sQ[hq * HD + k + 1] * P.scale_log2e;
+                const __nv_bfloat162 hi2 = __floats2bfloat162_rn(x0, x1);
+                const float2 hf = __bfloat1622float2(hi2);
+                const __nv_bfloat162 lo2 = __floats2bfloat162_rn(x0 - hf.x, x1 - hf.y);
+                *reinterpret_cast<__nv_bfloat162*>(smem + C::OFF_QT + opb_offset(hq, k)) = hi2;
+                *reinterpret_cast<__nv_bfloat162*>(smem + C::OFF_QT + opb_offset(hq + GQA, k)) = lo2;
+            }
+            fence_proxy_async_smem();
+            tc_fence_before();
+            named_bar_sync(1, C::NCONS);
+            tc_fence_after();
+            const uint32_t tm = *tmem_slot;
+            const uint32_t sb = smem_u32(smem);
+            // the range's stages: rows [lo_all, hi_all) in 16-row boxes, of
+            // which [r0, r_end) count (r_end includes the new token's row)
+            const int r_end = s.r1 + (s.has_new ? 1 : 0);
+            const int lo_all = s.r0 & ~(DEC_BOX - 1);
+            const int hi_all = (r_end + DEC_BOX - 1) & ~(DEC_BOX - 1);
+            const int ntiles = r_end > lo_all ? (r_end - lo_all + C::TILE - 1) / C::TILE : 0;
+            const int it0 = it;
+            if (warp == GQA) {
+                // ================================== MMA issuer (one thread)
+                if (lane == 0 && ntiles > 0) {
+                    bool dead = false;
+                    auto issue_s = [&](int g) {
+                        // S^T (128 rows x 16) = K (128 x 128, K-major) . Q^T
+                        const uint32_t kb = sb + C::OFF_K + (g % C::STAGES) * C::TILE_BYTES;
+                        const uint32_t qb = sb + C::OFF_QT;
+                        const uint32_t dcol = tm + DTC_S_COL + (uint32_t)(g & 1) * 16u;
 #pragma unroll
-        for (int w = 0; w < C::CWARPS; w++) M = fmaxf(M, sW[w * C::WST + GQA * HD + h]);
-        float L = 0.0f, o0 = 0.0f, o1 = 0.0f;
+                        for (int kk = 0; kk < HD / 16; kk++) {
+                            const uint32_t koff = (kk & 3) * 32;
+                            // K: 8-row groups 2048 B apart, dim-halves 1024 B
+                            tc_mma_ss(dcol, smem_desc(kb + (kk >> 2) * 1024 + koff, 16, 2048),
+                                      smem_desc(qb + (kk >> 2) * 2048 + koff, 16, 1024), IDESC_DS,
+                                      kk > 0 ? 1u : 0u);
+                        }
+                        tc_commit(&sfull[g & 1]);
+                    };
+                    if (mbar_wait(&full[it0 % C::STAGES], (uint32_t)(it0 / C::STAGES) & 1u)) {
+                        tc_fence_after();
+                        issue_s(it0);
+                    } else {
+                        dead = true;
+                    }
+                    for (int j = 0; j < ntiles && !dead; j++) {
+                        const int g = it0 + j;
+                        if (j + 1 < ntiles) {
+                            // S of the next stage goes first; its buffer was
+                            // freed by the softmax of stage g-1
+                            const int gn = g + 1;
+                            if (!mbar_wait(&full[gn % C::STAGES], (uint32_t)(gn / C::STAGES) & 1u)) {
+                                dead = true;
+                                break;
+                            }
+                            tc_fence_after();
+                            issue_s(gn);
+                        }
+                        if (!mbar_wait(&pfull[g & 1], (uint32_t)(g >> 1) & 1u)) {
+                            dead = true;
+                            break;
+                        }
+                        tc_fence_after();
+                        // O^T tile (128 dims x 16) = V^T (MN-major) . P^T over
+                        // the loaded 16-row steps only
+                        const int t0 = lo_all + j * C::TILE;
+                        const int nk = (min(t0 + C::TILE, hi_all) - t0) / DEC_BOX;
+                        const uint32_t vb = sb + C::OFF_V + (g % C::STAGES) * C::TILE_BYTES;
+                        const uint32_t pb = sb + C::OFF_PT + (uint32_t)(g & 1) * C::OPB_BYTES;
+                        const uint32_t dcol = tm + DTC_O_COL + (uint32_t)(g & 1) * 16u;
+                        // V read MN-major: dim-halves 1024 B apart (LBO), 8-row
+                        // groups 2048 B apart (SBO), 16 rows per step
+                        for (int kk = 0; kk < nk; kk++)
+                            tc_mma_ss(dcol, smem_desc(vb + kk * 4096, 1024, 2048),
+                                      smem_desc(pb + (kk >> 2) * 2048 + (kk & 3) * 32, 16, 1024),
+                                      IDESC_DPV, kk > 0 ? 1u : 0u);
+                        tc_commit(&ofull[g & 1]);
+                        tc_commit(&empty[g % C::STAGES]);
+                    }
+                    if (dead) atomicExch(P.err, DEV_ERR_TIMEOUT);
+                }
+                __syncwarp();
+            } else if (warp < GQA) {
+                // ================================== softmax (128 threads)
+                // thread tid: cache row lo_all + 128 j + tid of stage j for
+                // the scores, dimension tid for the output
+                float mh[GQA], lsum[GQA], Oh[GQA], al_prev[GQA];
 #pragma unroll
-        for (int w = 0; w < C::CWARPS; w++) {
-            const float mw = sW[w * C::WST + GQA * HD + h];
-            const float sc = (mw == -INFINITY) ? 0.0f : exp2f(mw - M);
-            L = fmaf(sW[w * C::WST + GQA * HD + 4 + h], sc, L);
-            o0 = fmaf(sW[w * C::WST + h * HD + d], sc, o0);
-            o1 = fmaf(sW[w * C::WST + h * HD + d + 1], sc, o1);
+                for (int q = 0; q < GQA; q++) {
+                    mh[q] = -INFINITY;
+                    lsum[q] = 0.0f;
+                    Oh[q] = 0.0f;
+                    al_prev[q] = 1.0f;
+                }
+                const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+                bool ok = true;
+                uint8_t* ptb = smem + C::OFF_PT;
+                float* red = sW + C::W_RED;
+                // O <- O * alpha(g) + O^T tile of stage g
+                auto fold = [&](int g) {
+                    bool got = ok && mbar_wait(&ofull[g & 1], (uint32_t)(g >> 1) & 1u);
+                    got = __all_sync(FULL, got);
+                    if (!got) {
+                        ok = false;
+                        return;
+                    }
+                    tc_fence_after();
+                    uint32_t r[8];
+                    Q3A_TC_LD8(tm + lane_base + DTC_O_COL + (uint32_t)(g & 1) * 16u, r);
+                    tc_wait_ld();
+#pragma unroll
+                    for (int q = 0; q < GQA; q++)
+                        Oh[q] = fmaf(Oh[q], al_prev[q], __uint_as_float(r[q]) + __uint_as_float(r[q + GQA]));
+                };
+                for (int j = 0; j < ntiles; j++) {
+                    const int g = it0 + j, bf = g & 1;
+                    bool got = ok && mbar_wait(&sfull[bf], (uint32_t)(g >> 1) & 1u);
+                    got = __all_sync(FULL, got);
+                    uint32_t r[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
+                    if (got) {
+                        tc_fence_after();
+                        Q3A_TC_LD8(tm + lane_base + DTC_S_COL + (uint32_t)bf * 16u, r);
+                        tc_wait_ld();
+                    }
+                    const int key = lo_all + j * C::TILE + tid;
+                    const bool valid = got && key >= s.r0 && key < r_end;
+                    float sc[GQA], mx[GQA];
+#pragma unroll
+                    for (int q = 0; q < GQA; q++) {
+                        sc[q] = valid ? __uint_as_float(r[q]) + __uint_as_float(r[q + GQA]) : -INFINITY;
+                        mx[q] = sc[q];
+                    }
+#pragma unroll
+                    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+                        for (int q = 0; q < GQA; q++) mx[q] = fmaxf(mx[q], __shfl_xor_sync(FULL, mx[q], o));
+                    if (lane == 0)
+#pragma unroll
+                        for (int q = 0; q < GQA; q++) red[bf * 16 + warp * 4 + q] = mx[q];
+                    // the stage's maxima of all 4 warps; a failed wait anywhere
+                    // stops all 4 warps together
+                    if (!named_bar_red_and(3, 128, got)) {
+                        ok = false;
+                        break;
+                    }
+                    float al[GQA];
+#pragma unroll
+                    for (int q = 0; q < GQA; q++) {
+                        const float tmx = fmaxf(fmaxf(red[bf * 16 + q], red[bf * 16 + 4 + q]),
+                                                fmaxf(red[bf * 16 + 8 + q], red[bf * 16 + 12 + q]));
+                        const float mn = fmaxf(mh[q], tmx);
+                        const bool none = mn == -INFINITY;
+                        al[q] = none ? 1.0f : exp2f(mh[q] - mn);
+                        const float pq = none ? 0.0f : exp2f(sc[q] - mn);
+                        lsum[q] = fmaf(lsum[q], al[q], pq);
+                        mh[q] = mn;
+                        // P^T: high and low bf16 parts of p for this row
+                        const __nv_bfloat16 ph = __float2bfloat16_rn(pq);
+                        const __nv_bfloat16 pl = __float2bfloat16_rn(pq - __bfloat162float(ph));
+                        *reinterpret_cast<__nv_bfloat16*>(ptb + bf * C::OPB_BYTES + opb_offset(q, tid)) = ph;
+                        *reinterpret_cast<__nv_bfloat16*>(ptb + bf * C::OPB_BYTES + opb_offset(q + GQA, tid)) = pl;
+                    }
+                    fence_proxy_async_smem();
+                    tc_fence_before();
+                    mbar_arrive(&pfull[bf]);
+                    // the previous stage's O^T tile (its PV ran meanwhile)
+                    if (j > 0) fold(g - 1);
+#pragma unroll
+                    for (int q = 0; q < GQA; q++) al_prev[q] = al[q];
+                }
+                if (ok && ntiles > 0) fold(it0 + ntiles - 1);
+                float* lred = sW + C::W_LSUM;
+#pragma unroll
+                for (int q = 0; q < GQA; q++) {
+                    float v = lsum[q];
+#pragma unroll
+                    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(FULL, v, o);
+                    if (lane == 0) lred[warp * 4 + q] = v;
+                }
+                named_bar_sync(3, 128);
+#pragma unroll
+                for (int q = 0; q < GQA; q++) {
+                    const float L = lred[q] + lred[4 + q] + lred[8 + q] + lred[12 + q];
+                    sW[q * HD + tid] = Oh[q] / L;
+                    if (tid == q) sW[C::W_LSE + q] = mh[q] + log2f(L);
+                }
+                if (!ok) atomicExch(P.err, DEV_ERR_TIMEOUT);
+            }
+            it += ntiles;
+            tc_fence_before();
+            named_bar_sync(1, C::NCONS);
+            tc_fence_after();
+            o0 = sW[h * HD + d];
+            o1 = sW[h * HD + d + 1];
+            lse = sW[C::W_LSE + h];
+        } else {
+            float2 qr[GQA][8];
+            load_q_regs<KV>(sQ, lane, P.scale_log2e, qr);
+            float m[GQA] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+            float lpart = 0.0f;
+            float2 O[GQA][2];
+#pragma unroll
+            for (int hh = 0; hh < GQA; hh++) O[hh][0] = O[hh][1] = make_float2(0.0f, 0.0f);
+
+            bool dead = false;
+            for (int t0 = s.r0 & ~(DEC_BOX - 1); t0 < s.r1; t0 += C::TILE) {
+                const int stage = it % C::STAGES;
+                const uint32_t ph = (uint32_t)(it / C::STAGES) & 1u;
+                if (!mbar_wait(&full[stage], ph)) {
+                    atomicExch(P.err, DEV_ERR_TIMEOUT);
+                    dead = true;
+                    break;
+                }
+                const int lo = max(s.r0 - t0, 0);
+                const int hi = min(s.r1 - t0, C::TILE);
+                process_rows<KV>(sK + stage * C::TILE * HD, sV + stage * C::TILE * HD, lo, hi, warp,
+                                 lane, qr, m, lpart, O, pw);
+                if (lane == 0) mbar_arrive(&empty[stage]);
+                it++;
+            }
+            if (dead) return;
+            if (s.has_new) process_rows<KV>(sNewK, sNewV, 0, 1, warp, lane, qr, m, lpart, O, pw);
+
+            // ---- merge the 8 warp states of this range
+            float lsum = lpart;
+            lsum += __shfl_xor_sync(FULL, lsum, 4);
+            lsum += __shfl_xor_sync(FULL, lsum, 8);
+            lsum += __shfl_xor_sync(FULL, lsum, 16);
+            {
+                float* ws = sW + warp * C::WST;
+#pragma unroll
+                for (int hh = 0; hh < GQA; hh++)
+                    *reinterpret_cast<float4*>(ws + hh * HD + 4 * lane) =
+                        make_float4(O[hh][0].x, O[hh][0].y, O[hh][1].x, O[hh][1].y);
+                if (lane < 4) {
+                    ws[GQA * HD + lane] = sel4(m, lane);
+                    ws[GQA * HD + 4 + lane] = lsum;
+                }
+            }
+            named_bar_sync(1, C::NCONS);
+            float M = -INFINITY;
+#pragma unroll
+            for (int w = 0; w < C::CWARPS; w++) M = fmaxf(M, sW[w * C::WST + GQA * HD + h]);
+            float L = 0.0f;
+            o0 = 0.0f;
+            o1 = 0.0f;
+#pragma unroll
+            for (int w = 0; w < C::CWARPS; w++) {
+                const float mw = sW[w * C::WST + GQA * HD + h];
+                const float sc = (mw == -INFINITY) ? 0.0f : exp2f(mw - M);
+                L = fmaf(sW[w * C::WST + GQA * HD + 4 + h], sc, L);
+                o0 = fmaf(sW[w * C::WST + h * HD + d], sc, o0);
+                o1 = fmaf(sW[w * C::WST + h * HD + d + 1], sc, o1);
+            }
+            const float inv = 1.0f / L;
+            o0 *= inv;
+            o1 *= inv;
+            lse = M + log2f(L);
         }
-        const float inv = 1.0f / L;
-        o0 *= inv;
-        o1 *= inv;
-        float lse = M + log2f(L);
 
         bool write_out = true;
         if ((SPREAD && s.ncontrib > 1)) {
@@ -1000,20 +1380,39 @@ __global__ void __launch_bounds__(DecCfg<KV>::NTHREADS, 1)
         }
         named_bar_sync(1, C::NCONS);
     }
+    if constexpr (TC) {
+        // teardown: every MMA issued has completed (bounded wait) before the
+        // allocating warp frees tensor memory
+        if (warp == GQA) {
+            if (lane == 0) {
+                tc_commit(drain);
+                if (!mbar_wait(drain, 0u)) atomicExch(P.err, DEV_ERR_TIMEOUT);
+            }
+            __syncwarp();
+        }
+        tc_fence_before();
+        named_bar_sync(1, C::NCONS);
+        tc_fence_after();
+        if (warp == GQA) {
+            asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(*tmem_slot),
+                         "r"(DTC_COLS)
+                         : "memory");
+        }
+    }
 }
 
-template <typename KV, bool SPREAD>
+template <typename KV, bool SPREAD, bool TC>
 static cudaError_t launch_decode_t(const DecodeParams& p, const CUtensorMap& tmK,
                                    const CUtensorMap& tmV, cudaStream_t st) {
-    using C = DecCfg<KV>;
+    using C = DecCfg<KV, TC>;
     static bool attr_set = false;
     if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(decode_kernel<KV, SPREAD>,
+        cudaError_t e = cudaFuncSetAttribute(decode_kernel<KV, SPREAD, TC>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
         if (e != cudaSuccess) return e;
         attr_set = true;
     }
-    decode_kernel<KV, SPREAD><<<p.n_ctas, C::NTHREADS, C::SMEM, st>>>(tmK, tmV, p);
+    decode_kernel<KV, SPREAD, TC><<<p.n_ctas, C::NTHREADS, C::SMEM, st>>>(tmK, tmV, p);
     return cudaGetLastError();
 }
 
@@ -1021,11 +1420,14 @@ cudaError_t launch_decode(const DecodeParams& p, const CUtensorMap& tmK, const C
                           bool bf16, cudaStream_t st) {
     // the spread merge needs every range resident at once: piece mode only
     const bool spread = p.spread && p.n_pieces > 0;
-    if (bf16)
-        return spread ? launch_decode_t<__nv_bfloat16, true>(p, tmK, tmV, st)
-                      : launch_decode_t<__nv_bfloat16, false>(p, tmK, tmV, st);
-    return spread ? launch_decode_t<float, true>(p, tmK, tmV, st)
-                  : launch_decode_t<float, false>(p, tmK, tmV, st);
+    // bf16 caches are the context's paged caches in the operand layout and
+    // are consumed on the tensor cores; fp32 caches on the CUDA cores
+    if (bf16 != (p.tc != 0) || (p.tc && p.cache_mode != CACHE_PAGED)) return cudaErrorInvalidValue;
+    if (p.tc)
+        return spread ? launch_decode_t<__nv_bfloat16, true, true>(p, tmK, tmV, st)
+                      : launch_decode_t<__nv_bfloat16, false, true>(p, tmK, tmV, st);
+    return spread ? launch_decode_t<float, true, false>(p, tmK, tmV, st)
+                  : launch_decode_t<float, false, false>(p, tmK, tmV, st);
 }
 
 int decode_smem_bytes(bool bf16) {

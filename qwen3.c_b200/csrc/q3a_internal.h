@@ -84,6 +84,7 @@ struct DecodeParams {
     int n_ctas;
     int n_pieces;            // > 0: piece mode with n_ctas == n_pieces
     int spread;              // 1: piece-mode groups merge by the spread merge
+    int tc;                  // 1: tensor-core consumer (bf16 paged cache; 16-row swizzled maps)
     unsigned long long* words;   // spread merge: MAX_PIECES slots of PART_STRIDE tagged words
     unsigned* group_epoch;   // spread merge: call number per group [MAX_PIECES]
     const float* inv_freq;   // [64] RoPE inverse frequencies (host powf, reference formula)
@@ -147,6 +148,8 @@ cudaError_t launch_lse_combine(float* xb, const float* o_parts, size_t o_stride,
                                cudaStream_t st);
 
 struct PrefillParams {
+    const __nv_bfloat16* kcache;  // the context's paged bf16 caches
+    const __nv_bfloat16* vcache;
     float* out_f32;
     __nv_bfloat16* out_bf16;
     int n_tok;
@@ -162,8 +165,7 @@ struct PrefillParams {
     float scale_log2e;
     int* err;
 };
-cudaError_t launch_prefill(const PrefillParams& p, const CUtensorMap& tmQ,
-                           const CUtensorMap& tmK, const CUtensorMap& tmV, cudaStream_t st);
+cudaError_t launch_prefill(const PrefillParams& p, const CUtensorMap& tmQ, cudaStream_t st);
 int prefill_smem_bytes();
 
 uint64_t stream_key(uint64_t seed, uint64_t stream);

@@ -11,8 +11,9 @@
 //    Items are dealt to a persistent grid (one CTA per SM) in a snake order
 //    of decreasing causal length.
 //  * Warp 0 streams Q (3-D TMA, 128B swizzle) and 128-key K/V tiles of the
-//    paged bf16 cache (2-D TMA boxes of 64 keys x 64 dims, 128B swizzle)
-//    through a 2-stage ring.
+//    paged bf16 cache through a 2-stage ring.  The cache keeps 8-row blocks
+//    in the 128B-swizzled operand layout, so a 64-key run inside a page is
+//    one 16 KB bulk copy (cp.async.bulk) per tensor.
 //  * Warp 1 issues every MMA from one lane.  Per head t and key tile j:
 //    S_t = Q_t.K_j^T (M128 N128 K128, both operands in shared memory) into
 //    the head's 128 tensor-memory columns; once the softmax has replaced S_t
@@ -46,8 +47,7 @@ constexpr int KT = 128;        // keys per K/V tile
 constexpr int STAGES = 2;
 constexpr int NTHREADS = 384;  // 12 warps
 constexpr int Q_TILE_BYTES = QT * HD * 2;          // 32 KB: 2 dim-blocks of [128 rows][128 B]
-constexpr int KV_TILE_BYTES = KT * HD * 2;         // 32 KB: 2 dim-blocks of [128 keys][128 B]
-constexpr int DBLK = KT * 128;                     // bytes of one 64-dim block of a K/V tile
+constexpr int KV_TILE_BYTES = KT * HD * 2;         // 32 KB: 16 blocks of [2 dim-halves][8 keys][128 B]
 constexpr int OFF_Q = 0;                           // [2 heads][32 KB]
 constexpr int OFF_K = OFF_Q + 2 * Q_TILE_BYTES;    // [STAGES][32 KB]
 constexpr int OFF_V = OFF_K + STAGES * KV_TILE_BYTES;
@@ -166,8 +166,7 @@ __device__ __forceinline__ int pf_item_index(int c, int r, int G) {
 }
 
 __global__ void __launch_bounds__(pf::NTHREADS, 1)
-    prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                   const __grid_constant__ CUtensorMap tmV, const __grid_constant__ PrefillParams P) {
+    prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ PrefillParams P) {
     using namespace pf;
     extern __shared__ uint8_t smem_raw[];
     // 1024-byte alignment for the 128B-swizzle atoms
@@ -212,8 +211,6 @@ __global__ void __launch_bounds__(pf::NTHREADS, 1)
     }
     if (warp == 0 && lane == 0) {
         tma_prefetch_desc(&tmQ);
-        tma_prefetch_desc(&tmK);
-        tma_prefetch_desc(&tmV);
     }
     tc_fence_before();
     __syncthreads();
@@ -245,14 +242,18 @@ __global__ void __launch_bounds__(pf::NTHREADS, 1)
                     const int st = kv_it % STAGES;
                     const uint32_t ph = (uint32_t)(kv_it / STAGES) & 1u;
                     // a 128-key tile is two 64-key runs, each inside one page
-                    // (pages hold a multiple of 64 tokens)
-                    int rows[2];
+                    // (pages hold a multiple of 64 tokens); the cache's 8-row
+                    // blocks are already in the operand layout, so a run is
+                    // one 16 KB bulk copy per tensor
+                    long long rows[2];
                     for (int hf = 0; hf < 2; hf++) {
-                        const int t0 = j * KT + hf * 64;
                         const int pt = P.page_tokens;
+                        // the last tile may reach past the slot's pages; those
+                        // keys are after every query (masked, p = 0), so any
+                        // finite rows of the slot serve: its last 64
+                        const int t0 = min(j * KT + hf * 64, P.pages_per_seq * pt - 64);
                         const long long phys = (long long)P.slot * P.pages_per_seq + t0 / pt;
-                        rows[hf] = (int)((((long long)P.layer * P.nkv + it.g) * P.n_pages + phys) * pt +
-                                         (t0 % pt));
+                        rows[hf] = (((long long)P.layer * P.nkv + it.g) * P.n_pages + phys) * pt + (t0 % pt);
                     }
                     if (kv_it >= STAGES && !pf_wait(&bars[B_KEMPTY + st], ph ^ 1u, abort_flag, P.err)) {
                         dead = true;
@@ -261,9 +262,8 @@ __global__ void __launch_bounds__(pf::NTHREADS, 1)
                     uint8_t* dk = smem + OFF_K + st * KV_TILE_BYTES;
                     mbar_arrive_expect_tx(&bars[B_KFULL + st], (uint32_t)KV_TILE_BYTES);
                     for (int hf = 0; hf < 2; hf++)
-                        for (int db = 0; db < 2; db++)
-                            tma_load_2d(dk + db * DBLK + hf * 64 * 128, &tmK, &bars[B_KFULL + st], db * 64,
-                                        rows[hf], pol_kv);
+                        bulk_load(dk + hf * (KV_TILE_BYTES / 2), P.kcache + rows[hf] * HD, KV_TILE_BYTES / 2,
+                                  &bars[B_KFULL + st], pol_kv);
                     k_issued = kv_it + 1;
                     if (kv_it >= STAGES && !pf_wait(&bars[B_VEMPTY + st], ph ^ 1u, abort_flag, P.err)) {
                         dead = true;
@@ -272,9 +272,8 @@ __global__ void __launch_bounds__(pf::NTHREADS, 1)
                     uint8_t* dv = smem + OFF_V + st * KV_TILE_BYTES;
                     mbar_arrive_expect_tx(&bars[B_VFULL + st], (uint32_t)KV_TILE_BYTES);
                     for (int hf = 0; hf < 2; hf++)
-                        for (int db = 0; db < 2; db++)
-                            tma_load_2d(dv + db * DBLK + hf * 64 * 128, &tmV, &bars[B_VFULL + st], db * 64,
-                                        rows[hf], pol_kv);
+                        bulk_load(dv + hf * (KV_TILE_BYTES / 2), P.vcache + rows[hf] * HD, KV_TILE_BYTES / 2,
+                                  &bars[B_VFULL + st], pol_kv);
                     v_issued = kv_it + 1;
                 }
             }
@@ -300,7 +299,8 @@ __global__ void __launch_bounds__(pf::NTHREADS, 1)
                 for (int kk = 0; kk < HD / 16; kk++) {
                     const uint32_t koff = (kk & 3) * 32;  // 16 bf16 along K in a 128-byte row
                     const uint64_t da = smem_desc(qb + (kk >> 2) * (QT * 128) + koff, 16, 1024);
-                    const uint64_t db = smem_desc(kb + (kk >> 2) * DBLK + koff, 16, 1024);
+                    // K: 8-key groups 2048 B apart, dim-halves 1024 B
+                    const uint64_t db = smem_desc(kb + (kk >> 2) * 1024 + koff, 16, 2048);
                     tc_mma_ss(d, da, db, IDESC_S, kk > 0 ? 1u : 0u);
                 }
                 tc_commit(&bars[B_SFULL + t]);
@@ -357,9 +357,10 @@ __global__ void __launch_bounds__(pf::NTHREADS, 1)
                             for (int k4 = 0; k4 < KT / 32; k4++) {
                                 // A = P columns [8kk, 8kk+8) (16 keys, bf16
                                 // pairs); B = V rows [16kk, 16kk+16),
-                                // MN-major, the two 64-dim blocks DBLK apart
+                                // MN-major: dim-halves 1024 B apart, 8-key
+                                // groups 2048 B apart
                                 const int kk = hf * (KT / 32) + k4;
-                                const uint64_t db = smem_desc(vb + kk * 16 * 128, DBLK, 1024);
+                                const uint64_t db = smem_desc(vb + kk * 4096, 1024, 2048);
                                 tc_mma_ts(d, pa + kk * 8, db, IDESC_PV, (j > 0 || kk > 0) ? 1u : 0u);
                             }
                         }
@@ -583,8 +584,7 @@ __global__ void __launch_bounds__(pf::NTHREADS, 1)
     }
 }
 
-cudaError_t launch_prefill(const PrefillParams& p, const CUtensorMap& tmQ, const CUtensorMap& tmK,
-                           const CUtensorMap& tmV, cudaStream_t st) {
+cudaError_t launch_prefill(const PrefillParams& p, const CUtensorMap& tmQ, cudaStream_t st) {
     static bool attr_set = false;
     if (!attr_set) {
         cudaError_t e = cudaFuncSetAttribute(prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -599,7 +599,7 @@ cudaError_t launch_prefill(const PrefillParams& p, const CUtensorMap& tmQ, const
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
     const int grid = n_items < nsm ? n_items : nsm;
-    prefill_kernel<<<grid, pf::NTHREADS, pf::SMEM, st>>>(tmQ, tmK, tmV, p);
+    prefill_kernel<<<grid, pf::NTHREADS, pf::SMEM, st>>>(tmQ, p);
     return cudaGetLastError();
 }
 

@@ -55,8 +55,9 @@ __global__ void __launch_bounds__(ROWS_PER_BLOCK * 32)
     const int pt = P.page_tokens;
     const long long phys = (long long)P.slot * P.pages_per_seq + pos / pt;
     const long long row = (((long long)P.layer * P.nkv + kvh) * P.n_pages + phys) * pt + pos % pt;
-    KV* kd = reinterpret_cast<KV*>(P.kcache) + row * HD + 4 * lane;
-    KV* vd = reinterpret_cast<KV*>(P.vcache) + row * HD + 4 * lane;
+    // dims 4*lane .. 4*lane+3 are contiguous in either layout
+    KV* kd = reinterpret_cast<KV*>(P.kcache) + kv_index<KV>(row, 4 * lane);
+    KV* vd = reinterpret_cast<KV*>(P.vcache) + kv_index<KV>(row, 4 * lane);
     kd[0] = from_f32<KV>(k4[0]);
     kd[1] = from_f32<KV>(k4[1]);
     kd[2] = from_f32<KV>(k4[2]);
@@ -81,8 +82,8 @@ __global__ void kv_read_kernel(const __grid_constant__ AppendParams P, float* __
     const long long phys = (long long)P.slot * P.pages_per_seq + pos / pt;
     const long long row = (((long long)P.layer * P.nkv + kvh) * P.n_pages + phys) * pt + pos % pt;
     const size_t dst = (size_t)tok * P.nkv * HD + (size_t)kvh * HD + d;
-    ko[dst] = to_f32<KV>(reinterpret_cast<const KV*>(P.kcache)[row * HD + d]);
-    vo[dst] = to_f32<KV>(reinterpret_cast<const KV*>(P.vcache)[row * HD + d]);
+    ko[dst] = to_f32<KV>(reinterpret_cast<const KV*>(P.kcache)[kv_index<KV>(row, d)]);
+    vo[dst] = to_f32<KV>(reinterpret_cast<const KV*>(P.vcache)[kv_index<KV>(row, d)]);
 }
 
 __global__ void __launch_bounds__(ROWS_PER_BLOCK * 32)
