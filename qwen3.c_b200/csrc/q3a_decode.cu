@@ -935,6 +935,7 @@ __global__ void __launch_bounds__(DecCfg<KV, TC>::NTHREADS, 1)
             const int hi_all = (r_end + DEC_BOX - 1) & ~(DEC_BOX - 1);
             const int ntiles = r_end > lo_all ? (r_end - lo_all + C::TILE - 1) / C::TILE : 0;
             const int it0 = it;
+            const bool direct = SPREAD && s.ncontrib > 1;
             if (warp == GQA) {
                 // ================================== MMA issuer (one thread)
                 if (lane == 0 && ntiles > 0) {
@@ -1085,7 +1086,7 @@ __global__ void __launch_bounds__(DecCfg<KV, TC>::NTHREADS, 1)
 #pragma unroll
                     for (int q = 0; q < GQA; q++) al_prev[q] = al[q];
                 }
-                if (ok && ntiles > 0) fold(it0 + ntiles - 1);
+                // row sums over the 128 threads while the last PV runs
                 float* lred = sW + C::W_LSUM;
 #pragma unroll
                 for (int q = 0; q < GQA; q++) {
@@ -1095,21 +1096,37 @@ __global__ void __launch_bounds__(DecCfg<KV, TC>::NTHREADS, 1)
                     if (lane == 0) lred[warp * 4 + q] = v;
                 }
                 named_bar_sync(3, 128);
+                if (ok && ntiles > 0) fold(it0 + ntiles - 1);
+                // a spread-merged range stores its words from here (thread
+                // tid holds dimension tid of the 4 heads); otherwise the
+                // outputs go through shared memory to the 256-thread layout
+                unsigned long long* mine = P.words + (size_t)s.slot * PART_STRIDE;
+                const unsigned tag = (((unsigned)misc[1] + 1u) << 8) | ((unsigned)s.grp & 0xFFu);
 #pragma unroll
                 for (int q = 0; q < GQA; q++) {
                     const float L = lred[q] + lred[4 + q] + lred[8 + q] + lred[12 + q];
-                    sW[q * HD + tid] = Oh[q] / L;
-                    if (tid == q) sW[C::W_LSE + q] = mh[q] + log2f(L);
+                    const float oq = Oh[q] / L, lq = mh[q] + log2f(L);
+                    if (direct) {
+                        st_word_gpu(mine + q * HD + tid, oq, tag);
+                        if (tid == q) st_word_gpu(mine + GQA * HD + q, lq, tag);
+                    } else {
+                        sW[q * HD + tid] = oq;
+                        if (tid == q) sW[C::W_LSE + q] = lq;
+                    }
                 }
                 if (!ok) atomicExch(P.err, DEV_ERR_TIMEOUT);
             }
             it += ntiles;
-            tc_fence_before();
-            named_bar_sync(1, C::NCONS);
-            tc_fence_after();
-            o0 = sW[h * HD + d];
-            o1 = sW[h * HD + d + 1];
-            lse = sW[C::W_LSE + h];
+            if (!direct) {
+                tc_fence_before();
+                named_bar_sync(1, C::NCONS);
+                tc_fence_after();
+                o0 = sW[h * HD + d];
+                o1 = sW[h * HD + d + 1];
+                lse = sW[C::W_LSE + h];
+            } else {
+                o0 = o1 = lse = 0.0f;  // unused: the words are stored
+            }
         } else {
             float2 qr[GQA][8];
             load_q_regs<KV>(sQ, lane, P.scale_log2e, qr);
@@ -1185,10 +1202,12 @@ __global__ void __launch_bounds__(DecCfg<KV, TC>::NTHREADS, 1)
             // resident).  The tag is (call number of the group << 8 | group).
             const unsigned gep = (unsigned)misc[1] + 1u;
             const unsigned tag = (gep << 8) | ((unsigned)s.grp & 0xFFu);
-            unsigned long long* mine = P.words + (size_t)s.slot * PART_STRIDE;
-            st_word_gpu(mine + h * HD + d, o0, tag);
-            st_word_gpu(mine + h * HD + d + 1, o1, tag);
-            if ((tid & 63) == 0) st_word_gpu(mine + GQA * HD + h, lse, tag);
+            if constexpr (!TC) {  // the tensor-core softmax threads stored them
+                unsigned long long* mine = P.words + (size_t)s.slot * PART_STRIDE;
+                st_word_gpu(mine + h * HD + d, o0, tag);
+                st_word_gpu(mine + h * HD + d + 1, o1, tag);
+                if ((tid & 63) == 0) st_word_gpu(mine + GQA * HD + h, lse, tag);
+            }
             const int k = s.ncontrib, i = s.slot - s.slot0;
             const int v0 = i * (GQA * HD) / k, nv = (i + 1) * (GQA * HD) / k - v0;
             int tpv = 32;
