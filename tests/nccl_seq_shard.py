@@ -1,4 +1,4 @@
-"""Worker of test_shard_gpu.py::test_sequence_shards_over_nccl_two_gpus, run
+"""Worker of test_shard_gpu.py::test_sequence_shards_over_gpus, run
 under torchrun (one process per GPU): a 20000-token bf16 sequence split over
 the ranks, one decode step through shard.SeqShardDecode (q3a_attn_partial,
 NCCL all-gather, q3a_lse_combine_packed; or, with SHARD_MODE=peer, the

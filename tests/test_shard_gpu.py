@@ -204,22 +204,23 @@ def _free_port():
     return port
 
 
+@pytest.mark.parametrize("world", [2, 4, 8])
 @pytest.mark.parametrize("mode", ["nccl", "peer"])
-def test_sequence_shards_over_nccl_two_gpus(tmp_path, mode):
-    """Two ranks launched the way bench.py --gpus 2 is (torchrun, one process
-    per GPU); the exchange is an NCCL all-gather or the peer-memory stores of
-    q3a_attn_seqshard; each rank checks its combined xb against the oracle
-    and writes the error to a file."""
+def test_sequence_shards_over_gpus(tmp_path, mode, world):
+    """`world` ranks launched the way bench.py --gpus N is (torchrun, one
+    process per GPU); the exchange is an NCCL all-gather or the peer-memory
+    stores of q3a_attn_seqshard; each rank checks its combined xb against the
+    oracle and writes the error to a file."""
     import subprocess
     import torch
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs two GPUs")
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     env = dict(os.environ, NCCL_NVLS_ENABLE="0", SHARD_TEST_OUT=str(tmp_path), SHARD_MODE=mode)
-    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2",
-           "--master-addr", "127.0.0.1", "--master-port", str(_free_port()),
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node",
+           str(world), "--master-addr", "127.0.0.1", "--master-port", str(_free_port()),
            os.path.join(ROOT, "tests", "nccl_seq_shard.py")]
     r = subprocess.run(cmd, env=env, timeout=240, capture_output=True, text=True)
     assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
-    for rank in range(2):
+    for rank in range(world):
         err = float(open(os.path.join(tmp_path, f"rank{rank}.txt")).read())
         assert err <= TOL_BF16_ABS, f"rank {rank}: max-abs {err}"
