@@ -290,6 +290,12 @@ def prefill_run(args, torch, dev, local, seed, world, rank=0):
             if gather is not None:
                 gather(out[l])
 
+    def step_sharded_out():
+        # the same launches without the all-gather: each rank's output keeps
+        # its own heads (the layout a head-sharded o-projection consumes)
+        for l in range(N_LAYERS):
+            ctx.prefill_attn(out[l], q3attn.OUT_BF16, qs[l], 0, l, 0, S)
+
     with torch.cuda.stream(stream):
         for _ in range(args.warmup):
             step()
@@ -299,10 +305,13 @@ def prefill_run(args, torch, dev, local, seed, world, rank=0):
     n0 = ctx.launch_count()
     t_ms, clocks = time_graph(torch, dev, local, stream, step, K, world)
     launches = ctx.launch_count() - n0
+    t_so = None
+    if world > 1:
+        t_so, _ = time_graph(torch, dev, local, stream, step_sharded_out, K, world)
     ctx.check_device_error()
     ctx.close()
     return {"t_ms": t_ms, "launches": launches, "kernel_us": 1000.0 * t_ms / launches,
-            "clocks": clocks, "steps": K}
+            "clocks": clocks, "steps": K, "t_ms_sharded_out": t_so}
 
 
 def time_graph(torch, dev, local, stream, step, K, world):
@@ -732,6 +741,14 @@ def main():
                            "parallelism": f"kvhead{world}" if world > 1 else "single",
                            "scaling": "strong",
                            "clocks": pr["clocks"], "gpu_launches": pr["launches"]}
+        if pr["t_ms_sharded_out"] is not None:
+            # kernel time with each rank's output left head-sharded (no gather)
+            t_so = max_over_ranks(pr["t_ms_sharded_out"], world, dev)
+            line["prefill"]["sharded_out"] = {
+                "us_per_layer": t_so * 1000.0 / pr["launches"],
+                "value": fl * pr["launches"] / (t_so / 1000.0) / 1e12, "unit": "TFLOP/s",
+                "note": "same launches without the all-gather of the output head slices"}
+            line["gpu_launches"] += pr["launches"]
         line["gpu_launches"] += pr["launches"]
     if not args.no_variants:
         lc = long_ctx_run(args, torch, dev, local, world, rank)

@@ -91,6 +91,10 @@ struct q3a_ctx {
     int* counters = nullptr;
     unsigned long long* words = nullptr;  // spread-merge slots (tagged words)
     unsigned* group_epoch = nullptr;      // spread-merge call number per group
+    float* pf_part = nullptr;             // prefill split partials (growable)
+    size_t pf_part_floats = 0;
+    int pf_key_tok = -1, pf_key_pos = -1; // prompt shape of the cached split choice
+    int pf_nsplit = 1, pf_cap = 1;
     int* err = nullptr;
     cudaStream_t own_stream = nullptr;
     cudaStream_t stream = nullptr;
@@ -187,6 +191,7 @@ static void destroy_ctx(q3a_ctx* c) {
     cudaFree(c->counters);
     cudaFree(c->words);
     cudaFree(c->group_epoch);
+    cudaFree(c->pf_part);
     cudaFree(c->err);
     cudaFree(c->d_inv_freq);
     cudaFree(c->d_stage);
@@ -1117,10 +1122,86 @@ extern "C" int q3a_prefill_attn(q3a_ctx* c, void* out, int out_dtype, const void
     pp.n_pages = c->n_pages;
     pp.scale_log2e = (float)(1.4426950408889634 / sqrt((double)HD));
     pp.err = c->err;
+    // Long causal items may be split over several CTAs (KV-head-sharded
+    // contexts, short prompts leave many SMs idle behind the longest item).
+    // The part size is chosen by replaying the kernel's snake deal of chunks
+    // on the host with a cost model measured on B200 (per chunk ~2 us of Q
+    // load and pipeline start, ~2.3 us per key tile of a head pair, ~3 us to
+    // write a split part, ~5 us for the combine launch); the decision is
+    // cached per prompt shape.  At most 8 parts, partial scratch <= 1 GiB.
+    int pf_launches = 1;
+    {
+        const int n_qt = (n_tok + 127) / 128;
+        const int per_qt = c->nkv * 2;
+        const long long n_items = (long long)n_qt * per_qt;
+        std::vector<int> nj_of(n_qt);
+        int max_nj = 0;
+        for (int qt = 0; qt < n_qt; qt++) {
+            const int last_q = std::min(pos0 + (qt + 1) * 128, pos0 + n_tok) - 1;
+            nj_of[qt] = last_q / 128 + 1;
+            max_nj = std::max(max_nj, nj_of[qt]);
+        }
+        int nsplit = 1, cap = max_nj;
+        if (c->pf_key_tok == n_tok && c->pf_key_pos == pos0) {
+            nsplit = c->pf_nsplit;
+            cap = c->pf_cap;
+        } else {
+            const int G = std::min<long long>(c->num_sms, n_items * 8);
+            auto cost = [&](int ns, int cp) {
+                std::vector<double> load(G, 0.0);
+                const long long n_chunks = n_items * ns;
+                for (int cc = 0; cc < G; cc++) {
+                    for (long long r = 0;; r++) {
+                        const long long x = r * G + ((r & 1) ? (G - 1 - cc) : cc);
+                        if (x >= n_chunks) break;
+                        const long long item = x / ns;
+                        const int nj = nj_of[n_qt - 1 - (int)(item / per_qt)];
+                        const int k = std::min(ns, (nj + cp - 1) / cp);
+                        const int part = (int)(x % ns);
+                        if (part >= k) continue;
+                        const int tiles = (part + 1) * nj / k - part * nj / k;
+                        load[cc] += 2.0 + 2.3 * tiles + (k > 1 ? 3.0 : 0.0);
+                    }
+                }
+                return *std::max_element(load.begin(), load.end()) + (ns > 1 ? 5.0 : 0.0);
+            };
+            double best = cost(1, max_nj);
+            for (int cp : {8, 6, 5, 4, 3, 2}) {
+                const int ns = (max_nj + cp - 1) / cp;
+                if (cp >= max_nj || ns > 8) continue;
+                if ((double)n_items * ns * 2 * PF_PART_FLOATS * 4 > (double)(1LL << 30)) continue;
+                const double cc = cost(ns, cp);
+                if (cc < 0.9 * best) {  // split only for a clear gain
+                    best = cc;
+                    nsplit = ns;
+                    cap = cp;
+                }
+            }
+            c->pf_key_tok = n_tok;
+            c->pf_key_pos = pos0;
+            c->pf_nsplit = nsplit;
+            c->pf_cap = cap;
+        }
+        if (nsplit > 1) {
+            const size_t need = (size_t)n_items * nsplit * 2 * PF_PART_FLOATS;
+            if (need > c->pf_part_floats) {
+                cudaFree(c->pf_part);
+                c->pf_part = nullptr;
+                c->pf_part_floats = 0;
+                if (cudaMalloc(&c->pf_part, need * 4) != cudaSuccess)
+                    return fail(Q3A_ERR_OOM, "prefill split scratch of %zu bytes", need * 4);
+                c->pf_part_floats = need;
+            }
+            pf_launches = 2;  // + prefill_combine_kernel
+        }
+        pp.nsplit = nsplit;
+        pp.part_tiles = std::max(cap, 1);
+        pp.part = c->pf_part;
+    }
     pp.kcache = reinterpret_cast<const __nv_bfloat16*>(c->kcache);
     pp.vcache = reinterpret_cast<const __nv_bfloat16*>(c->vcache);
     CUDA_TRY(launch_prefill(pp, tq, c->stream));
-    c->launches++;
+    c->launches += pf_launches;
     if (c->cfg.ptr_mode == Q3A_PTR_HOST) {
         CUDA_TRY(cudaMemcpyAsync(out, dout, out_bytes, cudaMemcpyDeviceToHost, c->stream));
         CUDA_TRY(cudaStreamSynchronize(c->stream));

@@ -195,6 +195,20 @@ __device__ __forceinline__ void rope_pair(float& v0, float& v1, int pos, float i
     v1 = b;
 }
 
+// Named barrier that also returns the AND of a predicate over its threads.
+__device__ __forceinline__ bool named_bar_red_and(int id, int nthreads, bool v) {
+    int r;
+    asm volatile(
+        "{\n\t.reg .pred pi, po;\n\t"
+        "setp.ne.b32 pi, %1, 0;\n\t"
+        "barrier.cta.red.and.pred po, %2, %3, pi;\n\t"
+        "selp.b32 %0, 1, 0, po;\n\t}"
+        : "=r"(r)
+        : "r"((int)v), "r"(id), "r"(nthreads)
+        : "memory");
+    return r != 0;
+}
+
 // Element index of (row R, dim d) in a context's paged cache.  fp32 rows are
 // plain 128-float rows.  bf16 rows are kept in blocks of 8 rows (2 KB, the
 // same bytes the 8 rows would occupy row by row): [2 dim-halves][8 rows][64

@@ -110,20 +110,6 @@ constexpr uint32_t DTC_S_COL = 0, DTC_O_COL = 32;
 constexpr uint32_t IDESC_DS = (1u << 4) | (1u << 7) | (1u << 10) | ((16u >> 3) << 17) | ((128u >> 4) << 24);
 constexpr uint32_t IDESC_DPV = IDESC_DS | (1u << 15);
 
-// Named barrier that also returns the AND of a predicate over its threads.
-__device__ __forceinline__ bool named_bar_red_and(int id, int nthreads, bool v) {
-    int r;
-    asm volatile(
-        "{\n\t.reg .pred pi, po;\n\t"
-        "setp.ne.b32 pi, %1, 0;\n\t"
-        "barrier.cta.red.and.pred po, %2, %3, pi;\n\t"
-        "selp.b32 %0, 1, 0, po;\n\t}"
-        : "=r"(r)
-        : "r"((int)v), "r"(id), "r"(nthreads)
-        : "memory");
-    return r != 0;
-}
-
 __device__ __forceinline__ void fence_proxy_async_global() {
     asm volatile("fence.proxy.async.global;" ::: "memory");
 }

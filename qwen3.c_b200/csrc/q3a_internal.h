@@ -164,7 +164,15 @@ struct PrefillParams {
     int n_pages;
     float scale_log2e;
     int* err;
+    // split of long causal items: item i (a 128-row query tile of one head
+    // pair) with nj key tiles is cut into min(nsplit, ceil(nj/part_tiles))
+    // parts of whole key tiles; every part of a split item writes a
+    // normalised partial (o, lse) and prefill_combine_kernel merges them.
+    int nsplit;              // most parts of an item (1: nothing is split)
+    int part_tiles;          // key tiles per part, at most
+    float* part;             // [items][nsplit][2 heads][PF_PART_FLOATS]
 };
+constexpr int PF_PART_FLOATS = 128 * 128 + 128;  // o [128 rows][128] + lse [128]
 cudaError_t launch_prefill(const PrefillParams& p, const CUtensorMap& tmQ, cudaStream_t st);
 int prefill_smem_bytes();
 

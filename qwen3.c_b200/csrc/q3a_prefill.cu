@@ -142,9 +142,11 @@ __device__ __forceinline__ bool pf_wait(uint64_t* bar, uint32_t parity, volatile
     return true;
 }
 
-// Work item i (in decreasing-length order) -> (query tile, kv head, pair).
+// Work item i (in decreasing-length order) -> (query tile, kv head, pair);
+// a chunk is the part of an item over key tiles [j0, j1).
 struct PfItem {
     int qt, g, hp, nj;
+    int item, part, nparts, j0, j1;
 };
 
 __device__ __forceinline__ PfItem pf_item(const PrefillParams& P, int i) {
@@ -160,11 +162,39 @@ __device__ __forceinline__ PfItem pf_item(const PrefillParams& P, int i) {
     return it;
 }
 
-// The r-th item of CTA c in snake order.
+// Chunk x: part x % nsplit of item x / nsplit (empty, j0 == j1, when the
+// item has fewer parts).  Without SPLIT every item is one chunk.
+template <bool SPLIT>
+__device__ __forceinline__ PfItem pf_chunk(const PrefillParams& P, int x) {
+    if constexpr (!SPLIT) {
+        PfItem it = pf_item(P, x);
+        it.item = x;
+        it.part = 0;
+        it.nparts = 1;
+        it.j0 = 0;
+        it.j1 = it.nj;
+        return it;
+    }
+    PfItem it = pf_item(P, x / P.nsplit);
+    it.item = x / P.nsplit;
+    it.part = x % P.nsplit;
+    it.nparts = min(P.nsplit, (it.nj + P.part_tiles - 1) / P.part_tiles);
+    it.j0 = it.j1 = 0;
+    if (it.part < it.nparts) {
+        it.j0 = it.part * it.nj / it.nparts;
+        it.j1 = (it.part + 1) * it.nj / it.nparts;
+    }
+    return it;
+}
+
+// The r-th chunk of CTA c in snake order.
 __device__ __forceinline__ int pf_item_index(int c, int r, int G) {
     return r * G + ((r & 1) ? (G - 1 - c) : c);
 }
 
+// SPLIT: long items are cut into parts merged by the last one to finish (a
+// separate instantiation, so the unsplit kernel keeps its own code).
+template <bool SPLIT>
 __global__ void __launch_bounds__(pf::NTHREADS, 1)
     prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ PrefillParams P) {
     using namespace pf;
@@ -181,6 +211,7 @@ __global__ void __launch_bounds__(pf::NTHREADS, 1)
     const int c = blockIdx.x, G = gridDim.x;
     const int n_qt = (P.n_tok + QT - 1) / QT;
     const int n_items = n_qt * P.nkv * 2;
+    const int n_chunks = SPLIT ? n_items * P.nsplit : n_items;
 
     if (tid == 0) {
         mbar_init(&bars[B_QFULL], 1);
@@ -226,8 +257,9 @@ __global__ void __launch_bounds__(pf::NTHREADS, 1)
             bool dead = false;
             for (int r = 0; !dead; r++) {
                 const int i = pf_item_index(c, r, G);
-                if (i >= n_items) break;
-                const PfItem it = pf_item(P, i);
+                if (i >= n_chunks) break;
+                const PfItem it = pf_chunk<SPLIT>(P, i);
+                if (it.j0 == it.j1) continue;
                 if (item_it > 0 && !pf_wait(&bars[B_QEMPTY], (item_it - 1) & 1, abort_flag, P.err))
                     break;
                 mbar_arrive_expect_tx(&bars[B_QFULL], 2u * Q_TILE_BYTES);
@@ -238,7 +270,7 @@ __global__ void __launch_bounds__(pf::NTHREADS, 1)
                     tma_load_3d(dq + QT * 128, &tmQ, &bars[B_QFULL], 64, h, it.qt * QT, pol_q);
                 }
                 item_it++;
-                for (int j = 0; j < it.nj; j++, kv_it++) {
+                for (int j = it.j0; j < it.j1; j++, kv_it++) {
                     const int st = kv_it % STAGES;
                     const uint32_t ph = (uint32_t)(kv_it / STAGES) & 1u;
                     // a 128-key tile is two 64-key runs, each inside one page
@@ -307,9 +339,10 @@ __global__ void __launch_bounds__(pf::NTHREADS, 1)
             };
             for (int r = 0; !dead; r++) {
                 const int i = pf_item_index(c, r, G);
-                if (i >= n_items) break;
-                const PfItem it = pf_item(P, i);
-                const int nj = it.nj;
+                if (i >= n_chunks) break;
+                const PfItem it = pf_chunk<SPLIT>(P, i);
+                const int nj = it.j1 - it.j0;  // key tiles of this chunk
+                if (nj == 0) continue;
                 if (!pf_wait(&bars[B_QFULL], item_it & 1, abort_flag, P.err)) break;
                 {
                     // S(0) of both heads; head t's columns still hold P of the
@@ -408,13 +441,17 @@ __global__ void __launch_bounds__(pf::NTHREADS, 1)
         int s_it = 0, item_it = 0;
         for (int r = 0;; r++) {
             const int i = pf_item_index(c, r, G);
-            if (i >= n_items) break;
-            const PfItem it = pf_item(P, i);
+            if (i >= n_chunks) break;
+            const PfItem it = pf_chunk<SPLIT>(P, i);
+            if (it.j0 == it.j1) continue;
             const int q_abs = P.pos0 + it.qt * QT + row;  // this row's position
             float m_ref = -INFINITY, l_sum = 0.0f;
             bool dead = false;
-            for (int j = 0; j < it.nj; j++) {
-                if (!pf_wait(&bars[B_SFULL + t], (uint32_t)s_it & 1u, abort_flag, P.err)) {
+            for (int j = it.j0; j < it.j1; j++) {
+                // the warp leaves together (its lanes later meet in warp
+                // barriers and shuffles)
+                const bool got = pf_wait(&bars[B_SFULL + t], (uint32_t)s_it & 1u, abort_flag, P.err);
+                if (SPLIT ? !__all_sync(FULL, got) : !got) {
                     dead = true;
                     break;
                 }
@@ -460,7 +497,10 @@ __global__ void __launch_bounds__(pf::NTHREADS, 1)
                 // first half of PV runs while the second half is computed.
                 // One pair in EXP2_POLY_EVERY takes the polynomial 2^x on the
                 // FMA pipe instead of the MUFU unit.
-                const float2 nm2 = make_float2(-m_ref, -m_ref);
+                // (a row with no visible key so far -- only in a chunk that
+                // starts after the row's position -- gets p = 0, not NaN)
+                const float nm = (SPLIT && m_ref == -INFINITY) ? 0.0f : -m_ref;
+                const float2 nm2 = make_float2(nm, nm);
                 float2 ps2[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f),
                                  make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
@@ -511,19 +551,87 @@ __global__ void __launch_bounds__(pf::NTHREADS, 1)
             // stages 32 rows x 32 columns at a time in its own shared-memory
             // buffer (16-byte chunks XOR-swizzled by row) and writes them
             // back row-contiguous, so every global store fills whole sectors.
-            if (!pf_wait(&bars[B_OFULL + t], (uint32_t)item_it & 1u, abort_flag, P.err)) break;
+            {
+                const bool got = pf_wait(&bars[B_OFULL + t], (uint32_t)item_it & 1u, abort_flag, P.err);
+                if (SPLIT ? !__all_sync(FULL, got) : !got) break;
+            }
             tc_fence_after();
             const int srow0 = it.qt * QT + rw * 32;  // prompt row of lane 0
             const int h = (P.kv0 + it.g) * GQA + 2 * it.hp + t;
-            const float inv = 1.0f / l_sum;
             uint8_t* stg = smem + OFF_STG + (warp - 4) * STG_BYTES;
-#pragma unroll 1
-            for (int q = 0; q < 4; q++) {
-                uint32_t orr[32];
-                Q3A_TC_LD32(tl + COL_O + 32 * q, orr, 0);
-                tc_wait_ld();
+            // columns [32q, 32q+32) of this row, orr (fp32 bits) x sc, to the output
+            auto emit = [&](int q, const uint32_t (&orr)[32], float sc) {
                 if (P.out_f32) {
                     // row: 32 fp32 = 8 chunks of 16 B
+#pragma unroll
+                    for (int c4 = 0; c4 < 8; c4++)
+                        *reinterpret_cast<float4*>(stg + lane * 128 + ((c4 ^ (lane & 7)) << 4)) =
+                            make_float4(__uint_as_float(orr[4 * c4]) * sc, __uint_as_float(orr[4 * c4 + 1]) * sc,
+                                        __uint_as_float(orr[4 * c4 + 2]) * sc,
+                                        __uint_as_float(orr[4 * c4 + 3]) * sc);
+                    __syncwarp();
+#pragma unroll
+                    for (int k = 0; k < 8; k++) {
+                        const int rr = 4 * k + (lane >> 3), c4 = lane & 7;
+                        const float4 x =
+                            *reinterpret_cast<const float4*>(stg + rr * 128 + ((c4 ^ (rr & 7)) << 4));
+                        if (srow0 + rr < P.n_tok)
+                            *reinterpret_cast<float4*>(P.out_f32 + ((size_t)(srow0 + rr) * P.hq_total + h) * HD +
+                                                       q * 32 + c4 * 4) = x;
+                    }
+                } else {
+                    // row: 32 bf16 = 4 chunks of 16 B
+#pragma unroll
+                    for (int c8 = 0; c8 < 4; c8++) {
+                        uint32_t w[4];
+#pragma unroll
+                        for (int e = 0; e < 4; e++) {
+                            __nv_bfloat162 b2 = __floats2bfloat162_rn(__uint_as_float(orr[8 * c8 + 2 * e]) * sc,
+                                                                      __uint_as_float(orr[8 * c8 + 2 * e + 1]) * sc);
+                            w[e] = *reinterpret_cast<uint32_t*>(&b2);
+                        }
+                        *reinterpret_cast<uint4*>(stg + lane * 128 + ((c8 ^ (lane & 7)) << 4)) =
+                            make_uint4(w[0], w[1], w[2], w[3]);
+                    }
+                    __syncwarp();
+#pragma unroll
+                    for (int k = 0; k < 4; k++) {
+                        const int rr = 8 * k + (lane >> 2), c8 = lane & 3;
+                        const uint4 x = *reinterpret_cast<const uint4*>(stg + rr * 128 + ((c8 ^ (rr & 7)) << 4));
+                        if (srow0 + rr < P.n_tok)
+                            *reinterpret_cast<uint4*>(P.out_bf16 + ((size_t)(srow0 + rr) * P.hq_total + h) * HD +
+                                                      q * 32 + c8 * 8) = x;
+                    }
+                }
+                __syncwarp();  // the staging buffer is rewritten by the next chunk
+            };
+            // a row that saw no visible key in this part (only possible in a
+            // part after the first) contributes nothing: o = 0, lse = -inf
+            const bool none = SPLIT && ((m_ref == -INFINITY) || !(l_sum > 0.0f));
+            const float inv = none ? 0.0f : 1.0f / l_sum;
+            if (!SPLIT || it.nparts == 1) {
+#pragma unroll 1
+                for (int q = 0; q < 4; q++) {
+                    uint32_t orr[32];
+                    Q3A_TC_LD32(tl + COL_O + 32 * q, orr, 0);
+                    tc_wait_ld();
+                    emit(q, orr, inv);
+                }
+            } else if constexpr (SPLIT) {
+                // split item: store this part's normalised (o, lse) rows for
+                // prefill_combine_kernel.  The rows move 32 x 32 at a time
+                // through the warp's staging buffer, so the global stores are
+                // row-contiguous (a thread-per-row store would touch 32 lines
+                // per instruction).
+                const size_t pstride = (size_t)2 * PF_PART_FLOATS;  // parts of an item
+                float* mine = P.part + ((size_t)it.item * P.nsplit + it.part) * pstride +
+                              (size_t)t * PF_PART_FLOATS;
+                const int r0w = rw * 32;  // this warp's first row of the tile
+#pragma unroll 1
+                for (int q = 0; q < 4; q++) {
+                    uint32_t orr[32];
+                    Q3A_TC_LD32(tl + COL_O + 32 * q, orr, 0);
+                    tc_wait_ld();
 #pragma unroll
                     for (int c4 = 0; c4 < 8; c4++)
                         *reinterpret_cast<float4*>(stg + lane * 128 + ((c4 ^ (lane & 7)) << 4)) =
@@ -534,37 +642,12 @@ __global__ void __launch_bounds__(pf::NTHREADS, 1)
 #pragma unroll
                     for (int k = 0; k < 8; k++) {
                         const int rr = 4 * k + (lane >> 3), c4 = lane & 7;
-                        const float4 v =
+                        *reinterpret_cast<float4*>(mine + (size_t)(r0w + rr) * HD + q * 32 + c4 * 4) =
                             *reinterpret_cast<const float4*>(stg + rr * 128 + ((c4 ^ (rr & 7)) << 4));
-                        if (srow0 + rr < P.n_tok)
-                            *reinterpret_cast<float4*>(P.out_f32 + ((size_t)(srow0 + rr) * P.hq_total + h) * HD +
-                                                       q * 32 + c4 * 4) = v;
-                    }
-                } else {
-                    // row: 32 bf16 = 4 chunks of 16 B
-#pragma unroll
-                    for (int c8 = 0; c8 < 4; c8++) {
-                        uint32_t w[4];
-#pragma unroll
-                        for (int e = 0; e < 4; e++) {
-                            __nv_bfloat162 b2 = __floats2bfloat162_rn(__uint_as_float(orr[8 * c8 + 2 * e]) * inv,
-                                                                      __uint_as_float(orr[8 * c8 + 2 * e + 1]) * inv);
-                            w[e] = *reinterpret_cast<uint32_t*>(&b2);
-                        }
-                        *reinterpret_cast<uint4*>(stg + lane * 128 + ((c8 ^ (lane & 7)) << 4)) =
-                            make_uint4(w[0], w[1], w[2], w[3]);
                     }
                     __syncwarp();
-#pragma unroll
-                    for (int k = 0; k < 4; k++) {
-                        const int rr = 8 * k + (lane >> 2), c8 = lane & 3;
-                        const uint4 v = *reinterpret_cast<const uint4*>(stg + rr * 128 + ((c8 ^ (rr & 7)) << 4));
-                        if (srow0 + rr < P.n_tok)
-                            *reinterpret_cast<uint4*>(P.out_bf16 + ((size_t)(srow0 + rr) * P.hq_total + h) * HD +
-                                                      q * 32 + c8 * 8) = v;
-                    }
                 }
-                __syncwarp();  // the staging buffer is rewritten by the next chunk
+                mine[128 * HD + row] = none ? -INFINITY : m_ref + log2f(l_sum);
             }
             // the next item's first P arrive (after this code in program
             // order, behind wait::ld and a before_thread_sync fence) is what
@@ -584,22 +667,98 @@ __global__ void __launch_bounds__(pf::NTHREADS, 1)
     }
 }
 
-cudaError_t launch_prefill(const PrefillParams& p, const CUtensorMap& tmQ, cudaStream_t st) {
+// Merge of the parts of split items: one warp per row (CTA = 8 rows of one
+// (item, head of its pair)), so every row's loads are in flight at once; a
+// row's 128 outputs are one coalesced load per part (lane l: columns
+// 4l..4l+3) weighted by 2^(lse_part - max).  CTAs of unsplit items return
+// at once.
+__global__ void __launch_bounds__(256)
+    prefill_combine_kernel(const __grid_constant__ PrefillParams P) {
+    const int item = blockIdx.x >> 5, t = (blockIdx.x >> 4) & 1, rg = blockIdx.x & 15;
+    const PfItem it = pf_item(P, item);
+    const int nparts = min(P.nsplit, (it.nj + P.part_tiles - 1) / P.part_tiles);
+    if (nparts <= 1) return;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const size_t pstride = (size_t)2 * PF_PART_FLOATS;
+    const float* base = P.part + (size_t)item * P.nsplit * pstride + (size_t)t * PF_PART_FLOATS;
+    const int h = (P.kv0 + it.g) * GQA + 2 * it.hp + t;
+    {
+        const int row = rg * 8 + warp;
+        const int srow = it.qt * pf::QT + row;
+        if (srow >= P.n_tok) return;
+        float lp[8], M = -INFINITY;
+        float4 x[8];
+#pragma unroll
+        for (int pp = 0; pp < 8; pp++) {
+            lp[pp] = -INFINITY;
+            x[pp] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (pp < nparts) {
+                const float* src = base + (size_t)pp * pstride;
+                lp[pp] = __ldcg(src + 128 * HD + row);
+                x[pp] = __ldcg(reinterpret_cast<const float4*>(src + (size_t)row * HD) + lane);
+            }
+            M = fmaxf(M, lp[pp]);
+        }
+        float W = 0.0f;
+        float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int pp = 0; pp < 8; pp++) {
+            const float w = (lp[pp] == -INFINITY) ? 0.0f : exp2f(lp[pp] - M);
+            W += w;
+            a.x = fmaf(w, x[pp].x, a.x);
+            a.y = fmaf(w, x[pp].y, a.y);
+            a.z = fmaf(w, x[pp].z, a.z);
+            a.w = fmaf(w, x[pp].w, a.w);
+        }
+        const float iw = W > 0.0f ? 1.0f / W : 0.0f;
+        a.x *= iw;
+        a.y *= iw;
+        a.z *= iw;
+        a.w *= iw;
+        const size_t o = ((size_t)srow * P.hq_total + h) * HD + 4 * lane;
+        if (P.out_f32) {
+            *reinterpret_cast<float4*>(P.out_f32 + o) = a;
+        } else {
+            __nv_bfloat162 b0 = __floats2bfloat162_rn(a.x, a.y), b1 = __floats2bfloat162_rn(a.z, a.w);
+            uint2 u;
+            u.x = *reinterpret_cast<uint32_t*>(&b0);
+            u.y = *reinterpret_cast<uint32_t*>(&b1);
+            *reinterpret_cast<uint2*>(P.out_bf16 + o) = u;
+        }
+    }
+}
+
+template <bool SPLIT>
+static cudaError_t set_prefill_attr() {
     static bool attr_set = false;
     if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             pf::SMEM);
+        cudaError_t e = cudaFuncSetAttribute(prefill_kernel<SPLIT>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, pf::SMEM);
         if (e != cudaSuccess) return e;
         attr_set = true;
     }
+    return cudaSuccess;
+}
+
+cudaError_t launch_prefill(const PrefillParams& p, const CUtensorMap& tmQ, cudaStream_t st) {
+    const bool split = p.nsplit > 1;
+    cudaError_t e = split ? set_prefill_attr<true>() : set_prefill_attr<false>();
+    if (e != cudaSuccess) return e;
     const int n_qt = (p.n_tok + pf::QT - 1) / pf::QT;
-    const int n_items = n_qt * p.nkv * 2;
+    const int n_chunks = n_qt * p.nkv * 2 * p.nsplit;
     int nsm = 0;
     int dev = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
-    const int grid = n_items < nsm ? n_items : nsm;
-    prefill_kernel<<<grid, pf::NTHREADS, pf::SMEM, st>>>(tmQ, p);
+    const int grid = n_chunks < nsm ? n_chunks : nsm;
+    if (split) {
+        prefill_kernel<true><<<grid, pf::NTHREADS, pf::SMEM, st>>>(tmQ, p);
+        e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+        prefill_combine_kernel<<<n_qt * p.nkv * 2 * 2 * 16, 256, 0, st>>>(p);
+    } else {
+        prefill_kernel<false><<<grid, pf::NTHREADS, pf::SMEM, st>>>(tmQ, p);
+    }
     return cudaGetLastError();
 }
 

@@ -154,3 +154,38 @@ def test_prefill_2048_matches_oracle_sampled_rows():
         ref = orc.attn_decode(q[r * qd:(r + 1) * qd].copy(), kc, vc, 0, int(r), HQ, KV_MUL, HD,
                               KV_DIM, S)
         assert max_abs(got[r], ref) <= TOL_BF16_ABS, f"row {r}"
+
+
+@pytest.mark.parametrize("nh,pos0,S", [(1, 0, 2048), (2, 0, 2048), (1, 100, 1948)])
+def test_prefill_split_items_match_oracle_sampled_rows(nh, pos0, S):
+    """Contexts holding 1 or 2 KV heads (the per-rank share of KV-head
+    sharding over 8 or 4 GPUs): the kernel cuts the long causal items into
+    parts merged by prefill_combine_kernel.  pos0 = 100 puts rows before the
+    start of later parts (rows that see no key in such a part).  Sampled rows
+    of the context's heads against the oracle."""
+    torch = _torch()
+    dev = torch.device("cuda:0")
+    n_tok = pos0 + S
+    kc, vc, _, _ = orc.make_cache(5000 + nh, 0, n_tok, HKV, HD, n_tok, bf16=True)
+    _, q = prepped_q(5000 + nh, pos0, S)
+    h0 = 2  # first KV head of the context
+    c0, c1 = h0 * KV_MUL * HD, (h0 + nh) * KV_MUL * HD
+    rows = np.array([0, 1, 27, 28, 127, 128, 129, 700, 1023, 1500, S - 2, S - 1])
+    with q3attn.Context(n_layers=1, max_seq=n_tok, kv_dtype=q3attn.KV_BF16,
+                        ptr_mode=q3attn.PTR_DEVICE, kv_head_begin=h0, kv_head_count=nh) as ctx:
+        ctx.kv_load(0, 0, 0, n_tok, torch.from_numpy(kc).to(dev), torch.from_numpy(vc).to(dev))
+        out = torch.zeros((S, HQ * HD), device=dev)
+        n0 = ctx.launch_count()
+        ctx.prefill_attn(out, q3attn.OUT_F32, torch.from_numpy(q).to(dev).to(torch.bfloat16),
+                         0, 0, pos0, S)
+        ctx.sync()
+        ctx.check_device_error()
+        launches = ctx.launch_count() - n0
+        got = out.cpu().numpy()
+    assert launches == 2, "expected the split kernel and its combine launch"
+    qd = HQ * HD
+    for r in rows:
+        ref = orc.attn_decode(q[r * qd:(r + 1) * qd].copy(), kc, vc, 0, pos0 + int(r), HQ,
+                              KV_MUL, HD, KV_DIM, n_tok)
+        assert np.all(np.isfinite(got[r, c0:c1])), f"row {r}"
+        assert max_abs(got[r, c0:c1], ref[c0:c1]) <= TOL_BF16_ABS, f"nh {nh} row {r}"
