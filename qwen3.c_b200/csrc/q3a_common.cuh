@@ -209,6 +209,17 @@ __device__ __forceinline__ bool named_bar_red_and(int id, int nthreads, bool v) 
     return r != 0;
 }
 
+// Programmatic dependent launch: a kernel launched with the PDL attribute
+// may be scheduled while the previous kernel of its stream is still
+// running; griddep_wait() returns once that kernel has completed and its
+// memory is visible (a no-op without the attribute).  Kernels here wait
+// before their first global-memory access, so only launch latency and
+// shared-memory set-up overlap the previous kernel.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // Element index of (row R, dim d) in a context's paged cache.  fp32 rows are
 // plain 128-float rows.  bf16 rows are kept in blocks of 8 rows (2 KB, the
 // same bytes the 8 rows would occupy row by row): [2 dim-halves][8 rows][64

@@ -654,6 +654,7 @@ __global__ void __launch_bounds__(DecCfg<KV, TC>::NTHREADS, 1)
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int c = blockIdx.x;
+    if (tid == 0) griddep_launch_dependents();
 
     if (warp == C::CWARPS) {
         // ================================================= producer
@@ -681,6 +682,7 @@ __global__ void __launch_bounds__(DecCfg<KV, TC>::NTHREADS, 1)
         __syncwarp();
         named_bar_arrive(2, C::NTHREADS);
         if (lane == 0) {
+            griddep_wait();  // the previous kernel's writes (cache rows) are visible
             const uint64_t pol = l2_policy_evict_first();
             int it = 0;
             bool dead = false;
@@ -824,6 +826,7 @@ __global__ void __launch_bounds__(DecCfg<KV, TC>::NTHREADS, 1)
         fence_proxy_async_smem();
         tc_fence_before();
     }
+    griddep_wait();  // inputs written by the previous kernel are visible
     while (next_seg(P, c, cur, s)) {
         const int b = s.b, kvh = s.kvh;
         const int hq0 = (P.kv0 + kvh) * GQA;
@@ -1417,8 +1420,19 @@ static cudaError_t launch_decode_t(const DecodeParams& p, const CUtensorMap& tmK
         if (e != cudaSuccess) return e;
         attr_set = true;
     }
-    decode_kernel<KV, SPREAD, TC><<<p.n_ctas, C::NTHREADS, C::SMEM, st>>>(tmK, tmV, p);
-    return cudaGetLastError();
+    // programmatic dependent launch: scheduled while the previous kernel of
+    // the stream finishes; the kernel waits for it before touching memory
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(p.n_ctas);
+    cfg.blockDim = dim3(C::NTHREADS);
+    cfg.dynamicSmemBytes = C::SMEM;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, decode_kernel<KV, SPREAD, TC>, tmK, tmV, p);
 }
 
 cudaError_t launch_decode(const DecodeParams& p, const CUtensorMap& tmK, const CUtensorMap& tmV,
