@@ -247,6 +247,8 @@ __global__ void __launch_bounds__(pf::NTHREADS, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    if (tid == 0) griddep_launch_dependents();
+    griddep_wait();  // the previous kernel's writes (cache, q rows) are visible
 
     if (warp == 0) {
         // ============================================ TMA producer
@@ -675,6 +677,7 @@ __global__ void __launch_bounds__(pf::NTHREADS, 1)
 __global__ void __launch_bounds__(256)
     prefill_combine_kernel(const __grid_constant__ PrefillParams P) {
     const int item = blockIdx.x >> 5, t = (blockIdx.x >> 4) & 1, rg = blockIdx.x & 15;
+    griddep_wait();  // the split kernel's partials are complete and visible
     const PfItem it = pf_item(P, item);
     const int nparts = min(P.nsplit, (it.nj + P.part_tiles - 1) / P.part_tiles);
     if (nparts <= 1) return;
@@ -751,15 +754,29 @@ cudaError_t launch_prefill(const PrefillParams& p, const CUtensorMap& tmQ, cudaS
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
     const int grid = n_chunks < nsm ? n_chunks : nsm;
+    // programmatic dependent launches: each kernel is scheduled while the
+    // previous one of the stream finishes and waits for it before it touches
+    // memory
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(pf::NTHREADS);
+    cfg.dynamicSmemBytes = pf::SMEM;
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
     if (split) {
-        prefill_kernel<true><<<grid, pf::NTHREADS, pf::SMEM, st>>>(tmQ, p);
-        e = cudaGetLastError();
+        e = cudaLaunchKernelEx(&cfg, prefill_kernel<true>, tmQ, p);
         if (e != cudaSuccess) return e;
-        prefill_combine_kernel<<<n_qt * p.nkv * 2 * 2 * 16, 256, 0, st>>>(p);
-    } else {
-        prefill_kernel<false><<<grid, pf::NTHREADS, pf::SMEM, st>>>(tmQ, p);
+        cudaLaunchConfig_t cc = cfg;
+        cc.gridDim = dim3(n_qt * p.nkv * 2 * 2 * 16);
+        cc.blockDim = dim3(256);
+        cc.dynamicSmemBytes = 0;
+        return cudaLaunchKernelEx(&cc, prefill_combine_kernel, p);
     }
-    return cudaGetLastError();
+    return cudaLaunchKernelEx(&cfg, prefill_kernel<false>, tmQ, p);
 }
 
 int prefill_smem_bytes() { return pf::SMEM; }
