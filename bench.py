@@ -259,8 +259,9 @@ def prefill_run(args, torch, dev, local, seed, world, rank=0):
     output.  One step = 36 launches of q3a_prefill_attn (the attention of
     each layer over its cache), timed as one CUDA graph between two events.
     With N > 1 ranks each rank holds 8/N KV heads (and their query heads) and
-    one NCCL all-gather of the output head slices per layer rebuilds the
-    output on every rank (strong scaling)."""
+    one all-gather of the output head slices per layer (q3a_gather_cols:
+    every rank stores its columns into every rank's output over NVLink)
+    rebuilds the output on every rank (strong scaling)."""
     import q3attn
     import shard
     S = PREFILL_S
@@ -281,8 +282,9 @@ def prefill_run(args, torch, dev, local, seed, world, rank=0):
         qs.append(qf.to(torch.bfloat16).view(S, HQ * HD).contiguous())
     out = torch.empty(N_LAYERS, S, HQ * HD, dtype=torch.bfloat16, device=dev)
     stream.synchronize()
-    gather = shard.HeadSliceGather(torch, world=world, rank=rank, rows=S, device=dev,
-                                   dtype=torch.bfloat16) if world > 1 else None
+    # output head slices: one q3a_gather_cols launch per layer (each rank
+    # stores its columns into every rank's `out` over NVLink)
+    gather = shard.PeerHeadGather(torch, ctx, world=world, rank=rank, buf=out) if world > 1 else None
 
     def step():
         for l in range(N_LAYERS):
@@ -305,13 +307,17 @@ def prefill_run(args, torch, dev, local, seed, world, rank=0):
     n0 = ctx.launch_count()
     t_ms, clocks = time_graph(torch, dev, local, stream, step, K, world)
     launches = ctx.launch_count() - n0
-    t_so = None
+    t_so, launches_so = None, 0
     if world > 1:
+        n1 = ctx.launch_count()
         t_so, _ = time_graph(torch, dev, local, stream, step_sharded_out, K, world)
+        launches_so = ctx.launch_count() - n1
     ctx.check_device_error()
     ctx.close()
-    return {"t_ms": t_ms, "launches": launches, "kernel_us": 1000.0 * t_ms / launches,
-            "clocks": clocks, "steps": K, "t_ms_sharded_out": t_so}
+    # a layer is one launch, or two when long items are split (+ the combine
+    # kernel), plus the gather launch at N > 1: time per layer uses layers
+    return {"t_ms": t_ms, "launches": launches, "layers": K * N_LAYERS,
+            "clocks": clocks, "steps": K, "t_ms_sharded_out": t_so, "launches_sharded_out": launches_so}
 
 
 def time_graph(torch, dev, local, stream, step, K, world):
@@ -400,7 +406,8 @@ def ragged_run(args, torch, dev, local, world, rank):
     """64 sequences, one new token each, bf16 caches, one fused
     batched launch (QK-norm, RoPE, append, attention) per step; rank r holds
     KV heads kv_heads(8, N, r) of every sequence, writes its query heads'
-    columns of xb, and one NCCL all-gather of the slices rebuilds xb."""
+    columns of xb, and one all-gather of the slices over NVLink
+    (q3a_gather_cols) rebuilds xb."""
     import q3attn
     import shard
     lens = ragged_lengths()
@@ -430,8 +437,7 @@ def ragged_run(args, torch, dev, local, world, rank):
     stream.synchronize()
     seq_ids = list(range(RAGGED_B))
     pos = [int(L) - 1 for L in lens]
-    gather = shard.HeadSliceGather(torch, world=world, rank=rank, rows=RAGGED_B,
-                                   device=dev) if world > 1 else None
+    gather = shard.PeerHeadGather(torch, ctx, world=world, rank=rank, buf=xb) if world > 1 else None
 
     def step():
         ctx.attn_layer_batched(xb, q, k, v, ones, ones, 0, seq_ids, pos)
@@ -721,10 +727,10 @@ def main():
         pr = prefill_run(args, torch, dev, local, seed, world, rank)
         t_p = max_over_ranks(pr["t_ms"], world, dev)
         fl = prefill_flops()
-        # each launch is one layer (N = 1) or one rank's 8/N KV heads of a
-        # layer (N > 1): the job computes launches layers in t_p
-        us_l = t_p * 1000.0 / pr["launches"]
-        tf = fl * pr["launches"] / (t_p / 1000.0) / 1e12
+        # every rank processes its 8/N KV heads of each layer: the job
+        # computes `layers` whole layers in t_p
+        us_l = t_p * 1000.0 / pr["layers"]
+        tf = fl * pr["layers"] / (t_p / 1000.0) / 1e12
         line["prefill"] = {"metric": "prefill attn TFLOP/s (2K tok)", "value": tf,
                            "unit": "TFLOP/s", "us_per_layer": us_l,
                            "flops_per_layer": fl, "steps": pr["steps"],
@@ -745,10 +751,10 @@ def main():
             # kernel time with each rank's output left head-sharded (no gather)
             t_so = max_over_ranks(pr["t_ms_sharded_out"], world, dev)
             line["prefill"]["sharded_out"] = {
-                "us_per_layer": t_so * 1000.0 / pr["launches"],
-                "value": fl * pr["launches"] / (t_so / 1000.0) / 1e12, "unit": "TFLOP/s",
+                "us_per_layer": t_so * 1000.0 / pr["layers"],
+                "value": fl * pr["layers"] / (t_so / 1000.0) / 1e12, "unit": "TFLOP/s",
                 "note": "same launches without the all-gather of the output head slices"}
-            line["gpu_launches"] += pr["launches"]
+            line["gpu_launches"] += pr["launches_sharded_out"]
         line["gpu_launches"] += pr["launches"]
     if not args.no_variants:
         lc = long_ctx_run(args, torch, dev, local, world, rank)
@@ -779,8 +785,9 @@ def main():
                                 "parallelism": f"kvhead{world}" if world > 1 else "single",
                                 "workload": "configs[4]: 64 sequences, KV lengths U[512, 32768] "
                                             f"(mean {rg['mean_len']:.0f}), bf16, one fused "
-                                            "q3a_attn_layer_batched launch per step + NCCL "
-                                            "all-gather of the xb head slices",
+                                            "q3a_attn_layer_batched launch per step + "
+                                            "all-gather of the xb head slices over NVLink "
+                                            "(q3a_gather_cols)",
                                 "bytes_per_step": rg["bytes_per_step"],
                                 "hbm_frac_per_gpu": rg["bytes_per_step"] / world / (us_s * 1e-6)
                                 / 1e9 / hbm_peak,

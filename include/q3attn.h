@@ -47,6 +47,7 @@ extern "C" {
 
 #define Q3A_MAX_PEERS 8         /* ranks of a peer-memory sequence shard */
 #define Q3A_IPC_HANDLE_BYTES 64 /* bytes of one exported buffer handle */
+#define Q3A_PEER_REG_BYTES 136  /* bytes of one q3a_peer_register handle */
 
 #define Q3A_OUT_F32 0
 #define Q3A_OUT_BF16 1
@@ -236,6 +237,34 @@ int q3a_peer_export(q3a_ctx *ctx, int world, void *handle);
 int q3a_peer_open(q3a_ctx *ctx, int rank, int world, const void *handles);
 int q3a_attn_seqshard(q3a_ctx *ctx, float *xb, const float *q, int seq, int layer,
                       int n_local);
+
+/* All-gather of column slices over peer memory (NVLink), for KV-head shards:
+ * rank r computed columns [col0_r, col0_r + col_bytes) of every row of a
+ * row-major matrix (its query heads' slice of xb or of a prefill output);
+ * afterwards every rank holds every rank's columns.  No collective library
+ * is called; the reference has no multi-GPU path and these calls replace
+ * nothing in it.
+ * Set-up, once per context, in the same order on every rank (one process
+ * per GPU, device-pointer mode):
+ *   q3a_peer_register(ctx, buf, bytes, handle)  makes the caller's device
+ *       buffer [buf, buf+bytes) (cudaMalloc'd, directly or by an allocator)
+ *       and a flag block mappable by the other ranks; `handle` receives
+ *       Q3A_PEER_REG_BYTES bytes;
+ *   the caller exchanges the handles and calls
+ *   q3a_peer_register_open(ctx, rank, world, handles)  with all ranks'
+ *       handles in rank order.
+ * Per call: q3a_gather_cols(ctx, off, rows, row_bytes, col0, col_bytes)
+ * gathers the matrix starting `off` bytes into every rank's registered
+ * buffer (same layout on every rank; row_bytes, col0 and col_bytes multiples
+ * of 16; this rank's columns start at col0).  One launch: the ranks first
+ * meet (so no rank writes into a buffer another rank still reads from its
+ * previous call), each copies its columns into every other rank's buffer,
+ * then they meet again; bounded waits (Q3A_ERR_TIMEOUT after about a
+ * second).  Stream-ordered; all ranks make the same sequence of calls. */
+int q3a_peer_register(q3a_ctx *ctx, void *buf, size_t bytes, void *handle);
+int q3a_peer_register_open(q3a_ctx *ctx, int rank, int world, const void *handles);
+int q3a_gather_cols(q3a_ctx *ctx, size_t off, long long rows, size_t row_bytes, size_t col0,
+                    size_t col_bytes);
 
 /* Seeded N(0,1) fill of n elements (fp32 or bf16 by out_dtype): element i is
  * the Box-Muller transform of uniforms u(2j), u(2j+1), j = (offset+i)/2, with

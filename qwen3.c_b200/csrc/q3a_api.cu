@@ -116,6 +116,16 @@ struct q3a_ctx {
     float* peer_buf = nullptr;            // this rank's receive buffer
     float* peer_ptrs[PEER_MAX] = {};      // every rank's buffer, mapped here
     unsigned* peer_epoch = nullptr;       // call counter + finisher ticket
+    // registered caller buffer for column all-gathers (q3a_peer_register)
+    uint8_t* reg_buf = nullptr;           // the caller's buffer
+    size_t reg_bytes = 0;
+    unsigned* reg_flags = nullptr;        // [2 phases][PEER_MAX], written by peers
+    unsigned* reg_state = nullptr;        // call number, CTA arrivals, go
+    int reg_world = 0, reg_rank = -1;
+    uint8_t* reg_peer[PEER_MAX] = {};     // every rank's buffer, mapped here
+    unsigned* reg_peer_flags[PEER_MAX] = {};
+    void* reg_ipc_bases[PEER_MAX] = {};   // mappings to close
+    void* reg_ipc_flags[PEER_MAX] = {};
 };
 
 static int ensure_device(const q3a_ctx* c) {
@@ -185,6 +195,12 @@ static void destroy_ctx(q3a_ctx* c) {
         if (c->peer_ptrs[r] && c->peer_ptrs[r] != c->peer_buf) cudaIpcCloseMemHandle(c->peer_ptrs[r]);
     cudaFree(c->peer_buf);
     cudaFree(c->peer_epoch);
+    for (int r = 0; r < PEER_MAX; r++) {
+        if (c->reg_ipc_bases[r]) cudaIpcCloseMemHandle(c->reg_ipc_bases[r]);
+        if (c->reg_ipc_flags[r]) cudaIpcCloseMemHandle(c->reg_ipc_flags[r]);
+    }
+    cudaFree(c->reg_flags);
+    cudaFree(c->reg_state);
     cudaFree(c->kcache);
     cudaFree(c->vcache);
     cudaFree(c->partials);
@@ -830,6 +846,124 @@ extern "C" int q3a_peer_open(q3a_ctx* c, int rank, int world, const void* handle
         c->peer_ptrs[r] = reinterpret_cast<float*>(p);
     }
     c->peer_rank = rank;
+    return Q3A_OK;
+}
+
+// ---------------------------------------------------- column all-gather (peer memory)
+typedef CUresult (*AddrRangeFn)(CUdeviceptr*, size_t*, CUdeviceptr);
+
+extern "C" int q3a_peer_register(q3a_ctx* c, void* buf, size_t bytes, void* handle) {
+    g_err[0] = 0;
+    if (!c || !buf || !handle || bytes == 0) return fail(Q3A_ERR_INVALID, "bad argument");
+    if (c->cfg.ptr_mode != Q3A_PTR_DEVICE) return fail(Q3A_ERR_UNSUPPORTED, "peer gathers run in device-pointer mode");
+    if (c->reg_buf) return fail(Q3A_ERR_INVALID, "a buffer is already registered");
+    int rc = ensure_device(c);
+    if (rc) return rc;
+    // the IPC handle names the whole allocation: find its base and our offset
+    static AddrRangeFn range = nullptr;
+    if (!range) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &p, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            return fail(Q3A_ERR_CUDA, "cuMemGetAddressRange entry point unavailable");
+        range = reinterpret_cast<AddrRangeFn>(p);
+    }
+    CUdeviceptr base = 0;
+    size_t size = 0;
+    if (range(&base, &size, reinterpret_cast<CUdeviceptr>(buf)) != CUDA_SUCCESS)
+        return fail(Q3A_ERR_INVALID, "buffer is not device memory of this context's device");
+    const uint64_t off = reinterpret_cast<CUdeviceptr>(buf) - base;
+    if (off + bytes > size) return fail(Q3A_ERR_INVALID, "buffer runs past its allocation");
+    if (cudaMalloc(&c->reg_flags, 2 * PEER_MAX * sizeof(unsigned)) != cudaSuccess ||
+        cudaMalloc(&c->reg_state, 4 * sizeof(unsigned)) != cudaSuccess)
+        return fail(Q3A_ERR_OOM, "gather flags");
+    CUDA_TRY(cudaMemset(c->reg_flags, 0, 2 * PEER_MAX * sizeof(unsigned)));
+    CUDA_TRY(cudaMemset(c->reg_state, 0, 4 * sizeof(unsigned)));
+    CUDA_TRY(cudaDeviceSynchronize());
+    cudaIpcMemHandle_t hb, hf;
+    CUDA_TRY(cudaIpcGetMemHandle(&hb, reinterpret_cast<void*>(base)));
+    CUDA_TRY(cudaIpcGetMemHandle(&hf, c->reg_flags));
+    static_assert(2 * sizeof(cudaIpcMemHandle_t) + 8 == Q3A_PEER_REG_BYTES, "handle layout");
+    uint8_t* h = reinterpret_cast<uint8_t*>(handle);
+    memcpy(h, &hb, sizeof(hb));
+    memcpy(h + sizeof(hb), &off, 8);
+    memcpy(h + sizeof(hb) + 8, &hf, sizeof(hf));
+    c->reg_buf = reinterpret_cast<uint8_t*>(buf);
+    c->reg_bytes = bytes;
+    return Q3A_OK;
+}
+
+extern "C" int q3a_peer_register_open(q3a_ctx* c, int rank, int world, const void* handles) {
+    g_err[0] = 0;
+    if (!c || !handles) return fail(Q3A_ERR_INVALID, "null argument");
+    if (!c->reg_buf) return fail(Q3A_ERR_INVALID, "q3a_peer_register must come first");
+    if (world < 1 || world > PEER_MAX || rank < 0 || rank >= world)
+        return fail(Q3A_ERR_INVALID, "rank %d of %d", rank, world);
+    if (c->reg_rank >= 0) return fail(Q3A_ERR_INVALID, "peers already open");
+    int rc = ensure_device(c);
+    if (rc) return rc;
+    const uint8_t* hs = reinterpret_cast<const uint8_t*>(handles);
+    for (int r = 0; r < world; r++) {
+        if (r == rank) {
+            c->reg_peer[r] = c->reg_buf;
+            c->reg_peer_flags[r] = c->reg_flags;
+            continue;
+        }
+        const uint8_t* h = hs + (size_t)r * Q3A_PEER_REG_BYTES;
+        cudaIpcMemHandle_t hb, hf;
+        uint64_t off = 0;
+        memcpy(&hb, h, sizeof(hb));
+        memcpy(&off, h + sizeof(hb), 8);
+        memcpy(&hf, h + sizeof(hb) + 8, sizeof(hf));
+        void *pb = nullptr, *pf = nullptr;
+        if (cudaIpcOpenMemHandle(&pb, hb, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess ||
+            cudaIpcOpenMemHandle(&pf, hf, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+            cudaGetLastError();
+            return fail(Q3A_ERR_CUDA, "cannot map the registered buffer of rank %d", r);
+        }
+        c->reg_ipc_bases[r] = pb;
+        c->reg_ipc_flags[r] = pf;
+        c->reg_peer[r] = reinterpret_cast<uint8_t*>(pb) + off;
+        c->reg_peer_flags[r] = reinterpret_cast<unsigned*>(pf);
+    }
+    c->reg_world = world;
+    c->reg_rank = rank;
+    return Q3A_OK;
+}
+
+extern "C" int q3a_gather_cols(q3a_ctx* c, size_t off, long long rows, size_t row_bytes, size_t col0,
+                               size_t col_bytes) {
+    g_err[0] = 0;
+    if (!c) return fail(Q3A_ERR_INVALID, "null context");
+    if (c->reg_rank < 0) return fail(Q3A_ERR_INVALID, "q3a_peer_register_open must come first");
+    if (rows <= 0 || row_bytes % 16 || col0 % 16 || col_bytes % 16 || col_bytes == 0 ||
+        col0 + col_bytes > row_bytes || off % 16)
+        return fail(Q3A_ERR_INVALID, "rows %lld, row/column bytes must be multiples of 16", rows);
+    if (off + (size_t)rows * row_bytes > c->reg_bytes)
+        return fail(Q3A_ERR_INVALID, "matrix runs past the registered buffer");
+    int rc = ensure_device(c);
+    if (rc) return rc;
+    ColGatherParams p;
+    memset(&p, 0, sizeof(p));
+    p.local = c->reg_buf + off;
+    for (int r = 0; r < c->reg_world; r++) {
+        p.peer[r] = c->reg_peer[r] + off;
+        p.peer_flags[r] = c->reg_peer_flags[r];
+    }
+    p.flags = c->reg_flags;
+    p.state = c->reg_state;
+    p.world = c->reg_world;
+    p.rank = c->reg_rank;
+    p.rows = rows;
+    p.row_bytes = (long long)row_bytes;
+    p.col0 = (long long)col0;
+    p.vecs = (int)(col_bytes / 16);
+    p.err = c->err;
+    const long long work = rows * p.vecs;
+    const int n_ctas = (int)std::min<long long>(c->num_sms, std::max<long long>(1, (work + 255) / 256));
+    CUDA_TRY(launch_gather_cols(p, n_ctas, c->stream));
+    c->launches++;
     return Q3A_OK;
 }
 

@@ -147,6 +147,22 @@ cudaError_t launch_lse_combine(float* xb, const float* o_parts, size_t o_stride,
                                const float* lse_parts, size_t lse_stride, int n_parts, int n_heads,
                                cudaStream_t st);
 
+// All-gather of column slices over peer memory (q3a_gather_cols).
+struct ColGatherParams {
+    const uint8_t* local;          // this rank's matrix (registered buffer + off)
+    uint8_t* peer[PEER_MAX];       // every rank's matrix, as mapped here
+    unsigned* flags;               // this rank's flag block: [2 phases][PEER_MAX], written by peers
+    unsigned* peer_flags[PEER_MAX];// every rank's flag block, as mapped here
+    unsigned* state;               // this rank: [0] call number, [1] CTA arrivals, [2] go
+    int world, rank;
+    long long rows;
+    long long row_bytes;
+    long long col0;                // bytes
+    int vecs;                      // 16-byte vectors per row slice
+    int* err;
+};
+cudaError_t launch_gather_cols(const ColGatherParams& p, int n_ctas, cudaStream_t st);
+
 struct PrefillParams {
     const __nv_bfloat16* kcache;  // the context's paged bf16 caches
     const __nv_bfloat16* vcache;

@@ -12,6 +12,7 @@ import os
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "lib", "libq3attn.so")
 IPC_HANDLE_BYTES = 64  # Q3A_IPC_HANDLE_BYTES
+PEER_REG_BYTES = 136   # Q3A_PEER_REG_BYTES
 MAX_PEERS = 8          # Q3A_MAX_PEERS
 
 OK, ERR_INVALID, ERR_CUDA, ERR_OOM, ERR_UNSUPPORTED, ERR_TIMEOUT = 0, 1, 2, 3, 4, 5
@@ -27,6 +28,7 @@ EXPORTS = [
     "q3a_attn_layer_batched", "q3a_kv_append", "q3a_kv_load", "q3a_kv_read", "q3a_prefill",
     "q3a_prefill_attn", "q3a_attn_partial", "q3a_lse_combine", "q3a_lse_combine_packed",
     "q3a_peer_export", "q3a_peer_open", "q3a_attn_seqshard",
+    "q3a_peer_register", "q3a_peer_register_open", "q3a_gather_cols",
     "q3a_randn",
     "q3a_launch_count", "q3a_attn_decode_noalloc",
 ]
@@ -83,6 +85,9 @@ def load():
         L.q3a_peer_export.argtypes = [_P, _I, _P]
         L.q3a_peer_open.argtypes = [_P, _I, _I, _P]
         L.q3a_attn_seqshard.argtypes = [_P, _P, _P, _I, _I, _I]
+        L.q3a_peer_register.argtypes = [_P, _P, _SZ, _P]
+        L.q3a_peer_register_open.argtypes = [_P, _I, _I, _P]
+        L.q3a_gather_cols.argtypes = [_P, _SZ, ctypes.c_longlong, _SZ, _SZ, _SZ]
         L.q3a_randn.argtypes = [_P, _P, _I, _SZ, _U64, _U64, _U64]
         L.q3a_attn_decode_noalloc.argtypes = [_P, _P, _P, _P, _SZ, _I, _I, _I, _I, _I, _I, _P]
         L.q3a_launch_count.argtypes = [_P]
@@ -217,6 +222,22 @@ class Context:
 
     def attn_seqshard(self, xb, q, seq, layer, n_local):
         check(self.lib.q3a_attn_seqshard(self.h, ptr(xb), ptr(q), seq, layer, n_local))
+
+    def peer_register(self, buf, nbytes) -> bytes:
+        """Registers a device buffer for column all-gathers; returns this
+        rank's handle (PEER_REG_BYTES bytes)."""
+        out = ctypes.create_string_buffer(PEER_REG_BYTES)
+        check(self.lib.q3a_peer_register(self.h, ptr(buf), nbytes, out))
+        return out.raw
+
+    def peer_register_open(self, rank, world, handles):
+        """handles: every rank's peer_register() bytes, in rank order."""
+        blob = b"".join(handles)
+        buf = ctypes.create_string_buffer(blob, len(blob))
+        check(self.lib.q3a_peer_register_open(self.h, rank, world, buf))
+
+    def gather_cols(self, off, rows, row_bytes, col0, col_bytes):
+        check(self.lib.q3a_gather_cols(self.h, off, rows, row_bytes, col0, col_bytes))
 
     def randn(self, dst, out_dtype, n, seed, stream_id, offset=0):
         check(self.lib.q3a_randn(self.h, ptr(dst), out_dtype, n, seed, stream_id, offset))

@@ -20,7 +20,10 @@ issues are new, and all arithmetic stays in the library's kernels.
     ``q3a_lse_combine_packed`` merges them into the full xb on every rank.
 * KV-head shards (batched decode, prefill).  Rank r holds KV heads
   ``kv_heads(n_kv, world, r)`` and their query heads; attention needs no
-  exchange, and one all-gather of the xb head slices rebuilds xb.
+  exchange, and one all-gather of the head slices rebuilds xb (or a prefill
+  output): ``HeadSliceGather`` through NCCL, or ``PeerHeadGather``, one
+  ``q3a_gather_cols`` launch that stores each rank's columns straight into
+  every rank's registered buffer over NVLink.
 """
 from __future__ import annotations
 
@@ -131,3 +134,32 @@ class HeadSliceGather:
         for r in range(self.world):
             if r != self.rank:
                 xb[:, r * self.w:(r + 1) * self.w].copy_(self.recv[r])
+
+
+class PeerHeadGather:
+    """All-gather of KV-head-sharded column slices over peer memory: ``buf``
+    (a device tensor, registered once on every rank) holds row-major
+    matrices [rows, n_heads*hd]; rank r computed the columns of its query
+    heads; ``gather(t)`` for a matrix view ``t`` inside ``buf`` gives every
+    rank all columns of ``t`` (one ``q3a_gather_cols`` launch)."""
+
+    def __init__(self, torch, ctx, *, world: int, rank: int, buf, group=None, n_heads: int = 32,
+                 hd: int = 128):
+        import torch.distributed as dist
+        if n_heads % world != 0:
+            raise ValueError(f"{n_heads} query heads do not split over {world} ranks")
+        self.ctx, self.world, self.rank = ctx, world, rank
+        self.buf = buf
+        handle = ctx.peer_register(buf, buf.numel() * buf.element_size())
+        handles = [handle]
+        if world > 1:
+            handles = [None] * world
+            dist.all_gather_object(handles, handle, group=group)
+        ctx.peer_register_open(rank, world, handles)
+        self.w = n_heads // world * hd
+
+    def __call__(self, t):
+        """t: a [rows, n_heads*hd] view of ``buf`` with contiguous rows."""
+        es = t.element_size()
+        off = t.data_ptr() - self.buf.data_ptr()
+        self.ctx.gather_cols(off, t.shape[0], t.stride(0) * es, self.rank * self.w * es, self.w * es)

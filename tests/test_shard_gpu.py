@@ -224,3 +224,23 @@ def test_sequence_shards_over_gpus(tmp_path, mode, world):
     for rank in range(world):
         err = float(open(os.path.join(tmp_path, f"rank{rank}.txt")).read())
         assert err <= TOL_BF16_ABS, f"rank {rank}: max-abs {err}"
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_peer_head_gather(tmp_path, world):
+    """q3a_gather_cols over `world` GPUs (torchrun, one process per GPU):
+    every rank ends with every rank's column slice, bit-exact, over repeated
+    calls on two matrices of one registered buffer."""
+    import subprocess
+    import torch
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", SHARD_TEST_OUT=str(tmp_path))
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node",
+           str(world), "--master-addr", "127.0.0.1", "--master-port", str(_free_port()),
+           os.path.join(ROOT, "tests", "peer_gather_worker.py")]
+    r = subprocess.run(cmd, env=env, timeout=240, capture_output=True, text=True)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
+    for rank in range(world):
+        bad = int(open(os.path.join(tmp_path, f"rank{rank}.txt")).read())
+        assert bad == 0, f"rank {rank}: {bad} slices differ"
