@@ -9,29 +9,34 @@
 //  * Work is split into contiguous cache-row ranges of (sequence, KV head)
 //    groups.  With at most one group per SM (the single-sequence decode of the
 //    reference) every CTA gets exactly one range, sized so that ranges are
-//    equal to within one 16-row TMA box; larger batches use a linear list of
-//    64-row tiles cut into equal shares.  Grid size <= SM count, one CTA per
-//    SM.
+//    equal to within one 16-row box ("piece mode"); larger batches use a
+//    linear list of 64-row tiles cut into equal shares.  Grid size <= SM
+//    count, one CTA per SM.
 //  * Warp 8 is the producer: one lane streams K and V into a ring of
-//    64-row shared-memory stages, each tile of the paged cache as one bulk
-//    copy per tensor (cp.async.bulk; two where a tile crosses a page
-//    boundary), with an L2 evict-first policy since each cache row is read
-//    once per step, completing on per-stage mbarriers.  The caller-owned
-//    position-major cache of q3a_attn_decode is strided and moves in 16-row
-//    2-D TMA boxes (cp.async.bulk.tensor) instead.
-//  * Warps 0-7 consume: each takes 8 rows of a stage, so every K/V element
-//    leaves shared memory once and feeds all 4 query heads of its KV head.
-//    q.k uses 8 lanes per row with 16 dims each (packed fp32x2 FMA), then a
-//    7-shuffle reduce-scatter gives one (row, head) score per lane; each warp
-//    keeps its own online-softmax state (log2 domain) in registers, so no
-//    CTA-wide barrier is taken per tile.
+//    shared-memory stages, each stage of the paged cache as one bulk copy per
+//    tensor (cp.async.bulk; two where a stage crosses a page boundary), with
+//    an L2 evict-first policy since each cache row is read once per step.
+//    The caller-owned position-major cache of q3a_attn_decode is strided and
+//    moves in 16-row 2-D TMA boxes (cp.async.bulk.tensor) instead.
+//  * fp32 caches are consumed on the CUDA cores by warps 0-7, each taking 8
+//    rows of a 64-row stage, so every K/V element leaves shared memory once
+//    and feeds all 4 query heads of its KV head; q.k uses 8 lanes per row
+//    with 16 dims each (packed fp32x2 FMA), a 7-shuffle reduce-scatter gives
+//    one (row, head) score per lane, and each warp keeps its own online
+//    softmax (log2 domain), merged through shared memory at the end.
+//  * bf16 caches are consumed on the tensor cores (TC instantiation): the
+//    cache's 8-row blocks are already the 128B-swizzled operand layout, so a
+//    128-row stage is used as is; warp 4 issues S^T = K.Q^T and
+//    O^T = V^T.P^T (tcgen05.mma, accumulators in tensor memory) and warps 0-3
+//    run the softmax between them.
 //  * The prologue issues every global load of the range's inputs at once (q,
 //    norm gains, the new token's k and v) and reduces the RMS norms with warp
-//    shuffles, overlapping the first TMA round trip.
-//  * At the end of a range the 8 warp states merge through shared memory;
-//    ranges sharing a group write normalised partials (o, lse) to scratch and
-//    the last CTA to arrive (atomic counter, reset by that CTA) merges them by
-//    log-sum-exp into xb.
+//    shuffles, overlapping the first stage's load.
+//  * Ranges sharing a group merge by log-sum-exp: in piece mode by the
+//    spread merge (tagged words in scratch, each range merges one slice of
+//    the outputs), in linear mode by a ticket (the last range to arrive
+//    merges all partials); sequence shards then exchange (o, lse) with every
+//    rank over peer memory the same way.
 #include "q3a_common.cuh"
 #include "q3a_internal.h"
 #include "q3a_tcgen05.cuh"
@@ -44,7 +49,7 @@ struct DecCfg {
     static constexpr int CWARPS = 8;
     static constexpr int NCONS = CWARPS * 32;
     static constexpr int NTHREADS = NCONS + 32;
-    static constexpr int STAGES = sizeof(KV) == 4 ? 3 : 6;
+    static constexpr int STAGES = 3;  // fp32 (bf16 caches use the configuration below)
     static constexpr int TILE_BYTES = TILE * HD * (int)sizeof(KV);
     static constexpr int BOX_BYTES = DEC_BOX * HD * (int)sizeof(KV);
     static constexpr int OFF_K = 0;
@@ -214,33 +219,22 @@ __device__ __forceinline__ int atom_add_acq_rel(int* p, int v) {
 }
 
 // q registers of one lane as fp32 pairs, 4 heads x 16 dims, pre-scaled by
-// log2(e)/sqrt(hd).  fp32 tiles: lane j=lane&7 holds dims 4j+32s+e (s<4,
-// e<4); bf16 tiles: dims 8j+64s+e (s<2, e<8); both give conflict-free 16-byte
-// shared loads (the 8 lanes of a row read 128 consecutive bytes).
+// log2(e)/sqrt(hd): lane j=lane&7 holds dims 4j+32s+e (s<4, e<4), which gives
+// conflict-free 16-byte shared loads (the 8 lanes of a row read 128
+// consecutive bytes).  The CUDA-core consumer reads fp32 caches only (bf16
+// caches go to the tensor cores).
 template <typename KV>
 __device__ __forceinline__ void load_q_regs(const float* sQ, int lane, float sl2e,
                                             float2 (&qr)[GQA][8]) {
+    static_assert(sizeof(KV) == 4, "the CUDA-core consumer reads fp32 caches");
     const int j = lane & 7;
 #pragma unroll
     for (int h = 0; h < GQA; h++) {
-        if constexpr (sizeof(KV) == 4) {
 #pragma unroll
-            for (int s = 0; s < 4; s++) {
-                const float4 t = *reinterpret_cast<const float4*>(sQ + h * HD + 4 * j + 32 * s);
-                qr[h][2 * s] = make_float2(t.x * sl2e, t.y * sl2e);
-                qr[h][2 * s + 1] = make_float2(t.z * sl2e, t.w * sl2e);
-            }
-        } else {
-#pragma unroll
-            for (int s = 0; s < 2; s++) {
-                const float4 t0 = *reinterpret_cast<const float4*>(sQ + h * HD + 8 * j + 64 * s);
-                const float4 t1 =
-                    *reinterpret_cast<const float4*>(sQ + h * HD + 8 * j + 64 * s + 4);
-                qr[h][4 * s + 0] = make_float2(t0.x * sl2e, t0.y * sl2e);
-                qr[h][4 * s + 1] = make_float2(t0.z * sl2e, t0.w * sl2e);
-                qr[h][4 * s + 2] = make_float2(t1.x * sl2e, t1.y * sl2e);
-                qr[h][4 * s + 3] = make_float2(t1.z * sl2e, t1.w * sl2e);
-            }
+        for (int s = 0; s < 4; s++) {
+            const float4 t = *reinterpret_cast<const float4*>(sQ + h * HD + 4 * j + 32 * s);
+            qr[h][2 * s] = make_float2(t.x * sl2e, t.y * sl2e);
+            qr[h][2 * s + 1] = make_float2(t.z * sl2e, t.w * sl2e);
         }
     }
 }
@@ -248,8 +242,6 @@ __device__ __forceinline__ void load_q_regs(const float* sQ, int lane, float sl2
 __device__ __forceinline__ float sel4(const float (&a)[4], int i) {
     return i == 0 ? a[0] : i == 1 ? a[1] : i == 2 ? a[2] : a[3];
 }
-
-__device__ __forceinline__ float2 bf16pair(uint32_t u) { return make_float2(bf16lo(u), bf16hi(u)); }
 
 // Scores of rows 2g and 2g+1 (relative to r0) of one warp's 8-row share:
 // acc[tt][h] holds fp32 pairs (even/odd dims) for row 2g+tt.  FULL_ROWS
@@ -263,7 +255,8 @@ __device__ __forceinline__ void qk_rows(const KV* Kt, int r0, int rlo, int rhi, 
 #pragma unroll
         for (int h = 0; h < GQA; h++) acc[tt][h] = make_float2(0.0f, 0.0f);
     }
-    if constexpr (sizeof(KV) == 4) {
+    static_assert(sizeof(KV) == 4, "the CUDA-core consumer reads fp32 caches");
+    {
         float4 kv[2][4];
 #pragma unroll
         for (int tt = 0; tt < 2; tt++) {
@@ -290,35 +283,6 @@ __device__ __forceinline__ void qk_rows(const KV* Kt, int r0, int rlo, int rhi, 
                 }
             }
         }
-    } else {
-        uint4 ku[2][2];
-#pragma unroll
-        for (int tt = 0; tt < 2; tt++) {
-            const int rr = 2 * g + tt;
-            const __nv_bfloat16* kr =
-                reinterpret_cast<const __nv_bfloat16*>(Kt) + (r0 + rr) * HD + 8 * j;
-#pragma unroll
-            for (int s = 0; s < 2; s++) {
-                if (FULL_ROWS || (rr >= rlo && rr < rhi))
-                    ku[tt][s] = *reinterpret_cast<const uint4*>(kr + 64 * s);
-                else
-                    ku[tt][s] = make_uint4(0u, 0u, 0u, 0u);
-            }
-        }
-#pragma unroll
-        for (int tt = 0; tt < 2; tt++) {
-#pragma unroll
-            for (int s = 0; s < 2; s++) {
-                const float2 k2[4] = {bf16pair(ku[tt][s].x), bf16pair(ku[tt][s].y),
-                                      bf16pair(ku[tt][s].z), bf16pair(ku[tt][s].w)};
-#pragma unroll
-                for (int h = 0; h < GQA; h++) {
-#pragma unroll
-                    for (int e = 0; e < 4; e++)
-                        acc[tt][h] = __ffma2_rn(qr[h][4 * s + e], k2[e], acc[tt][h]);
-                }
-            }
-        }
     }
 }
 
@@ -331,17 +295,10 @@ __device__ __forceinline__ void pv_rows(const KV* Vt, int r0, int rlo, int rhi, 
 #pragma unroll
     for (int tt = 0; tt < 8; tt++) {
         if (FULL_ROWS || (tt >= rlo && tt < rhi)) {
-            if constexpr (sizeof(KV) == 4) {
-                const float4 t = *reinterpret_cast<const float4*>(
-                    reinterpret_cast<const float*>(Vt) + (r0 + tt) * HD + 4 * lane);
-                va[tt] = make_float2(t.x, t.y);
-                vb[tt] = make_float2(t.z, t.w);
-            } else {
-                const uint2 u = *reinterpret_cast<const uint2*>(
-                    reinterpret_cast<const __nv_bfloat16*>(Vt) + (r0 + tt) * HD + 4 * lane);
-                va[tt] = bf16pair(u.x);
-                vb[tt] = bf16pair(u.y);
-            }
+            const float4 t = *reinterpret_cast<const float4*>(
+                reinterpret_cast<const float*>(Vt) + (r0 + tt) * HD + 4 * lane);
+            va[tt] = make_float2(t.x, t.y);
+            vb[tt] = make_float2(t.z, t.w);
         } else {
             va[tt] = vb[tt] = make_float2(0.0f, 0.0f);  // p is 0 there too
         }
