@@ -64,6 +64,8 @@ def _worker(rank, world, port, kind, q):
         dist.init_process_group("gloo", rank=rank, world_size=world)
         if kind == "seq":
             err = _seq_case(torch, orc, shard, rank, world)
+        elif kind == "peer_gather":
+            err = _peer_gather_case(torch, shard, rank, world)
         else:
             err = _head_case(torch, orc, shard, rank, world)
         dist.barrier()
@@ -117,7 +119,39 @@ def _head_case(torch, orc, shard, rank, world):
     return normwise(xb.numpy(), ref)
 
 
-@pytest.mark.parametrize("kind", ["seq", "head"])
+def _peer_gather_case(torch, shard, rank, world):
+    """PeerHeadGather's host side with a stand-in context: the registered
+    handles travel to every rank in rank order, and a gather of a matrix view
+    inside the buffer asks for this rank's column slice at the right byte
+    offsets.  Returns 0.0 when every check holds."""
+
+    class FakeCtx:
+        def __init__(self):
+            self.opened = None
+            self.calls = []
+
+        def peer_register(self, buf, nbytes):
+            assert nbytes == buf.numel() * buf.element_size()
+            return bytes([rank]) * 136
+
+        def peer_register_open(self, r, w, handles):
+            self.opened = (r, w, list(handles))
+
+        def gather_cols(self, off, rows, row_bytes, col0, col_bytes):
+            self.calls.append((off, rows, row_bytes, col0, col_bytes))
+
+    ctx = FakeCtx()
+    buf = torch.zeros(3, 40, HQ * HD, dtype=torch.bfloat16)
+    g = shard.PeerHeadGather(torch, ctx, world=world, rank=rank, buf=buf)
+    assert ctx.opened == (rank, world, [bytes([r]) * 136 for r in range(world)])
+    g(buf[2])
+    es = 2
+    w = HQ * HD // world
+    assert ctx.calls == [(2 * 40 * HQ * HD * es, 40, HQ * HD * es, rank * w * es, w * es)]
+    return 0.0
+
+
+@pytest.mark.parametrize("kind", ["seq", "head", "peer_gather"])
 def test_sharded_exchange_on_two_gloo_ranks(kind):
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
