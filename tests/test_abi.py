@@ -74,3 +74,33 @@ def test_create_rejects_bad_shapes_without_gpu_work():
         rc = lib.q3a_create(ctypes.byref(h), ctypes.byref(cfg))
         assert rc in (q3attn.ERR_UNSUPPORTED, q3attn.ERR_INVALID)
         assert lib.q3a_last_error().decode() != ""
+
+
+def test_c_host_links_and_calls_the_library(tmp_path):
+    """A C host, as the reference's main.c would be: includes the header,
+    links libq3attn.so, fills the default configuration and gets a clean
+    error for an unsupported shape (no device work)."""
+    lib_dir = os.path.dirname(q3attn.LIB_PATH)
+    src = tmp_path / "host.c"
+    src.write_text(r"""
+#include <stdio.h>
+#include <string.h>
+#include "q3attn.h"
+int main(void) {
+    q3a_cfg cfg;
+    q3a_cfg_default(&cfg);
+    if (cfg.n_heads != 32 || cfg.n_kv_heads != 8 || cfg.head_dim != 128) return 2;
+    cfg.head_dim = 64;
+    q3a_ctx *ctx = NULL;
+    int rc = q3a_create(&ctx, &cfg);
+    if (rc != Q3A_ERR_UNSUPPORTED || ctx != NULL || strlen(q3a_last_error()) == 0) return 3;
+    printf("ok %s\n", q3a_last_error());
+    return 0;
+}
+""")
+    exe = tmp_path / "host"
+    subprocess.run(["gcc", "-std=c11", "-I", os.path.join(ROOT, "include"), str(src), "-o", str(exe),
+                    "-L", lib_dir, "-lq3attn", "-Wl,-rpath," + lib_dir], check=True)
+    r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0, r.stdout + r.stderr
+    assert r.stdout.startswith("ok ")
