@@ -139,10 +139,20 @@ int q3a_attn_decode(q3a_ctx *ctx, float *xb, const float *q, const float *kc,
  * can overlap on the GPU (other streams, other host threads) race and must be
  * serialised by the caller.  Work is queued on `cuda_stream` (a
  * cudaStream_t, NULL for the legacy default stream) and the call returns
- * without waiting for it. */
+ * without waiting for it.  Each call clears the array's error word before
+ * its launch; q3a_noalloc_check_error reports what the last launch left.
+ * The stored array address belongs to the device's context: do not use
+ * this entry point on a device after cudaDeviceReset. */
 int q3a_attn_decode_noalloc(float *xb, const float *q, const float *kc, const float *vc,
                             size_t loff, int pos, int n_heads, int kv_mul, int hd, int kv_dim,
                             int max_seq, void *cuda_stream);
+
+/* Companion of q3a_attn_decode_noalloc, allocating nothing either: waits for
+ * `cuda_stream` and reads, then clears, the error word of the current
+ * device's fixed array.  Q3A_ERR_TIMEOUT if a bounded wait inside the last
+ * noalloc launch expired (its xb is then not valid), else Q3A_OK.  No
+ * counterpart in the reference, which has no device-side waits. */
+int q3a_noalloc_check_error(void *cuda_stream);
 
 /* Batched ragged decode: n new tokens, token i belongs to cache slot
  * seq_ids[i] (distinct) at position pos[i] (host arrays).  The block of
@@ -238,6 +248,16 @@ int q3a_peer_open(q3a_ctx *ctx, int rank, int world, const void *handles);
 int q3a_attn_seqshard(q3a_ctx *ctx, float *xb, const float *q, int seq, int layer,
                       int n_local);
 
+/* Single-process form of the set-up above, for a host that drives every
+ * rank's context from one process (one context per GPU with peer access
+ * enabled between the devices by the caller, or several on one device):
+ * after q3a_peer_export on every context, q3a_peer_buffer gives each
+ * context's receive buffer as a device pointer, and
+ * q3a_peer_open_ptrs(ctx, rank, world, bufs) takes all ranks' buffers in rank
+ * order instead of IPC handles.  No counterpart in the reference. */
+int q3a_peer_buffer(q3a_ctx *ctx, void **buf);
+int q3a_peer_open_ptrs(q3a_ctx *ctx, int rank, int world, void *const *bufs);
+
 /* All-gather of column slices over peer memory (NVLink), for KV-head shards:
  * rank r computed columns [col0_r, col0_r + col_bytes) of every row of a
  * row-major matrix (its query heads' slice of xb or of a prefill output);
@@ -265,6 +285,24 @@ int q3a_peer_register(q3a_ctx *ctx, void *buf, size_t bytes, void *handle);
 int q3a_peer_register_open(q3a_ctx *ctx, int rank, int world, const void *handles);
 int q3a_gather_cols(q3a_ctx *ctx, size_t off, long long rows, size_t row_bytes, size_t col0,
                     size_t col_bytes);
+
+/* Single-process form of q3a_peer_register_open: after q3a_peer_register on
+ * every context, q3a_peer_register_flags gives each context's flag block, and
+ * q3a_peer_register_open_ptrs takes all ranks' registered buffers (the `buf`
+ * each passed to q3a_peer_register) and flag blocks in rank order. */
+int q3a_peer_register_flags(q3a_ctx *ctx, void **flags);
+int q3a_peer_register_open_ptrs(q3a_ctx *ctx, int rank, int world, void *const *bufs,
+                                void *const *flags);
+
+/* Limit of every device-side wait of this context's kernels on another CTA
+ * or another rank (the split-KV merge, the sequence-shard exchange, the
+ * column all-gather), in seconds at the device's highest SM clock; 0 restores
+ * the default of about one second.  A wait that runs out stops the kernel,
+ * which leaves its output unwritten and the device error flag set
+ * (q3a_check_device_error gives Q3A_ERR_TIMEOUT); the context stays usable.
+ * Replaces the reference's HIPCHK exit (qwen3-8b/gpu/main.c:47-53), which has
+ * no device-side waits at all. */
+int q3a_set_wait_limit(q3a_ctx *ctx, double seconds);
 
 /* Seeded N(0,1) fill of n elements (fp32 or bf16 by out_dtype): element i is
  * the Box-Muller transform of uniforms u(2j), u(2j+1), j = (offset+i)/2, with

@@ -20,31 +20,48 @@
 /* qwen3-8b/cpu/main.c:1175-1183; cpu-multicore/main.c:1180-1189 adds the
  * per-head OpenMP loop.  Sequential sum of squares per head, then
  * v *= (1/sqrtf(ss/hd + eps)) * w[i]. */
+static void norm_head(float *seg, const float *w, int hd, float eps) {
+    float ss = 0.0f;
+    for (int i = 0; i < hd; i++) ss += seg[i] * seg[i];
+    ss = 1.0f / sqrtf(ss / hd + eps);
+    for (int i = 0; i < hd; i++) seg[i] *= ss * w[i];
+}
+
 void orc_rmsnorm_head(float *vec, const float *w, int n_heads, int hd, float eps) {
     #pragma omp parallel for schedule(static)
-    for (int h = 0; h < n_heads; h++) {
-        float *seg = vec + (size_t)h * hd;
-        float ss = 0.0f;
-        for (int i = 0; i < hd; i++) ss += seg[i] * seg[i];
-        ss = 1.0f / sqrtf(ss / hd + eps);
-        for (int i = 0; i < hd; i++) seg[i] *= ss * w[i];
-    }
+    for (int h = 0; h < n_heads; h++) norm_head(vec + (size_t)h * hd, w, hd, eps);
 }
 
 /* qwen3-8b/cpu/main.c:1282-1295: adjacent pairs (2i, 2i+1) rotated by
  * pos * theta^(-2i/hd), angle and trig in fp32. */
+static void rope_head(float *seg, int hd, int pos, float theta) {
+    for (int i = 0; i < hd; i += 2) {
+        float freq = 1.0f / powf(theta, (float)i / hd);
+        float val = pos * freq;
+        float cr = cosf(val);
+        float ci = sinf(val);
+        float v0 = seg[i], v1 = seg[i + 1];
+        seg[i] = v0 * cr - v1 * ci;
+        seg[i + 1] = v0 * ci + v1 * cr;
+    }
+}
+
 void orc_rope(float *vec, int n_heads, int hd, int pos, float theta) {
     #pragma omp parallel for schedule(static)
-    for (int h = 0; h < n_heads; h++) {
-        for (int i = 0; i < hd; i += 2) {
-            float freq = 1.0f / powf(theta, (float)i / hd);
-            float val = pos * freq;
-            float cr = cosf(val);
-            float ci = sinf(val);
-            int idx = h * hd + i;
-            float v0 = vec[idx], v1 = vec[idx + 1];
-            vec[idx] = v0 * cr - v1 * ci;
-            vec[idx + 1] = v0 * ci + v1 * cr;
+    for (int h = 0; h < n_heads; h++) rope_head(vec + (size_t)h * hd, hd, pos, theta);
+}
+
+/* orc_rmsnorm_head then orc_rope on n consecutive rows [n][n_heads*hd], row t
+ * at position pos0 + t: the same per-head arithmetic, parallel over rows
+ * (a test-speed helper for building long synthetic caches). */
+void orc_prep_rows(float *rows, const float *w, int n, int n_heads, int hd, int pos0,
+                   float eps, float theta) {
+    #pragma omp parallel for schedule(static)
+    for (int t = 0; t < n; t++) {
+        for (int h = 0; h < n_heads; h++) {
+            float *seg = rows + ((size_t)t * n_heads + h) * hd;
+            norm_head(seg, w, hd, eps);
+            rope_head(seg, hd, pos0 + t, theta);
         }
     }
 }
@@ -148,6 +165,7 @@ static float bf16_round1(float f) {
 }
 
 void orc_bf16_round(float *x, size_t n) {
+    #pragma omp parallel for schedule(static)
     for (size_t i = 0; i < n; i++) x[i] = bf16_round1(x[i]);
 }
 

@@ -27,6 +27,8 @@ void orc_rmsnorm_head(float *vec, const float *w, int n_heads, int hd, float eps
 
 /* qwen3-8b/cpu/main.c:1282-1295 (OpenMP copy cpu-multicore/main.c:1293-1307) */
 void orc_rope(float *vec, int n_heads, int hd, int pos, float theta);
+void orc_prep_rows(float *rows, const float *w, int n, int n_heads, int hd, int pos0,
+                   float eps, float theta);
 
 /* qwen3-8b/cpu/main.c:1185-1195 */
 void orc_softmax(float *x, int n);

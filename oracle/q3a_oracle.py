@@ -38,6 +38,7 @@ def lib():
         L = ctypes.CDLL(LIB_PATH)
         L.orc_rmsnorm_head.argtypes = [_P, _P, _I, _I, _F]
         L.orc_rope.argtypes = [_P, _I, _I, _I, _F]
+        L.orc_prep_rows.argtypes = [_P, _P, _I, _I, _I, _I, _F, _F]
         L.orc_softmax.argtypes = [_P, _I]
         L.orc_attn_decode.argtypes = [_P, _P, _P, _P, _P, _SZ, _I, _I, _I, _I, _I, _I]
         L.orc_attn_block.argtypes = [_P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I,
@@ -163,11 +164,11 @@ def make_cache(seed: int, layer: int, n_tok: int, n_kv: int, hd: int, max_seq: i
         kw = np.ones(hd, np.float32)
     kraw = randn(n_tok * kv_dim, seed, layer * 16 + 1)
     vraw = randn(n_tok * kv_dim, seed, layer * 16 + 2)
-    for t in range(n_tok):
-        row = kraw[t * kv_dim:(t + 1) * kv_dim].copy()
-        rmsnorm_head(row, kw, n_kv, hd, eps)
-        rope(row, n_kv, hd, t, theta)
-        kc[t * kv_dim:(t + 1) * kv_dim] = row
+    kc[: n_tok * kv_dim] = kraw
+    if n_tok > 0:
+        # rmsnorm_head then rope at t, row by row (the same per-head arithmetic)
+        lib().orc_prep_rows(_ptr(kc), _ptr(np.ascontiguousarray(kw, np.float32)), n_tok, n_kv,
+                            hd, 0, eps, theta)
     vc[: n_tok * kv_dim] = vraw
     if bf16:
         kc = bf16_round(kc)

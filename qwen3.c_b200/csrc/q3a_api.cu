@@ -9,6 +9,8 @@
 #include <string.h>
 
 #include <algorithm>
+#include <mutex>
+#include <utility>
 #include <vector>
 
 #include "q3a_common.cuh"
@@ -99,6 +101,7 @@ struct q3a_ctx {
     cudaStream_t own_stream = nullptr;
     cudaStream_t stream = nullptr;
     int num_sms = 148;
+    long long wait_limit = WAIT_LIMIT_CYCLES;  // SM clocks per wait on another CTA / rank
     CUtensorMap tmK, tmV;          // decode maps of the paged cache
     float inv_freq[64];
     float* d_inv_freq = nullptr;   // the same table in device memory
@@ -116,6 +119,7 @@ struct q3a_ctx {
     float* peer_buf = nullptr;            // this rank's receive buffer
     float* peer_ptrs[PEER_MAX] = {};      // every rank's buffer, mapped here
     unsigned* peer_epoch = nullptr;       // call counter + finisher ticket
+    bool peer_ipc = false;                // peer_ptrs are IPC mappings (closed on destroy)
     // registered caller buffer for column all-gathers (q3a_peer_register)
     uint8_t* reg_buf = nullptr;           // the caller's buffer
     size_t reg_bytes = 0;
@@ -188,11 +192,27 @@ extern "C" const char* q3a_last_error(void) { return g_err; }
 // unit of the library and returns `code`.
 int q3a::record_error(int code, const char* msg) { return fail(code, "%s", msg); }
 
+cudaError_t q3a::ensure_smem_attr(const void* fn, int bytes) {
+    static std::mutex mu;
+    static std::vector<std::pair<const void*, int>> done;  // (kernel, device) pairs set
+    int dev = -1;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    std::lock_guard<std::mutex> lock(mu);
+    for (const auto& d : done)
+        if (d.first == fn && d.second == dev) return cudaSuccess;
+    e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e != cudaSuccess) return e;
+    done.emplace_back(fn, dev);
+    return cudaSuccess;
+}
+
 static void destroy_ctx(q3a_ctx* c) {
     if (!c) return;
     if (c->stream) cudaStreamSynchronize(c->stream);
     for (int r = 0; r < PEER_MAX; r++)
-        if (c->peer_ptrs[r] && c->peer_ptrs[r] != c->peer_buf) cudaIpcCloseMemHandle(c->peer_ptrs[r]);
+        if (c->peer_ipc && c->peer_ptrs[r] && c->peer_ptrs[r] != c->peer_buf)
+            cudaIpcCloseMemHandle(c->peer_ptrs[r]);
     cudaFree(c->peer_buf);
     cudaFree(c->peer_epoch);
     for (int r = 0; r < PEER_MAX; r++) {
@@ -373,6 +393,25 @@ extern "C" int q3a_check_device_error(q3a_ctx* c) {
 
 extern "C" uint64_t q3a_launch_count(const q3a_ctx* c) { return c ? c->launches : 0; }
 
+extern "C" int q3a_set_wait_limit(q3a_ctx* c, double seconds) {
+    if (!c) return fail(Q3A_ERR_INVALID, "null context");
+    if (!(seconds >= 0.0) || seconds > 60.0)
+        return fail(Q3A_ERR_INVALID, "wait limit %g s outside [0, 60]", seconds);
+    if (seconds == 0.0) {
+        c->wait_limit = WAIT_LIMIT_CYCLES;
+        return Q3A_OK;
+    }
+    int rc = ensure_device(c);
+    if (rc) return rc;
+    // clock64 counts SM clocks: the limit in clocks at the device's highest
+    // SM clock (at lower clocks the wait lasts proportionally longer)
+    int khz = 0;
+    if (cudaDeviceGetAttribute(&khz, cudaDevAttrClockRate, c->cfg.device) != cudaSuccess || khz <= 0)
+        khz = 2000000;
+    c->wait_limit = std::max(1LL, (long long)(seconds * khz * 1000.0));
+    return Q3A_OK;
+}
+
 // ------------------------------------------------------------------ decode dispatch
 static void base_params(q3a_ctx* c, DecodeParams& p, int layer) {
     memset(&p, 0, sizeof(p));
@@ -396,6 +435,7 @@ static void base_params(q3a_ctx* c, DecodeParams& p, int layer) {
     p.n_pages = c->n_pages;
     p.cache_mode = CACHE_PAGED;
     p.inv_freq = c->d_inv_freq;
+    p.wait_limit = c->wait_limit;
 }
 
 // Piece-mode schedule: every (sequence, kv head) group gets k_g >= 1 CTAs in
@@ -844,7 +884,31 @@ extern "C" int q3a_peer_open(q3a_ctx* c, int rank, int world, const void* handle
             return fail(Q3A_ERR_CUDA, "cannot map the buffer of rank %d", r);
         }
         c->peer_ptrs[r] = reinterpret_cast<float*>(p);
+        c->peer_ipc = true;
     }
+    c->peer_rank = rank;
+    return Q3A_OK;
+}
+
+extern "C" int q3a_peer_buffer(q3a_ctx* c, void** buf) {
+    g_err[0] = 0;
+    if (!c || !buf) return fail(Q3A_ERR_INVALID, "null argument");
+    if (!c->peer_buf) return fail(Q3A_ERR_INVALID, "q3a_peer_export must come first");
+    *buf = c->peer_buf;
+    return Q3A_OK;
+}
+
+extern "C" int q3a_peer_open_ptrs(q3a_ctx* c, int rank, int world, void* const* bufs) {
+    g_err[0] = 0;
+    if (!c || !bufs) return fail(Q3A_ERR_INVALID, "null argument");
+    if (!c->peer_buf || world != c->peer_world)
+        return fail(Q3A_ERR_INVALID, "q3a_peer_export(ctx, %d, ...) must come first", world);
+    if (rank < 0 || rank >= world) return fail(Q3A_ERR_INVALID, "rank %d of %d", rank, world);
+    if (c->peer_rank >= 0) return fail(Q3A_ERR_INVALID, "peers already open");
+    if (bufs[rank] != c->peer_buf) return fail(Q3A_ERR_INVALID, "bufs[%d] is not this context's buffer", rank);
+    for (int r = 0; r < world; r++)
+        if (!bufs[r]) return fail(Q3A_ERR_INVALID, "bufs[%d] is null", r);
+    for (int r = 0; r < world; r++) c->peer_ptrs[r] = reinterpret_cast<float*>(bufs[r]);
     c->peer_rank = rank;
     return Q3A_OK;
 }
@@ -932,6 +996,35 @@ extern "C" int q3a_peer_register_open(q3a_ctx* c, int rank, int world, const voi
     return Q3A_OK;
 }
 
+extern "C" int q3a_peer_register_flags(q3a_ctx* c, void** flags) {
+    g_err[0] = 0;
+    if (!c || !flags) return fail(Q3A_ERR_INVALID, "null argument");
+    if (!c->reg_flags) return fail(Q3A_ERR_INVALID, "q3a_peer_register must come first");
+    *flags = c->reg_flags;
+    return Q3A_OK;
+}
+
+extern "C" int q3a_peer_register_open_ptrs(q3a_ctx* c, int rank, int world, void* const* bufs,
+                                           void* const* flags) {
+    g_err[0] = 0;
+    if (!c || !bufs || !flags) return fail(Q3A_ERR_INVALID, "null argument");
+    if (!c->reg_buf) return fail(Q3A_ERR_INVALID, "q3a_peer_register must come first");
+    if (world < 1 || world > PEER_MAX || rank < 0 || rank >= world)
+        return fail(Q3A_ERR_INVALID, "rank %d of %d", rank, world);
+    if (c->reg_rank >= 0) return fail(Q3A_ERR_INVALID, "peers already open");
+    if (bufs[rank] != c->reg_buf || flags[rank] != c->reg_flags)
+        return fail(Q3A_ERR_INVALID, "entry %d is not this context's registration", rank);
+    for (int r = 0; r < world; r++)
+        if (!bufs[r] || !flags[r]) return fail(Q3A_ERR_INVALID, "entry %d is null", r);
+    for (int r = 0; r < world; r++) {
+        c->reg_peer[r] = reinterpret_cast<uint8_t*>(bufs[r]);
+        c->reg_peer_flags[r] = reinterpret_cast<unsigned*>(flags[r]);
+    }
+    c->reg_world = world;
+    c->reg_rank = rank;
+    return Q3A_OK;
+}
+
 extern "C" int q3a_gather_cols(q3a_ctx* c, size_t off, long long rows, size_t row_bytes, size_t col0,
                                size_t col_bytes) {
     g_err[0] = 0;
@@ -960,6 +1053,7 @@ extern "C" int q3a_gather_cols(q3a_ctx* c, size_t off, long long rows, size_t ro
     p.col0 = (long long)col0;
     p.vecs = (int)(col_bytes / 16);
     p.err = c->err;
+    p.wait_limit = c->wait_limit;
     const long long work = rows * p.vecs;
     const int n_ctas = (int)std::min<long long>(c->num_sms, std::max<long long>(1, (work + 255) / 256));
     CUDA_TRY(launch_gather_cols(p, n_ctas, c->stream));

@@ -459,13 +459,15 @@ __device__ __forceinline__ unsigned long long ld_word_sys(const unsigned long lo
     asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
     return w;
 }
-// Bounded wait for the word of call `ep`; false on timeout.
-__device__ __forceinline__ bool wait_word(const unsigned long long* p, unsigned ep, float& v) {
+// Bounded wait (`limit` SM clocks) for the word of call `ep`; false on
+// timeout.
+__device__ __forceinline__ bool wait_word(const unsigned long long* p, unsigned ep, float& v,
+                                          long long limit) {
     unsigned long long w = ld_word_sys(p);
     if ((unsigned)(w >> 32) != ep) {
         const long long t0 = clock64();
         do {
-            if (clock64() - t0 > WAIT_LIMIT_CYCLES) return false;
+            if (clock64() - t0 > limit) return false;
             w = ld_word_sys(p);
         } while ((unsigned)(w >> 32) != ep);
     }
@@ -505,12 +507,12 @@ __device__ __forceinline__ void lse_fold(float& M, float& W, float& A, float m2,
 // j = sub, sub + tpv, ... < n at base + j*stride + off_o / off_l, waits
 // (bounded) until each carries `tag`, and folds them; then the tpv lanes of
 // its value (consecutive lanes of one warp) combine by shuffles.  Returns
-// false when a word did not arrive within the limit.
+// false when a word did not arrive within `limit` SM clocks.
 template <bool SYS>
 __device__ __forceinline__ bool spread_gather(const unsigned long long* base, size_t stride, int n,
                                               int sub, int tpv, bool active, size_t off_o,
                                               size_t off_l, unsigned tag, float& M, float& W,
-                                              float& A) {
+                                              float& A, long long limit) {
     unsigned long long wo[SPREAD_MAXJ], wl[SPREAD_MAXJ];
     unsigned pend = 0;
 #pragma unroll
@@ -531,7 +533,7 @@ __device__ __forceinline__ bool spread_gather(const unsigned long long* base, si
             if (((pend >> u) & 1u) && (unsigned)(wo[u] >> 32) == tag && (unsigned)(wl[u] >> 32) == tag)
                 pend &= ~(1u << u);
         if (pend == 0) break;
-        if (clock64() - t0 > WAIT_LIMIT_CYCLES) {
+        if (clock64() - t0 > limit) {
             ok = false;
             break;
         }
@@ -567,12 +569,12 @@ __device__ __forceinline__ bool spread_gather(const unsigned long long* base, si
 // gather that follows, which waits again and reports it.
 template <bool SYS>
 __device__ __forceinline__ void wait_sentinels(const unsigned long long* base, size_t stride, int n,
-                                               int lane, unsigned tag) {
+                                               int lane, unsigned tag, long long limit) {
     const long long t0 = clock64();
     for (int j = lane; j < n; j += 32) {
         const unsigned long long* p = base + (size_t)j * stride;
         while ((unsigned)(ld_word<SYS>(p) >> 32) != tag) {
-            if (clock64() - t0 > WAIT_LIMIT_CYCLES) return;
+            if (clock64() - t0 > limit) return;
         }
     }
 }
@@ -1166,11 +1168,12 @@ __global__ void __launch_bounds__(DecCfg<KV, TC>::NTHREADS, 1)
             // once instead of being polled by every thread
             if (warp == 0)
                 wait_sentinels<false>(P.words + (size_t)s.slot0 * PART_STRIDE + GQA * HD + GQA - 1,
-                                      PART_STRIDE, k, lane, tag);
+                                      PART_STRIDE, k, lane, tag, P.wait_limit);
             named_bar_sync(1, C::NCONS);
             float Mv, Wv, Av;
             bool ok = spread_gather<false>(P.words + (size_t)s.slot0 * PART_STRIDE, PART_STRIDE, k,
-                                           sub, tpv, act, v, GQA * HD + vh, tag, Mv, Wv, Av);
+                                           sub, tpv, act, v, GQA * HD + vh, tag, Mv, Wv, Av,
+                                           P.wait_limit);
             float ov = Av / Wv, lv = Mv + log2f(Wv);
             const int gh = hq0 + vh;
             unsigned pep = 0;
@@ -1196,10 +1199,11 @@ __global__ void __launch_bounds__(DecCfg<KV, TC>::NTHREADS, 1)
                     reinterpret_cast<const unsigned long long*>(P.peer_recv[R]) + (size_t)par * Wr * row;
                 if (warp == 0)
                     wait_sentinels<true>(src + (size_t)P.hq_total * HD + hq0 + (v0 >> 7), row, Wr, lane,
-                                         pep);
+                                         pep, P.wait_limit);
                 named_bar_sync(1, C::NCONS);
                 ok = spread_gather<true>(src, row, Wr, sub, tpv, act && ok, (size_t)gh * HD + vd,
-                                         (size_t)P.hq_total * HD + gh, pep, Mv, Wv, Av) && ok;
+                                         (size_t)P.hq_total * HD + gh, pep, Mv, Wv, Av,
+                                         P.wait_limit) && ok;
                 ov = Av / Wv;
                 lv = Mv + log2f(Wv);
             }
@@ -1313,9 +1317,9 @@ __global__ void __launch_bounds__(DecCfg<KV, TC>::NTHREADS, 1)
                         lr[r] = __uint_as_float((unsigned)wl[u]);
                         x0[r] = __uint_as_float((unsigned)w0[u]);
                         x1[r] = __uint_as_float((unsigned)w1[u]);
-                        if ((unsigned)(wl[u] >> 32) != ep) ok = ok && wait_word(sr + P.hq_total * HD + gh, ep, lr[r]);
-                        if ((unsigned)(w0[u] >> 32) != ep) ok = ok && wait_word(sr + gh * HD + d, ep, x0[r]);
-                        if ((unsigned)(w1[u] >> 32) != ep) ok = ok && wait_word(sr + gh * HD + d + 1, ep, x1[r]);
+                        if ((unsigned)(wl[u] >> 32) != ep) ok = ok && wait_word(sr + P.hq_total * HD + gh, ep, lr[r], P.wait_limit);
+                        if ((unsigned)(w0[u] >> 32) != ep) ok = ok && wait_word(sr + gh * HD + d, ep, x0[r], P.wait_limit);
+                        if ((unsigned)(w1[u] >> 32) != ep) ok = ok && wait_word(sr + gh * HD + d + 1, ep, x1[r], P.wait_limit);
                     }
                 }
             }
@@ -1370,13 +1374,9 @@ template <typename KV, bool SPREAD, bool TC>
 static cudaError_t launch_decode_t(const DecodeParams& p, const CUtensorMap& tmK,
                                    const CUtensorMap& tmV, cudaStream_t st) {
     using C = DecCfg<KV, TC>;
-    static bool attr_set = false;
-    if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(decode_kernel<KV, SPREAD, TC>,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
-        if (e != cudaSuccess) return e;
-        attr_set = true;
-    }
+    cudaError_t e = ensure_smem_attr(reinterpret_cast<const void*>(decode_kernel<KV, SPREAD, TC>),
+                                     C::SMEM);
+    if (e != cudaSuccess) return e;
     // programmatic dependent launch: scheduled while the previous kernel of
     // the stream finishes; the kernel waits for it before touching memory
     cudaLaunchConfig_t cfg = {};

@@ -44,7 +44,7 @@ __device__ __forceinline__ bool wait_all_ranks(const ColGatherParams& P, int pha
     const long long t0 = clock64();
     for (int r = 0; r < P.world; r++) {
         while ((int)(ld_acquire_sys(P.flags + phase * PEER_MAX + r) - ep) < 0) {
-            if (clock64() - t0 > WAIT_LIMIT_CYCLES) return false;
+            if (clock64() - t0 > P.wait_limit) return false;
         }
     }
     return true;
@@ -65,7 +65,7 @@ __global__ void __launch_bounds__(256) gather_cols_kernel(const __grid_constant_
         } else {
             const long long t0 = clock64();
             while ((int)(ld_acquire_gpu(P.state + 2) - ep) < 0) {
-                if (clock64() - t0 > WAIT_LIMIT_CYCLES) {
+                if (clock64() - t0 > P.wait_limit) {
                     ok = false;
                     break;
                 }

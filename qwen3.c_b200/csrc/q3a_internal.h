@@ -88,6 +88,7 @@ struct DecodeParams {
     unsigned long long* words;   // spread merge: MAX_PIECES slots of PART_STRIDE tagged words
     unsigned* group_epoch;   // spread merge: call number per group [MAX_PIECES]
     const float* inv_freq;   // [64] RoPE inverse frequencies (host powf, reference formula)
+    long long wait_limit;    // SM clocks a wait on another CTA or rank may take
     Piece pieces[MAX_PIECES];
     int t_begin[MAX_B];      // first cache position attended per sequence
     int t_end[MAX_B];        // one past the last cache position read from the cache
@@ -133,6 +134,11 @@ struct AppendParams {
     const float* inv_freq;   // [64] device table
 };
 
+// Raises the dynamic shared-memory limit of kernel `fn` to `bytes` on the
+// current device.  The attribute is per device, so it is set once per
+// (kernel, device) pair; safe to call from several host threads.
+cudaError_t ensure_smem_attr(const void* fn, int bytes);
+
 // ---------------------------------------------------------------- launchers
 // All return a cudaError_t of the launch.
 cudaError_t launch_decode(const DecodeParams& p, const CUtensorMap& tmK, const CUtensorMap& tmV,
@@ -160,6 +166,7 @@ struct ColGatherParams {
     long long col0;                // bytes
     int vecs;                      // 16-byte vectors per row slice
     int* err;
+    long long wait_limit;          // SM clocks a wait on another rank or CTA may take
 };
 cudaError_t launch_gather_cols(const ColGatherParams& p, int n_ctas, cudaStream_t st);
 

@@ -64,13 +64,28 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t,
 // clears counters and error word again before its launch.
 static __device__ __align__(256) unsigned char q3a_noalloc_scratch[NOALLOC_BYTES];
 
+static EncodeTiledFn g_encode = nullptr;  // cuTensorMapEncodeTiled, resolved once per process
+
 // Once per device, with that device current: the device address of the
 // scratch array (in host code the symbol names a host-side stand-in, not
-// device memory) and the SM count.
+// device memory) and the SM count; once per process, the driver's tensor-map
+// encoder.  The stored address belongs to the device's current context: a
+// cudaDeviceReset destroys that context (and the module holding the array),
+// so this entry point must not be used on a device after it was reset.
 static int noalloc_setup(int dev, DeviceScratch** out) {
     if (dev < 0 || dev >= MAX_DEVICES)
         return record_error(Q3A_ERR_UNSUPPORTED, "q3a_attn_decode_noalloc: device ordinal too large");
     std::lock_guard<std::mutex> lock(g_setup_mutex);
+    if (!g_encode) {
+        void* fnp = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fnp, cudaEnableDefault, &q) !=
+                cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            return record_error(Q3A_ERR_CUDA,
+                                "q3a_attn_decode_noalloc: cuTensorMapEncodeTiled unavailable");
+        g_encode = reinterpret_cast<EncodeTiledFn>(fnp);
+    }
     DeviceScratch& d = g_devices[dev];
     if (!d.ready) {
         void* p = nullptr;
@@ -91,20 +106,14 @@ static int noalloc_setup(int dev, DeviceScratch** out) {
 }
 
 static int noalloc_map(CUtensorMap* m, const float* base, uint64_t cols, uint64_t rows) {
-    void* fnp = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fnp, cudaEnableDefault, &q) !=
-            cudaSuccess ||
-        q != cudaDriverEntryPointSuccess)
-        return record_error(Q3A_ERR_CUDA, "q3a_attn_decode_noalloc: cuTensorMapEncodeTiled unavailable");
-    EncodeTiledFn fn = reinterpret_cast<EncodeTiledFn>(fnp);
     cuuint64_t dims[2] = {cols, rows};
     cuuint64_t strides[1] = {cols * sizeof(float)};
     cuuint32_t box[2] = {HD, DEC_BOX};
     cuuint32_t estr[2] = {1, 1};
-    if (fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box,
-           estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    if (g_encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides,
+                 box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) !=
+        CUDA_SUCCESS)
         return record_error(Q3A_ERR_CUDA, "q3a_attn_decode_noalloc: tensor map encoding failed");
     return Q3A_OK;
 }
@@ -163,6 +172,7 @@ extern "C" int q3a_attn_decode_noalloc(float* xb, const float* q, const float* k
     p.nkv_total = nkv;
     p.cache_mode = CACHE_POSMAJOR;
     p.fused = 0;
+    p.wait_limit = WAIT_LIMIT_CYCLES;
     p.t_begin[0] = 0;
     p.t_end[0] = pos + 1;
     p.unit_prefix[0] = 0;
@@ -207,4 +217,28 @@ extern "C" int q3a_attn_decode_noalloc(float* xb, const float* q, const float* k
     if (launch_decode(p, tk, tv, false, st) != cudaSuccess)
         return record_error(Q3A_ERR_CUDA, "q3a_attn_decode_noalloc: kernel launch failed");
     return Q3A_OK;
+}
+
+// Reads and clears the error word a bounded wait of the last noalloc launch
+// on this device may have set: queued on `stream` behind that launch, then
+// the host waits for the stream.  Nothing is allocated: the word is read
+// into a host variable and cleared in place.
+extern "C" int q3a_noalloc_check_error(void* stream) {
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess)
+        return record_error(Q3A_ERR_CUDA, "q3a_noalloc_check_error: no current device");
+    DeviceScratch* ds = nullptr;
+    int rc = noalloc_setup(dev, &ds);
+    if (rc) return rc;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    int h = 0;
+    if (cudaMemcpyAsync(&h, ds->base + NOALLOC_ERR_OFF, sizeof(int), cudaMemcpyDeviceToHost, st) !=
+            cudaSuccess ||
+        cudaStreamSynchronize(st) != cudaSuccess)
+        return record_error(Q3A_ERR_CUDA, "q3a_noalloc_check_error: reading the error word failed");
+    if (h == 0) return Q3A_OK;
+    if (cudaMemsetAsync(ds->base + NOALLOC_ERR_OFF, 0, sizeof(int), st) != cudaSuccess ||
+        cudaStreamSynchronize(st) != cudaSuccess)
+        return record_error(Q3A_ERR_CUDA, "q3a_noalloc_check_error: clearing the error word failed");
+    return record_error(Q3A_ERR_TIMEOUT, "q3a_attn_decode_noalloc: a bounded device wait expired");
 }

@@ -733,14 +733,7 @@ __global__ void __launch_bounds__(256)
 
 template <bool SPLIT>
 static cudaError_t set_prefill_attr() {
-    static bool attr_set = false;
-    if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(prefill_kernel<SPLIT>,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize, pf::SMEM);
-        if (e != cudaSuccess) return e;
-        attr_set = true;
-    }
-    return cudaSuccess;
+    return ensure_smem_attr(reinterpret_cast<const void*>(prefill_kernel<SPLIT>), pf::SMEM);
 }
 
 cudaError_t launch_prefill(const PrefillParams& p, const CUtensorMap& tmQ, cudaStream_t st) {

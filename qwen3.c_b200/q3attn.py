@@ -28,9 +28,11 @@ EXPORTS = [
     "q3a_attn_layer_batched", "q3a_kv_append", "q3a_kv_load", "q3a_kv_read", "q3a_prefill",
     "q3a_prefill_attn", "q3a_attn_partial", "q3a_lse_combine", "q3a_lse_combine_packed",
     "q3a_peer_export", "q3a_peer_open", "q3a_attn_seqshard",
+    "q3a_peer_buffer", "q3a_peer_open_ptrs",
     "q3a_peer_register", "q3a_peer_register_open", "q3a_gather_cols",
+    "q3a_peer_register_flags", "q3a_peer_register_open_ptrs", "q3a_set_wait_limit",
     "q3a_randn",
-    "q3a_launch_count", "q3a_attn_decode_noalloc",
+    "q3a_launch_count", "q3a_attn_decode_noalloc", "q3a_noalloc_check_error",
 ]
 
 
@@ -88,8 +90,15 @@ def load():
         L.q3a_peer_register.argtypes = [_P, _P, _SZ, _P]
         L.q3a_peer_register_open.argtypes = [_P, _I, _I, _P]
         L.q3a_gather_cols.argtypes = [_P, _SZ, ctypes.c_longlong, _SZ, _SZ, _SZ]
+        L.q3a_peer_buffer.argtypes = [_P, ctypes.POINTER(_P)]
+        L.q3a_peer_open_ptrs.argtypes = [_P, _I, _I, ctypes.POINTER(_P)]
+        L.q3a_peer_register_flags.argtypes = [_P, ctypes.POINTER(_P)]
+        L.q3a_peer_register_open_ptrs.argtypes = [_P, _I, _I, ctypes.POINTER(_P),
+                                                  ctypes.POINTER(_P)]
+        L.q3a_set_wait_limit.argtypes = [_P, ctypes.c_double]
         L.q3a_randn.argtypes = [_P, _P, _I, _SZ, _U64, _U64, _U64]
         L.q3a_attn_decode_noalloc.argtypes = [_P, _P, _P, _P, _SZ, _I, _I, _I, _I, _I, _I, _P]
+        L.q3a_noalloc_check_error.argtypes = [_P]
         L.q3a_launch_count.argtypes = [_P]
         L.q3a_launch_count.restype = _U64
         _lib = L
@@ -118,6 +127,13 @@ def attn_decode_noalloc(xb, q, kc, vc, loff, pos, n_heads, kv_mul, hd, kv_dim, m
     allocated; queued on the given CUDA stream handle."""
     check(load().q3a_attn_decode_noalloc(ptr(xb), ptr(q), ptr(kc), ptr(vc), loff, pos, n_heads,
                                          kv_mul, hd, kv_dim, max_seq, stream_handle))
+
+
+def noalloc_check_error(stream_handle=None):
+    """q3a_noalloc_check_error: waits for the stream, then reads and clears
+    the fixed array's device error word (Q3AError with ERR_TIMEOUT if a
+    bounded wait of the last noalloc launch expired)."""
+    check(load().q3a_noalloc_check_error(stream_handle))
 
 
 def default_cfg(**kw) -> Cfg:
@@ -220,6 +236,17 @@ class Context:
         buf = ctypes.create_string_buffer(blob, len(blob))
         check(self.lib.q3a_peer_open(self.h, rank, world, buf))
 
+    def peer_buffer(self) -> int:
+        """This context's receive buffer (device address), after peer_export."""
+        p = _P()
+        check(self.lib.q3a_peer_buffer(self.h, ctypes.byref(p)))
+        return p.value
+
+    def peer_open_ptrs(self, rank, world, bufs):
+        """Single-process set-up: every rank's peer_buffer() in rank order."""
+        arr = (_P * world)(*bufs)
+        check(self.lib.q3a_peer_open_ptrs(self.h, rank, world, arr))
+
     def attn_seqshard(self, xb, q, seq, layer, n_local):
         check(self.lib.q3a_attn_seqshard(self.h, ptr(xb), ptr(q), seq, layer, n_local))
 
@@ -235,6 +262,22 @@ class Context:
         blob = b"".join(handles)
         buf = ctypes.create_string_buffer(blob, len(blob))
         check(self.lib.q3a_peer_register_open(self.h, rank, world, buf))
+
+    def peer_register_flags(self) -> int:
+        """This context's gather flag block (device address), after peer_register."""
+        p = _P()
+        check(self.lib.q3a_peer_register_flags(self.h, ctypes.byref(p)))
+        return p.value
+
+    def peer_register_open_ptrs(self, rank, world, bufs, flags):
+        """Single-process set-up: every rank's registered buffer and flag
+        block, in rank order."""
+        b = (_P * world)(*bufs)
+        f = (_P * world)(*flags)
+        check(self.lib.q3a_peer_register_open_ptrs(self.h, rank, world, b, f))
+
+    def set_wait_limit(self, seconds: float):
+        check(self.lib.q3a_set_wait_limit(self.h, seconds))
 
     def gather_cols(self, off, rows, row_bytes, col0, col_bytes):
         check(self.lib.q3a_gather_cols(self.h, off, rows, row_bytes, col0, col_bytes))

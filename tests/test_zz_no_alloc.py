@@ -51,6 +51,9 @@ def test_noalloc_matches_context_entry_point_twice():
             ctx.attn_decode(want, dq, dk, dv, None, loff, pos, HQ, KV_MUL, HD, KV_DIM, max_seq)
             q3attn.attn_decode_noalloc(got, dq, dk, dv, loff, pos, HQ, KV_MUL, HD, KV_DIM,
                                        max_seq, stream.cuda_stream)
+            # no bounded wait of the launch expired (reads and clears the
+            # fixed array's error word, allocating nothing)
+            q3attn.noalloc_check_error(stream.cuda_stream)
             stream.synchronize()
             w = want.cpu().numpy()
             g = got.cpu().numpy()
@@ -70,3 +73,31 @@ def test_noalloc_rejects_shapes_beyond_its_scratch():
         q3attn.attn_decode_noalloc(buf, buf, buf, buf, 0, 0, 128, 4, 128, 32 * 128, 1)
     assert e.value.code == q3attn.ERR_INVALID
     assert "16 KV heads" in str(e.value)
+
+
+def test_noalloc_on_two_devices_in_one_process():
+    """The fixed array, its address and the kernel's shared-memory limit are
+    per device: one process calls the entry point on device 0, then on
+    device 1 (skipped with one GPU), each against the oracle."""
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    max_seq = 700
+    kc, vc = _inputs(77, 1, max_seq)
+    q = orc.randn(HQ * HD, 77, 52)
+    ref = orc.attn_decode(q, kc, vc, 0, max_seq - 1, HQ, KV_MUL, HD, KV_DIM, max_seq)
+    for d in (0, 1, 0):
+        dev = torch.device(f"cuda:{d}")
+        torch.cuda.set_device(dev)
+        stream = torch.cuda.Stream(device=dev)
+        dk = torch.from_numpy(kc).to(dev)
+        dv = torch.from_numpy(vc).to(dev)
+        dq = torch.from_numpy(q).to(dev)
+        got = torch.full((HQ * HD,), float("nan"), device=dev)
+        q3attn.attn_decode_noalloc(got, dq, dk, dv, 0, max_seq - 1, HQ, KV_MUL, HD, KV_DIM,
+                                   max_seq, stream.cuda_stream)
+        q3attn.noalloc_check_error(stream.cuda_stream)
+        g = got.cpu().numpy()
+        assert np.all(np.isfinite(g)), f"device {d}"
+        assert normwise(g, ref) <= TOL_F32_NORMWISE, f"device {d}"
+    torch.cuda.set_device(0)
