@@ -177,6 +177,16 @@ int q3a_kv_append(q3a_ctx *ctx, int seq, int layer, int pos0, int n, const float
 int q3a_kv_load(q3a_ctx *ctx, int seq, int layer, int pos0, int n, const float *k,
                 const float *v);
 
+/* Seeded synthetic cache rows, for harnesses and benchmarks that have no
+ * model data: raw k and v rows [n][n_kv*hd] ~ N(0,1) from the generator of
+ * q3a_randn (seed; streams stream_k, stream_v), stored at pos0.. exactly as
+ * q3a_kv_append stores raw rows with unit norm gains (QK-RMSNorm + RoPE of
+ * k at its position).  Generated on the device in the context's scratch, in
+ * either pointer mode.  No counterpart in the reference, which fills its
+ * cache only from real tokens. */
+int q3a_kv_synth(q3a_ctx *ctx, int seq, int layer, int pos0, int n, uint64_t seed,
+                 uint64_t stream_k, uint64_t stream_v);
+
 /* Reads cache rows back as fp32 position-major [n][n_kv*hd]. */
 int q3a_kv_read(q3a_ctx *ctx, int seq, int layer, int pos0, int n, float *k, float *v);
 
@@ -303,6 +313,18 @@ int q3a_peer_register_open_ptrs(q3a_ctx *ctx, int rank, int world, void *const *
  * Replaces the reference's HIPCHK exit (qwen3-8b/gpu/main.c:47-53), which has
  * no device-side waits at all. */
 int q3a_set_wait_limit(q3a_ctx *ctx, double seconds);
+
+/* Decode work split.  By default (on = 0) the ranges of a (sequence, KV
+ * head) group balance their work at run time: each streams a few fixed
+ * units of cache rows and then claims the group's remaining units one at a
+ * time, so ranges on SMs with lower memory throughput take fewer.  Which
+ * range sums which rows then varies from call to call, and results can
+ * differ in the last bits between identical calls (within the parity
+ * tolerances).  on = 1 gives every range a fixed row range: identical calls
+ * give bitwise-identical results, at some cost in speed.  The reference
+ * (single-threaded C loops) is deterministic; this switch has no
+ * counterpart there. */
+int q3a_set_deterministic(q3a_ctx *ctx, int on);
 
 /* Seeded N(0,1) fill of n elements (fp32 or bf16 by out_dtype): element i is
  * the Box-Muller transform of uniforms u(2j), u(2j+1), j = (offset+i)/2, with

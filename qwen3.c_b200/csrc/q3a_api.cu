@@ -93,6 +93,7 @@ struct q3a_ctx {
     int* counters = nullptr;
     unsigned long long* words = nullptr;  // spread-merge slots (tagged words)
     unsigned* group_epoch = nullptr;      // spread-merge call number per group
+    int* claims = nullptr;                // per-group unit counters of the balanced schedule
     float* pf_part = nullptr;             // prefill split partials (growable)
     size_t pf_part_floats = 0;
     int pf_key_tok = -1, pf_key_pos = -1; // prompt shape of the cached split choice
@@ -102,6 +103,7 @@ struct q3a_ctx {
     cudaStream_t stream = nullptr;
     int num_sms = 148;
     long long wait_limit = WAIT_LIMIT_CYCLES;  // SM clocks per wait on another CTA / rank
+    int deterministic = 0;         // 1: static row ranges (bitwise-repeatable results)
     CUtensorMap tmK, tmV;          // decode maps of the paged cache
     float inv_freq[64];
     float* d_inv_freq = nullptr;   // the same table in device memory
@@ -113,6 +115,14 @@ struct q3a_ctx {
     void* d_scratch = nullptr;
     size_t scratch_bytes = 0;
     uint64_t launches = 0;
+    // The last kernel this context queued, for the early cache streaming of
+    // the next decode launch: a decode kernel may read cache rows before its
+    // programmatic-dependency wait only when the kernel before it on the
+    // same stream was this context's decode of another layer (or one that
+    // appended nothing), so that no kernel still running can write them.
+    cudaStream_t last_stream = nullptr;
+    int last_decode_layer = -1;   // layer of the last launch if it was a decode, else -1
+    int last_decode_wrote = 0;    // that decode appended a row to its layer
     // peer-memory sequence shards (q3a_peer_export / q3a_peer_open)
     int peer_world = 0;
     int peer_rank = -1;
@@ -227,6 +237,7 @@ static void destroy_ctx(q3a_ctx* c) {
     cudaFree(c->counters);
     cudaFree(c->words);
     cudaFree(c->group_epoch);
+    cudaFree(c->claims);
     cudaFree(c->pf_part);
     cudaFree(c->err);
     cudaFree(c->d_inv_freq);
@@ -307,6 +318,7 @@ extern "C" int q3a_create(q3a_ctx** out, const q3a_cfg* cfg_in) {
         cudaMalloc(&c->counters, (size_t)max_groups * sizeof(int)) != cudaSuccess ||
         cudaMalloc(&c->words, (size_t)MAX_PIECES * PART_STRIDE * 8) != cudaSuccess ||
         cudaMalloc(&c->group_epoch, (size_t)MAX_PIECES * sizeof(unsigned)) != cudaSuccess ||
+        cudaMalloc(&c->claims, (size_t)MAX_PIECES * sizeof(int)) != cudaSuccess ||
         cudaMalloc(&c->err, sizeof(int)) != cudaSuccess ||
         cudaMalloc(&c->d_inv_freq, sizeof(c->inv_freq)) != cudaSuccess) {
         destroy_ctx(c);
@@ -323,6 +335,7 @@ extern "C" int q3a_create(q3a_ctx** out, const q3a_cfg* cfg_in) {
         cudaMemsetAsync(c->words, 0, (size_t)MAX_PIECES * PART_STRIDE * 8, c->stream) != cudaSuccess ||
         cudaMemsetAsync(c->group_epoch, 0, (size_t)MAX_PIECES * sizeof(unsigned), c->stream) !=
             cudaSuccess ||
+        cudaMemsetAsync(c->claims, 0, (size_t)MAX_PIECES * sizeof(int), c->stream) != cudaSuccess ||
         cudaMemsetAsync(c->err, 0, sizeof(int), c->stream) != cudaSuccess ||
         cudaMemcpyAsync(c->d_inv_freq, c->inv_freq, sizeof(c->inv_freq), cudaMemcpyHostToDevice,
                         c->stream) != cudaSuccess ||
@@ -385,6 +398,7 @@ extern "C" int q3a_check_device_error(q3a_ctx* c) {
         CUDA_TRY(cudaMemsetAsync(c->counters, 0, (size_t)max_groups * sizeof(int), c->stream));
         CUDA_TRY(cudaMemsetAsync(c->words, 0, (size_t)MAX_PIECES * PART_STRIDE * 8, c->stream));
         CUDA_TRY(cudaMemsetAsync(c->group_epoch, 0, (size_t)MAX_PIECES * sizeof(unsigned), c->stream));
+        CUDA_TRY(cudaMemsetAsync(c->claims, 0, (size_t)MAX_PIECES * sizeof(int), c->stream));
         CUDA_TRY(cudaStreamSynchronize(c->stream));
         return fail(Q3A_ERR_TIMEOUT, "a bounded device wait expired (device error %d)", h);
     }
@@ -392,6 +406,12 @@ extern "C" int q3a_check_device_error(q3a_ctx* c) {
 }
 
 extern "C" uint64_t q3a_launch_count(const q3a_ctx* c) { return c ? c->launches : 0; }
+
+extern "C" int q3a_set_deterministic(q3a_ctx* c, int on) {
+    if (!c) return fail(Q3A_ERR_INVALID, "null context");
+    c->deterministic = on ? 1 : 0;
+    return Q3A_OK;
+}
 
 extern "C" int q3a_set_wait_limit(q3a_ctx* c, double seconds) {
     if (!c) return fail(Q3A_ERR_INVALID, "null context");
@@ -421,6 +441,7 @@ static void base_params(q3a_ctx* c, DecodeParams& p, int layer) {
     p.counters = c->counters;
     p.words = c->words;
     p.group_epoch = c->group_epoch;
+    p.claim = c->claims;
     p.spread = 1;
     p.err = c->err;
     p.eps = c->cfg.norm_eps;
@@ -508,6 +529,27 @@ static void schedule_pieces(q3a_ctx* c, DecodeParams& p) {
     }
     p.n_pieces = np;
     p.n_ctas = np;
+    // CTA c takes pieces of the groups in turn (group 0's first piece, group
+    // 1's first, ..., group 0's second, ...): SMs with lower memory
+    // throughput sit in runs of consecutive ids, so interleaving gives every
+    // group a similar mix
+    int next[MAX_PIECES], first[MAX_PIECES];
+    int q = 0;
+    for (int g = 0; g < ng; g++) {
+        first[g] = q;
+        next[g] = 0;
+        while (q < np && p.pieces[q].g == g) q++;
+    }
+    int cta = 0;
+    while (cta < np) {
+        for (int g = 0; g < ng && cta < np; g++) {
+            const int pi = first[g] + next[g];
+            if (pi < np && p.pieces[pi].g == g) {
+                p.cta_piece[cta++] = (short)pi;
+                next[g]++;
+            }
+        }
+    }
 }
 
 // Fills the schedule: piece mode when every group can have its own CTA,
@@ -558,8 +600,28 @@ static int run_decode(q3a_ctx* c, DecodeParams& p, const CUtensorMap& tk, const 
     if (rc) return rc;
     // the context's bf16 paged cache is consumed on the tensor cores
     p.tc = (bf16 && p.cache_mode == CACHE_PAGED) ? 1 : 0;
+    // balanced schedule: piece-mode ranges of the paged cache claim units
+    p.dyn = (!c->deterministic && p.n_pieces > 0 && p.spread && p.cache_mode == CACHE_PAGED) ? 1 : 0;
+    // early cache streaming: the rows this launch reads from the context's
+    // cache cannot be written by the kernel it depends on (the previous
+    // launch on this stream was this context's decode of another layer, or
+    // a decode that appended nothing), and every kernel of the library
+    // releases its dependents only after its own dependency wait, so no
+    // earlier kernel is still running either
+    p.early = (p.cache_mode == CACHE_PAGED && c->last_decode_layer >= 0 &&
+               c->last_stream == c->stream &&
+               (c->last_decode_layer != p.layer || !c->last_decode_wrote))
+                  ? 1
+                  : 0;
     CUDA_TRY(launch_decode(p, tk, tv, bf16, c->stream));
     c->launches++;
+    if (p.cache_mode == CACHE_PAGED) {
+        c->last_stream = c->stream;
+        c->last_decode_layer = p.layer;
+        c->last_decode_wrote = p.fused;
+    } else {
+        c->last_decode_layer = -1;
+    }
     return Q3A_OK;
 }
 
@@ -814,6 +876,7 @@ extern "C" int q3a_lse_combine(q3a_ctx* c, float* xb, const float* o_parts, cons
     if (c->cfg.ptr_mode == Q3A_PTR_DEVICE) {
         CUDA_TRY(launch_lse_combine(xb, o_parts, qd, lse_parts, nh, n_parts, nh, c->stream));
         c->launches++;
+        c->last_decode_layer = -1;
         return Q3A_OK;
     }
     rc = grow_scratch(c, ((size_t)n_parts * (qd + nh) + qd) * 4);
@@ -824,6 +887,7 @@ extern "C" int q3a_lse_combine(q3a_ctx* c, float* xb, const float* o_parts, cons
     CUDA_TRY(cudaMemcpyAsync(d_l, lse_parts, (size_t)n_parts * nh * 4, cudaMemcpyHostToDevice, c->stream));
     CUDA_TRY(launch_lse_combine(d_x, d_o, qd, d_l, nh, n_parts, nh, c->stream));
     c->launches++;
+    c->last_decode_layer = -1;
     CUDA_TRY(cudaMemcpyAsync(xb, d_x, qd * 4, cudaMemcpyDeviceToHost, c->stream));
     CUDA_TRY(cudaStreamSynchronize(c->stream));
     return Q3A_OK;
@@ -1058,6 +1122,7 @@ extern "C" int q3a_gather_cols(q3a_ctx* c, size_t off, long long rows, size_t ro
     const int n_ctas = (int)std::min<long long>(c->num_sms, std::max<long long>(1, (work + 255) / 256));
     CUDA_TRY(launch_gather_cols(p, n_ctas, c->stream));
     c->launches++;
+    c->last_decode_layer = -1;
     return Q3A_OK;
 }
 
@@ -1100,6 +1165,7 @@ extern "C" int q3a_lse_combine_packed(q3a_ctx* c, float* xb, const float* parts,
     if (c->cfg.ptr_mode == Q3A_PTR_DEVICE) {
         CUDA_TRY(launch_lse_combine(xb, parts, pw, parts + qd, pw, n_parts, nh, c->stream));
         c->launches++;
+        c->last_decode_layer = -1;
         return Q3A_OK;
     }
     rc = grow_scratch(c, ((size_t)n_parts * pw + qd) * 4);
@@ -1109,6 +1175,7 @@ extern "C" int q3a_lse_combine_packed(q3a_ctx* c, float* xb, const float* parts,
     CUDA_TRY(cudaMemcpyAsync(d_p, parts, (size_t)n_parts * pw * 4, cudaMemcpyHostToDevice, c->stream));
     CUDA_TRY(launch_lse_combine(d_x, d_p, pw, d_p + qd, pw, n_parts, nh, c->stream));
     c->launches++;
+    c->last_decode_layer = -1;
     CUDA_TRY(cudaMemcpyAsync(xb, d_x, qd * 4, cudaMemcpyDeviceToHost, c->stream));
     CUDA_TRY(cudaStreamSynchronize(c->stream));
     return Q3A_OK;
@@ -1165,6 +1232,7 @@ static int append_common(q3a_ctx* c, int seq, int layer, int pos0, int n, const 
     }
     CUDA_TRY(launch_append(a, c->stream));
     c->launches++;
+    c->last_decode_layer = -1;
     if (c->cfg.ptr_mode == Q3A_PTR_HOST) CUDA_TRY(cudaStreamSynchronize(c->stream));
     return Q3A_OK;
 }
@@ -1177,6 +1245,40 @@ extern "C" int q3a_kv_append(q3a_ctx* c, int seq, int layer, int pos0, int n, co
 extern "C" int q3a_kv_load(q3a_ctx* c, int seq, int layer, int pos0, int n, const float* k,
                            const float* v) {
     return append_common(c, seq, layer, pos0, n, k, v, nullptr, 0);
+}
+
+extern "C" int q3a_kv_synth(q3a_ctx* c, int seq, int layer, int pos0, int n, uint64_t seed,
+                            uint64_t stream_k, uint64_t stream_v) {
+    g_err[0] = 0;
+    if (!c) return fail(Q3A_ERR_INVALID, "null context");
+    int rc = ensure_device(c);
+    if (rc) return rc;
+    AppendParams a;
+    rc = cache_io_params(c, a, seq, layer, pos0, n);
+    if (rc) return rc;
+    if (n == 0) return Q3A_OK;
+    // raw rows of all KV heads, as q3a_kv_append takes them; unit gains
+    static const float ones[HD] = {
+#define Q3A_ONE8 1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f
+        Q3A_ONE8, Q3A_ONE8, Q3A_ONE8, Q3A_ONE8, Q3A_ONE8, Q3A_ONE8, Q3A_ONE8, Q3A_ONE8,
+        Q3A_ONE8, Q3A_ONE8, Q3A_ONE8, Q3A_ONE8, Q3A_ONE8, Q3A_ONE8, Q3A_ONE8, Q3A_ONE8};
+#undef Q3A_ONE8
+    const size_t kd = (size_t)n * c->cfg.n_kv_heads * HD;
+    rc = grow_scratch(c, (2 * kd + HD) * 4);
+    if (rc) return rc;
+    float* s = reinterpret_cast<float*>(c->d_scratch);
+    CUDA_TRY(launch_randn(s, 0, kd, stream_key(seed, stream_k), 0, c->stream));
+    CUDA_TRY(launch_randn(s + kd, 0, kd, stream_key(seed, stream_v), 0, c->stream));
+    CUDA_TRY(cudaMemcpyAsync(s + 2 * kd, ones, sizeof(ones), cudaMemcpyHostToDevice, c->stream));
+    a.do_norm_rope = 1;
+    a.k = s;
+    a.v = s + kd;
+    a.k_norm_w = s + 2 * kd;
+    CUDA_TRY(launch_append(a, c->stream));
+    c->launches += 3;
+    c->last_decode_layer = -1;
+    if (c->cfg.ptr_mode == Q3A_PTR_HOST) CUDA_TRY(cudaStreamSynchronize(c->stream));
+    return Q3A_OK;
 }
 
 extern "C" int q3a_kv_read(q3a_ctx* c, int seq, int layer, int pos0, int n, float* k, float* v) {
@@ -1192,6 +1294,7 @@ extern "C" int q3a_kv_read(q3a_ctx* c, int seq, int layer, int pos0, int n, floa
     if (c->cfg.ptr_mode == Q3A_PTR_DEVICE) {
         CUDA_TRY(launch_kv_read(a, k, v, c->stream));
         c->launches++;
+        c->last_decode_layer = -1;
         return Q3A_OK;
     }
     rc = grow_scratch(c, 2 * kd * 4);
@@ -1199,6 +1302,7 @@ extern "C" int q3a_kv_read(q3a_ctx* c, int seq, int layer, int pos0, int n, floa
     float* s = reinterpret_cast<float*>(c->d_scratch);
     CUDA_TRY(launch_kv_read(a, s, s + kd, c->stream));
     c->launches++;
+    c->last_decode_layer = -1;
     CUDA_TRY(cudaMemcpyAsync(k, s, kd * 4, cudaMemcpyDeviceToHost, c->stream));
     CUDA_TRY(cudaMemcpyAsync(v, s + kd, kd * 4, cudaMemcpyDeviceToHost, c->stream));
     CUDA_TRY(cudaStreamSynchronize(c->stream));
@@ -1216,6 +1320,7 @@ extern "C" int q3a_randn(q3a_ctx* c, void* dst, int out_dtype, size_t n, uint64_
     CUDA_TRY(launch_randn(dst, out_dtype == Q3A_OUT_BF16, n, stream_key(seed, stream_id), offset,
                           c->stream));
     c->launches++;
+    c->last_decode_layer = -1;
     return Q3A_OK;
 }
 
@@ -1276,12 +1381,14 @@ extern "C" int q3a_prefill(q3a_ctx* c, void* out, int out_dtype, const float* q,
     pp.inv_freq = c->d_inv_freq;
     CUDA_TRY(launch_prep_rows(pp, c->stream));
     c->launches++;
+    c->last_decode_layer = -1;
     a.k = dk;
     a.v = dv;
     a.k_norm_w = dkw;
     a.do_norm_rope = 1;
     CUDA_TRY(launch_append(a, c->stream));
     c->launches++;
+    c->last_decode_layer = -1;
     // run the attention in device mode on the staged operands
     const int saved_mode = c->cfg.ptr_mode;
     c->cfg.ptr_mode = Q3A_PTR_DEVICE;
@@ -1430,6 +1537,7 @@ extern "C" int q3a_prefill_attn(q3a_ctx* c, void* out, int out_dtype, const void
     pp.vcache = reinterpret_cast<const __nv_bfloat16*>(c->vcache);
     CUDA_TRY(launch_prefill(pp, tq, c->stream));
     c->launches += pf_launches;
+    c->last_decode_layer = -1;
     if (c->cfg.ptr_mode == Q3A_PTR_HOST) {
         CUDA_TRY(cudaMemcpyAsync(out, dout, out_bytes, cudaMemcpyDeviceToHost, c->stream));
         CUDA_TRY(cudaStreamSynchronize(c->stream));

@@ -43,13 +43,17 @@
 
 namespace q3a {
 
+// fp32 caches (CUDA-core consumer): stages of 32 rows (16 KB of K + 16 KB of
+// V), six in the ring; the consumer warps form two groups of four that take
+// alternate stages, each warp 8 rows of a stage.
 template <typename KV, bool TC = false>
 struct DecCfg {
-    static constexpr int TILE = DEC_TILE;
+    static constexpr int TILE = 32;
     static constexpr int CWARPS = 8;
     static constexpr int NCONS = CWARPS * 32;
     static constexpr int NTHREADS = NCONS + 32;
-    static constexpr int STAGES = 3;  // fp32 (bf16 caches use the configuration below)
+    static constexpr int STAGES = 6;
+    static constexpr int STATIC_UNITS = 4;  // balanced schedule: units a range streams before claiming
     static constexpr int TILE_BYTES = TILE * HD * (int)sizeof(KV);
     static constexpr int BOX_BYTES = DEC_BOX * HD * (int)sizeof(KV);
     static constexpr int OFF_K = 0;
@@ -63,7 +67,8 @@ struct DecCfg {
     static constexpr int WST = GQA * HD + 8;                       // o[4][128], m[4], l[4]
     static constexpr int OFF_WST = OFF_P + CWARPS * 32 * 8;
     static constexpr int OFF_BAR = OFF_WST + CWARPS * WST * 4;
-    static constexpr int OFF_MISC = OFF_BAR + 2 * STAGES * 8;
+    static constexpr int OFF_META = OFF_BAR + 2 * STAGES * 8;    // int2 [STAGES]: first row, rows
+    static constexpr int OFF_MISC = OFF_META + STAGES * 8;
     static constexpr int SMEM = OFF_MISC + 64;
     static_assert(SMEM <= 232448, "decode shared memory exceeds the sm_100 limit");
 };
@@ -81,6 +86,7 @@ struct DecCfg<__nv_bfloat16, true> {
     static constexpr int NCONS = CWARPS * 32;
     static constexpr int NTHREADS = NCONS + 32;
     static constexpr int STAGES = 3;
+    static constexpr int STATIC_UNITS = 2;
     static constexpr int TILE_BYTES = TILE * HD * 2;        // one tensor of a stage
     static constexpr int OPB_BYTES = 16 * HD * 2;           // a [16][128] bf16 operand
     static constexpr int OFF_K = 0;
@@ -100,7 +106,8 @@ struct DecCfg<__nv_bfloat16, true> {
     static constexpr int OFF_BAR = OFF_WST + (W_LSUM + 16) * 4;
     // full[3] empty[3] sfull[2] pfull[2] ofull[2] newrow drain
     static constexpr int NBAR = 2 * STAGES + 8;
-    static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
+    static constexpr int OFF_META = OFF_BAR + NBAR * 8;       // int2 [STAGES]: first row, rows
+    static constexpr int OFF_MISC = OFF_META + STAGES * 8;
     static constexpr int SMEM = OFF_MISC + 64 + 1024;       // + slack for 1024-byte alignment
     static_assert(OFF_QT % 1024 == 0 && OFF_PT % 1024 == 0 && OFF_BAR % 8 == 0, "layout");
     static_assert(SMEM <= 232448, "decode shared memory exceeds the sm_100 limit");
@@ -148,14 +155,15 @@ __device__ __forceinline__ bool next_seg(const DecodeParams& P, int c, long long
     if (P.n_pieces > 0) {
         if (cur != 0) return false;
         cur = 1;
-        const Piece pc = P.pieces[c];
+        const int pi = P.cta_piece[c];
+        const Piece pc = P.pieces[pi];
         s.b = pc.g / P.nkv;
         s.kvh = pc.g % P.nkv;
         s.r0 = pc.r0;
         s.r1 = pc.r1;
         s.has_new = P.fused && pc.i == pc.k - 1;
-        s.slot = c;
-        s.slot0 = c - pc.i;
+        s.slot = pi;
+        s.slot0 = pi - pc.i;
         s.ncontrib = pc.k;
         s.grp = pc.g;
         return true;
@@ -206,6 +214,41 @@ __device__ __forceinline__ long long paged_row(const DecodeParams& P, int slot, 
     const int pt = P.page_tokens;
     const long long phys = (long long)slot * P.pages_per_seq + t / pt;
     return (((long long)P.layer * P.nkv + kvh) * P.n_pages + phys) * pt + (t % pt);
+}
+
+// Balanced schedule (P.dyn, piece mode on the paged cache).  The rows a
+// group attends are cut into units of U rows (one stage) aligned at a0;
+// units [0, n_claim) are streamed by the group's ranges -- range i first its
+// static units [i*S, (i+1)*S), which need nothing from the previous kernel
+// and may be streamed before the dependency wait, then units claimed one at
+// a time from the group's counter, starting at k*S -- so ranges on slower
+// SMs take fewer units.  On the tensor cores with a fused new token the
+// range that appends it also streams the tail [tail0, pos+1) last (the unit
+// holding pos, after the append).  Rows at or past r_lim are not attended
+// (the CUDA-core consumer takes the new token from shared memory).
+constexpr int DYN_END = -0x7fffffff;  // stage metadata of an end marker
+
+struct DynPlan {
+    int a0, n_claim, tb, r_lim, tail0;
+};
+
+template <bool TC>
+__device__ __forceinline__ DynPlan dyn_plan(const DecodeParams& P, int b, int U) {
+    DynPlan d;
+    d.tb = P.t_begin[b];
+    const int te = P.t_end[b];
+    d.a0 = d.tb & ~(U - 1);
+    if (TC && P.fused) {
+        const int pos = P.pos[b];  // == te: the new token's row
+        d.n_claim = (pos - d.a0) / U;
+        d.tail0 = d.a0 + d.n_claim * U;
+        d.r_lim = pos + 1;
+    } else {
+        d.n_claim = te > d.tb ? (te - d.a0 + U - 1) / U : 0;
+        d.tail0 = -1;
+        d.r_lim = te;
+    }
+    return d;
 }
 
 // acq_rel atomic add at GPU scope: releases this CTA's partial (ordered
@@ -507,7 +550,8 @@ __device__ __forceinline__ void lse_fold(float& M, float& W, float& A, float m2,
 // j = sub, sub + tpv, ... < n at base + j*stride + off_o / off_l, waits
 // (bounded) until each carries `tag`, and folds them; then the tpv lanes of
 // its value (consecutive lanes of one warp) combine by shuffles.  Returns
-// false when a word did not arrive within `limit` SM clocks.
+// false, in every lane of the warp, when a word did not arrive within
+// `limit` SM clocks.  Called by all 32 lanes of the warp.
 template <bool SYS>
 __device__ __forceinline__ bool spread_gather(const unsigned long long* base, size_t stride, int n,
                                               int sub, int tpv, bool active, size_t off_o,
@@ -561,7 +605,10 @@ __device__ __forceinline__ bool spread_gather(const unsigned long long* base, si
         const float a2 = __shfl_xor_sync(FULL, A, o);
         lse_fold(M, W, A, m2, w2, a2);
     }
-    return ok;
+    // a value's sources are spread over tpv lanes of this warp: the value is
+    // valid only if every one of them arrived, so one lane's timeout fails
+    // the warp (the writer lane must not store a partial merge)
+    return __all_sync(FULL, ok);
 }
 
 // Bounded wait of one warp until word base + j*stride carries `tag` for
@@ -610,10 +657,11 @@ __global__ void __launch_bounds__(DecCfg<KV, TC>::NTHREADS, 1)
     uint64_t* newrow = ofull + 2;         // the new token's row is in the cache
     uint64_t* drain = newrow + 1;         // every issued MMA complete
     volatile int* misc = reinterpret_cast<volatile int*>(smem + C::OFF_MISC);
+    // per stage: first cache row and rows loaded (balanced schedule)
+    volatile int* meta = reinterpret_cast<volatile int*>(smem + C::OFF_META);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int c = blockIdx.x;
-    if (tid == 0) griddep_launch_dependents();
 
     if (warp == C::CWARPS) {
         // ================================================= producer
@@ -623,7 +671,9 @@ __global__ void __launch_bounds__(DecCfg<KV, TC>::NTHREADS, 1)
 #pragma unroll
             for (int s = 0; s < C::STAGES; s++) {
                 mbar_init(&full[s], 1);
-                mbar_init(&empty[s], TC ? 1 : C::CWARPS);
+                // a stage is freed by the MMA commit (tensor cores) or by the
+                // four warps of the group that consumed it (CUDA cores)
+                mbar_init(&empty[s], TC ? 1 : C::CWARPS / 2);
             }
             if constexpr (TC) {
                 for (int t = 0; t < 2; t++) {
@@ -633,6 +683,7 @@ __global__ void __launch_bounds__(DecCfg<KV, TC>::NTHREADS, 1)
                 }
                 mbar_init(newrow, 2);
                 mbar_init(drain, 1);
+                misc[6] = -1;  // no end marker seen yet (balanced schedule)
             }
             fence_mbar_init();
             tma_prefetch_desc(&tmK);
@@ -641,14 +692,111 @@ __global__ void __launch_bounds__(DecCfg<KV, TC>::NTHREADS, 1)
         __syncwarp();
         named_bar_arrive(2, C::NTHREADS);
         if (lane == 0) {
-            griddep_wait();  // the previous kernel's writes (cache rows) are visible
+            // The producer reads cache rows only.  Unless the host found that
+            // the kernel this launch depends on cannot write them (`early`),
+            // it first waits for that kernel's writes to be visible; with
+            // `early` the stream starts at once, overlapping the previous
+            // kernel's tail.
+            if (!P.early) griddep_wait();
             const uint64_t pol = l2_policy_evict_first();
             int it = 0;
             bool dead = false;
             long long cur = 0;
             SegInfo s;
             int nnew = 0;  // ranges with a new token so far (phase of `newrow`)
-            if constexpr (TC) {
+            if (P.dyn) {
+                // ---- balanced schedule: one range, units of one stage
+                next_seg(P, c, cur, s);
+                const int slot = P.slot[s.b];
+                const DynPlan d = dyn_plan<TC>(P, s.b, C::TILE);
+                const int i = s.slot - s.slot0, k = s.ncontrib;
+                int u = i * C::STATIC_UNITS;
+                const int u_st_end = min(u + C::STATIC_UNITS, d.n_claim);
+                bool waited = !P.early, held = false;
+                constexpr int ESZ = (int)sizeof(KV);
+                // the next ring slot, once the consumers have freed it
+                auto acquire = [&]() -> bool {
+                    const int stage = it % C::STAGES;
+                    const uint32_t ph = (uint32_t)(it / C::STAGES) & 1u;
+                    return it < C::STAGES || mbar_wait(&empty[stage], ph ^ 1u);
+                };
+                // fills the acquired slot with rows [row0, row0 + n) of the
+                // range's (sequence, kv head); n = 0 is an end marker
+                auto fill = [&](int row0, int n, bool with_new) -> bool {
+                    const int stage = it % C::STAGES;
+                    if (with_new) {  // the consumers have appended the new row
+                        if (!mbar_wait(newrow, 0u)) return false;
+                        fence_proxy_async_global();
+                    }
+                    meta[2 * stage] = row0;
+                    meta[2 * stage + 1] = n;
+                    it++;
+                    if (n == 0) {
+                        mbar_arrive(&full[stage]);
+                        return true;
+                    }
+                    mbar_arrive_expect_tx(&full[stage], (uint32_t)(2 * n * HD * ESZ));
+                    uint8_t* kst = smem + C::OFF_K + stage * C::TILE * HD * ESZ;
+                    uint8_t* vst = smem + C::OFF_V + stage * C::TILE * HD * ESZ;
+                    for (int a = row0; a < row0 + n;) {
+                        // a and the page ends are multiples of 16 rows
+                        const int e = min(row0 + n, (a / P.page_tokens + 1) * P.page_tokens);
+                        const long long row = paged_row(P, slot, s.kvh, a);
+                        const uint32_t nb = (uint32_t)((e - a) * HD * ESZ);
+                        const int so = (a - row0) * HD * ESZ;
+                        bulk_load(kst + so, reinterpret_cast<const KV*>(P.kcache) + row * HD, nb,
+                                  &full[stage], pol);
+                        bulk_load(vst + so, reinterpret_cast<const KV*>(P.vcache) + row * HD, nb,
+                                  &full[stage], pol);
+                        a = e;
+                    }
+                    return true;
+                };
+                // rows a unit loads: whole 16-row MMA steps on the tensor cores
+                auto unit_rows = [&](int row0) {
+                    const int n = min(C::TILE, d.r_lim - row0);
+                    return TC ? ((n + DEC_BOX - 1) & ~(DEC_BOX - 1)) : n;
+                };
+                while (!dead) {
+                    int row0;
+                    if (u < u_st_end) {
+                        row0 = d.a0 + (u++) * C::TILE;
+                        if (!acquire()) dead = true;
+                    } else {
+                        if (!waited) {  // the counters are reset by the kernel before
+                            griddep_wait();
+                            waited = true;
+                        }
+                        // claim, then wait for a free slot while the claim returns
+                        const int cl = atomicAdd(P.claim + s.grp, 1);
+                        if (!acquire()) {
+                            dead = true;
+                            break;
+                        }
+                        const int cu = k * C::STATIC_UNITS + cl;
+                        if (cu >= d.n_claim) {
+                            held = true;  // keep the slot for what follows
+                            break;
+                        }
+                        row0 = d.a0 + cu * C::TILE;
+                    }
+                    if (dead || !fill(row0, unit_rows(row0), false)) dead = true;
+                }
+                if (!dead && TC && s.has_new) {  // the tail with the new token
+                    if (!held && !acquire()) dead = true;
+                    held = false;
+                    if (!dead && !fill(d.tail0, (d.r_lim - d.tail0 + DEC_BOX - 1) & ~(DEC_BOX - 1), true))
+                        dead = true;
+                }
+                // end markers: one per consumer sequence (on the CUDA cores
+                // two warp groups take alternate stages)
+                for (int e = 0; e < (TC ? 1 : 2) && !dead; e++) {
+                    if (!held && !acquire()) dead = true;
+                    held = false;
+                    if (!dead && !fill(DYN_END, 0, false)) dead = true;
+                }
+                if (dead) atomicExch(P.err, DEV_ERR_TIMEOUT);
+            } else if constexpr (TC) {
             while (!dead && next_seg(P, c, cur, s)) {
                 // 128-row stages; the cache's 8-row blocks are already in
                 // the operand layout, so rows [t0, hi) of a page are one
@@ -786,6 +934,10 @@ __global__ void __launch_bounds__(DecCfg<KV, TC>::NTHREADS, 1)
         tc_fence_before();
     }
     griddep_wait();  // inputs written by the previous kernel are visible
+    // Dependents may launch only once this kernel has passed its own wait:
+    // then every kernel before the previous one has completed, which is
+    // what lets a dependent decode stream cache rows before its wait.
+    if (tid == 0) griddep_launch_dependents();
     while (next_seg(P, c, cur, s)) {
         const int b = s.b, kvh = s.kvh;
         const int hq0 = (P.kv0 + kvh) * GQA;
@@ -884,9 +1036,14 @@ __global__ void __launch_bounds__(DecCfg<KV, TC>::NTHREADS, 1)
             const int ntiles = r_end > lo_all ? (r_end - lo_all + C::TILE - 1) / C::TILE : 0;
             const int it0 = it;
             const bool direct = SPREAD && s.ncontrib > 1;
+            // balanced schedule: stages carry their rows in `meta` and end
+            // with a marker; otherwise ntiles stages from lo_all
+            DynPlan dp;
+            if (P.dyn) dp = dyn_plan<true>(P, b, C::TILE);
+            volatile int* end_stage = misc + 6;  // stage index of the end marker
             if (warp == GQA) {
                 // ================================== MMA issuer (one thread)
-                if (lane == 0 && ntiles > 0) {
+                if (lane == 0 && (P.dyn || ntiles > 0)) {
                     bool dead = false;
                     auto issue_s = [&](int g) {
                         // S^T (128 rows x 16) = K (128 x 128, K-major) . Q^T
@@ -903,15 +1060,38 @@ __global__ void __launch_bounds__(DecCfg<KV, TC>::NTHREADS, 1)
                         }
                         tc_commit(&sfull[g & 1]);
                     };
+                    // stage g (the j-th of the range): is it real, and how many
+                    // rows does it hold (balanced: from its metadata, after
+                    // its full barrier; static: from the range)
+                    auto rows_of = [&](int j, int g) -> int {
+                        if (P.dyn) {
+                            const int st = g % C::STAGES;
+                            return meta[2 * st] == DYN_END ? 0 : meta[2 * st + 1];
+                        }
+                        const int t0 = lo_all + j * C::TILE;
+                        return min(t0 + C::TILE, hi_all) - t0;
+                    };
+                    // end marker: the softmax threads learn it from end_stage
+                    // behind the stage's S barrier
+                    auto signal_end = [&](int g) {
+                        *end_stage = g;
+                        mbar_arrive(&sfull[g & 1]);
+                    };
+                    int nrows = 0;
                     if (mbar_wait(&full[it0 % C::STAGES], (uint32_t)(it0 / C::STAGES) & 1u)) {
                         tc_fence_after();
-                        issue_s(it0);
+                        nrows = rows_of(0, it0);
+                        if (nrows > 0)
+                            issue_s(it0);
+                        else
+                            signal_end(it0);
                     } else {
                         dead = true;
                     }
-                    for (int j = 0; j < ntiles && !dead; j++) {
+                    for (int j = 0; nrows > 0 && !dead; j++) {
                         const int g = it0 + j;
-                        if (j + 1 < ntiles) {
+                        int nrows_next = 0;
+                        if (P.dyn || j + 1 < ntiles) {
                             // S of the next stage goes first; its buffer was
                             // freed by the softmax of stage g-1
                             const int gn = g + 1;
@@ -920,7 +1100,11 @@ __global__ void __launch_bounds__(DecCfg<KV, TC>::NTHREADS, 1)
                                 break;
                             }
                             tc_fence_after();
-                            issue_s(gn);
+                            nrows_next = rows_of(j + 1, gn);
+                            if (nrows_next > 0)
+                                issue_s(gn);
+                            else if (P.dyn)
+                                signal_end(gn);
                         }
                         if (!mbar_wait(&pfull[g & 1], (uint32_t)(g >> 1) & 1u)) {
                             dead = true;
@@ -929,8 +1113,7 @@ __global__ void __launch_bounds__(DecCfg<KV, TC>::NTHREADS, 1)
                         tc_fence_after();
                         // O^T tile (128 dims x 16) = V^T (MN-major) . P^T over
                         // the loaded 16-row steps only
-                        const int t0 = lo_all + j * C::TILE;
-                        const int nk = (min(t0 + C::TILE, hi_all) - t0) / DEC_BOX;
+                        const int nk = nrows / DEC_BOX;
                         const uint32_t vb = sb + C::OFF_V + (g % C::STAGES) * C::TILE_BYTES;
                         const uint32_t pb = sb + C::OFF_PT + (uint32_t)(g & 1) * C::OPB_BYTES;
                         const uint32_t dcol = tm + DTC_O_COL + (uint32_t)(g & 1) * 16u;
@@ -942,6 +1125,7 @@ __global__ void __launch_bounds__(DecCfg<KV, TC>::NTHREADS, 1)
                                       IDESC_DPV, kk > 0 ? 1u : 0u);
                         tc_commit(&ofull[g & 1]);
                         tc_commit(&empty[g % C::STAGES]);
+                        nrows = nrows_next;
                     }
                     if (dead) atomicExch(P.err, DEV_ERR_TIMEOUT);
                 }
@@ -978,18 +1162,34 @@ __global__ void __launch_bounds__(DecCfg<KV, TC>::NTHREADS, 1)
                     for (int q = 0; q < GQA; q++)
                         Oh[q] = fmaf(Oh[q], al_prev[q], __uint_as_float(r[q]) + __uint_as_float(r[q + GQA]));
                 };
-                for (int j = 0; j < ntiles; j++) {
+                int nt = 0;  // real stages of the range
+                for (int j = 0; P.dyn || j < ntiles; j++) {
                     const int g = it0 + j, bf = g & 1;
                     bool got = ok && mbar_wait(&sfull[bf], (uint32_t)(g >> 1) & 1u);
                     got = __all_sync(FULL, got);
+                    int row0 = lo_all + j * C::TILE, vlo = s.r0, vhi = r_end, nld = C::TILE;
+                    if (P.dyn && got) {
+                        if (*end_stage == g) break;  // end marker
+                        // the stage's metadata: its full barrier (completed
+                        // before its S) orders the producer's stores before
+                        // these loads
+                        const int st = g % C::STAGES;
+                        got = mbar_wait(&full[st], (uint32_t)(g / C::STAGES) & 1u);
+                        row0 = meta[2 * st];
+                        nld = meta[2 * st + 1];
+                        vlo = dp.tb;
+                        vhi = dp.r_lim;
+                    }
+                    got = __all_sync(FULL, got);
+                    nt = j + 1;
                     uint32_t r[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
                     if (got) {
                         tc_fence_after();
                         Q3A_TC_LD8(tm + lane_base + DTC_S_COL + (uint32_t)bf * 16u, r);
                         tc_wait_ld();
                     }
-                    const int key = lo_all + j * C::TILE + tid;
-                    const bool valid = got && key >= s.r0 && key < r_end;
+                    const int key = row0 + tid;
+                    const bool valid = got && tid < nld && key >= vlo && key < vhi;
                     float sc[GQA], mx[GQA];
 #pragma unroll
                     for (int q = 0; q < GQA; q++) {
@@ -1044,7 +1244,7 @@ __global__ void __launch_bounds__(DecCfg<KV, TC>::NTHREADS, 1)
                     if (lane == 0) lred[warp * 4 + q] = v;
                 }
                 named_bar_sync(3, 128);
-                if (ok && ntiles > 0) fold(it0 + ntiles - 1);
+                if (ok && nt > 0) fold(it0 + nt - 1);
                 // a spread-merged range stores its words from here (thread
                 // tid holds dimension tid of the 4 heads); otherwise the
                 // outputs go through shared memory to the 256-thread layout
@@ -1053,7 +1253,9 @@ __global__ void __launch_bounds__(DecCfg<KV, TC>::NTHREADS, 1)
 #pragma unroll
                 for (int q = 0; q < GQA; q++) {
                     const float L = lred[q] + lred[4 + q] + lred[8 + q] + lred[12 + q];
-                    const float oq = Oh[q] / L, lq = mh[q] + log2f(L);
+                    // a range that attended no row contributes o = 0, lse = -inf
+                    const float oq = L > 0.0f ? Oh[q] / L : 0.0f;
+                    const float lq = L > 0.0f ? mh[q] + log2f(L) : -INFINITY;
                     if (direct) {
                         st_word_gpu(mine + q * HD + tid, oq, tag);
                         if (tid == q) st_word_gpu(mine + GQA * HD + q, lq, tag);
@@ -1084,23 +1286,47 @@ __global__ void __launch_bounds__(DecCfg<KV, TC>::NTHREADS, 1)
 #pragma unroll
             for (int hh = 0; hh < GQA; hh++) O[hh][0] = O[hh][1] = make_float2(0.0f, 0.0f);
 
+            // two groups of four warps take alternate stages; warp wl of a
+            // group owns rows 8 wl .. 8 wl + 7 of each of its stages
+            const int wg = warp >> 2, wl = warp & 3;
             bool dead = false;
-            for (int t0 = s.r0 & ~(DEC_BOX - 1); t0 < s.r1; t0 += C::TILE) {
-                const int stage = it % C::STAGES;
-                const uint32_t ph = (uint32_t)(it / C::STAGES) & 1u;
-                if (!mbar_wait(&full[stage], ph)) {
-                    atomicExch(P.err, DEV_ERR_TIMEOUT);
-                    dead = true;
-                    break;
+            if (P.dyn) {
+                const DynPlan dp = dyn_plan<false>(P, b, C::TILE);
+                for (int j = wg;; j += 2) {
+                    const int g = it + j, stage = g % C::STAGES;
+                    if (!mbar_wait(&full[stage], (uint32_t)(g / C::STAGES) & 1u)) {
+                        dead = true;
+                        break;
+                    }
+                    const int row0 = meta[2 * stage];
+                    if (row0 == DYN_END) break;
+                    const int lo = max(dp.tb - row0, 0), hi = min(dp.r_lim - row0, C::TILE);
+                    process_rows<KV>(sK + stage * C::TILE * HD, sV + stage * C::TILE * HD, lo, hi, wl,
+                                     lane, qr, m, lpart, O, pw);
+                    if (lane == 0) mbar_arrive(&empty[stage]);
                 }
-                const int lo = max(s.r0 - t0, 0);
-                const int hi = min(s.r1 - t0, C::TILE);
-                process_rows<KV>(sK + stage * C::TILE * HD, sV + stage * C::TILE * HD, lo, hi, warp,
-                                 lane, qr, m, lpart, O, pw);
-                if (lane == 0) mbar_arrive(&empty[stage]);
-                it++;
+            } else {
+                const int lo_all = s.r0 & ~(DEC_BOX - 1);
+                const int ntiles = s.r1 > lo_all ? (s.r1 - lo_all + C::TILE - 1) / C::TILE : 0;
+                for (int j = wg; j < ntiles; j += 2) {
+                    const int g = it + j, stage = g % C::STAGES;
+                    if (!mbar_wait(&full[stage], (uint32_t)(g / C::STAGES) & 1u)) {
+                        dead = true;
+                        break;
+                    }
+                    const int t0 = lo_all + j * C::TILE;
+                    const int lo = max(s.r0 - t0, 0), hi = min(s.r1 - t0, C::TILE);
+                    process_rows<KV>(sK + stage * C::TILE * HD, sV + stage * C::TILE * HD, lo, hi, wl,
+                                     lane, qr, m, lpart, O, pw);
+                    if (lane == 0) mbar_arrive(&empty[stage]);
+                }
+                it += ntiles;
             }
-            if (dead) return;
+            // a failed wait voids the result (the error word tells the host);
+            // every warp still takes the barriers below
+            if (dead) atomicExch(P.err, DEV_ERR_TIMEOUT);
+            // the new token from shared memory: warp 0 (rows 8 warp .. of a
+            // one-row tile)
             if (s.has_new) process_rows<KV>(sNewK, sNewV, 0, 1, warp, lane, qr, m, lpart, O, pw);
 
             // ---- merge the 8 warp states of this range
@@ -1134,10 +1360,12 @@ __global__ void __launch_bounds__(DecCfg<KV, TC>::NTHREADS, 1)
                 o0 = fmaf(sW[w * C::WST + h * HD + d], sc, o0);
                 o1 = fmaf(sW[w * C::WST + h * HD + d + 1], sc, o1);
             }
-            const float inv = 1.0f / L;
+            // a range that attended no row (possible in the balanced schedule)
+            // contributes o = 0, lse = -inf
+            const float inv = L > 0.0f ? 1.0f / L : 0.0f;
             o0 *= inv;
             o1 *= inv;
-            lse = M + log2f(L);
+            lse = L > 0.0f ? M + log2f(L) : -INFINITY;
         }
 
         bool write_out = true;
@@ -1217,8 +1445,10 @@ __global__ void __launch_bounds__(DecCfg<KV, TC>::NTHREADS, 1)
             if (P.fused && P.q_out && P.peer_world == 0 && tid < nv)
                 P.q_out[(size_t)b * P.hq_total * HD + (size_t)hq0 * HD + v0 + tid] = sQ[v0 + tid];
             if (i == 0 && tid == 0) {
-                // every range of the group has read the call numbers by now
+                // every range of the group has read the call numbers by now,
+                // and has stopped claiming units
                 *reinterpret_cast<volatile unsigned*>(P.group_epoch + s.grp) = gep;
+                if (P.dyn) P.claim[s.grp] = 0;
                 if (P.peer_world > 0) *reinterpret_cast<volatile unsigned*>(P.peer_epoch + kvh) = pep;
             }
             write_out = false;
@@ -1338,6 +1568,9 @@ __global__ void __launch_bounds__(DecCfg<KV, TC>::NTHREADS, 1)
             if (tid == 0) *reinterpret_cast<volatile unsigned*>(P.peer_epoch + kvh) = ep;
             write_out = false;
         }
+        // a one-range group of the balanced schedule resets its unit
+        // counter (its producer has stopped claiming: the end marker came last)
+        if (P.dyn && s.ncontrib == 1 && tid == 0) P.claim[s.grp] = 0;
         if (write_out) {
             float* xo = P.xb + (size_t)b * P.hq_total * HD + (size_t)(hq0 + h) * HD + d;
             *reinterpret_cast<float2*>(xo) = make_float2(o0, o1);

@@ -85,11 +85,18 @@ struct DecodeParams {
     int n_pieces;            // > 0: piece mode with n_ctas == n_pieces
     int spread;              // 1: piece-mode groups merge by the spread merge
     int tc;                  // 1: tensor-core consumer (bf16 paged cache; 16-row swizzled maps)
+    int early;               // 1: the producer streams cache rows before the dependency wait
+                             //    (the host checked that the kernel depended on cannot write them)
+    int dyn;                 // 1 (piece mode, paged cache, spread merge): each range streams a
+                             //    few static units of its group, then claims the group's other
+                             //    units from claim[group] (balances ranges on slower SMs)
+    int* claim;              // [MAX_PIECES] per-group unit counters, zero between launches
     unsigned long long* words;   // spread merge: MAX_PIECES slots of PART_STRIDE tagged words
     unsigned* group_epoch;   // spread merge: call number per group [MAX_PIECES]
     const float* inv_freq;   // [64] RoPE inverse frequencies (host powf, reference formula)
     long long wait_limit;    // SM clocks a wait on another CTA or rank may take
     Piece pieces[MAX_PIECES];
+    short cta_piece[MAX_PIECES];  // piece mode: piece processed by CTA c (groups interleaved)
     int t_begin[MAX_B];      // first cache position attended per sequence
     int t_end[MAX_B];        // one past the last cache position read from the cache
     int pos[MAX_B];          // new-token position (fused)

@@ -209,6 +209,7 @@ extern "C" int q3a_attn_decode_noalloc(float* xb, const float* q, const float* k
     }
     p.n_pieces = np;
     p.n_ctas = np;
+    for (int c = 0; c < np; c++) p.cta_piece[c] = (short)c;
 
     // counters and the error word must start at zero
     if (cudaMemsetAsync(ds->base + NOALLOC_CNT_OFF, 0, NOALLOC_BYTES - NOALLOC_CNT_OFF, st) !=

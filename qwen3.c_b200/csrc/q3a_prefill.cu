@@ -247,8 +247,10 @@ __global__ void __launch_bounds__(pf::NTHREADS, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    if (tid == 0) griddep_launch_dependents();
     griddep_wait();  // the previous kernel's writes (cache, q rows) are visible
+    // dependents are released only after this kernel's own wait (so every
+    // kernel before the previous one has completed)
+    if (tid == 0) griddep_launch_dependents();
 
     if (warp == 0) {
         // ============================================ TMA producer

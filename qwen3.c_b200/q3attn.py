@@ -31,7 +31,8 @@ EXPORTS = [
     "q3a_peer_buffer", "q3a_peer_open_ptrs",
     "q3a_peer_register", "q3a_peer_register_open", "q3a_gather_cols",
     "q3a_peer_register_flags", "q3a_peer_register_open_ptrs", "q3a_set_wait_limit",
-    "q3a_randn",
+    "q3a_set_deterministic",
+    "q3a_randn", "q3a_kv_synth",
     "q3a_launch_count", "q3a_attn_decode_noalloc", "q3a_noalloc_check_error",
 ]
 
@@ -96,7 +97,9 @@ def load():
         L.q3a_peer_register_open_ptrs.argtypes = [_P, _I, _I, ctypes.POINTER(_P),
                                                   ctypes.POINTER(_P)]
         L.q3a_set_wait_limit.argtypes = [_P, ctypes.c_double]
+        L.q3a_set_deterministic.argtypes = [_P, _I]
         L.q3a_randn.argtypes = [_P, _P, _I, _SZ, _U64, _U64, _U64]
+        L.q3a_kv_synth.argtypes = [_P, _I, _I, _I, _I, _U64, _U64, _U64]
         L.q3a_attn_decode_noalloc.argtypes = [_P, _P, _P, _P, _SZ, _I, _I, _I, _I, _I, _I, _P]
         L.q3a_noalloc_check_error.argtypes = [_P]
         L.q3a_launch_count.argtypes = [_P]
@@ -276,11 +279,17 @@ class Context:
         f = (_P * world)(*flags)
         check(self.lib.q3a_peer_register_open_ptrs(self.h, rank, world, b, f))
 
+    def set_deterministic(self, on: bool):
+        check(self.lib.q3a_set_deterministic(self.h, 1 if on else 0))
+
     def set_wait_limit(self, seconds: float):
         check(self.lib.q3a_set_wait_limit(self.h, seconds))
 
     def gather_cols(self, off, rows, row_bytes, col0, col_bytes):
         check(self.lib.q3a_gather_cols(self.h, off, rows, row_bytes, col0, col_bytes))
+
+    def kv_synth(self, seq, layer, pos0, n, seed, stream_k, stream_v):
+        check(self.lib.q3a_kv_synth(self.h, seq, layer, pos0, n, seed, stream_k, stream_v))
 
     def randn(self, dst, out_dtype, n, seed, stream_id, offset=0):
         check(self.lib.q3a_randn(self.h, ptr(dst), out_dtype, n, seed, stream_id, offset))

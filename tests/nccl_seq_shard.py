@@ -36,6 +36,7 @@ def main():
     with q3attn.Context(n_layers=1, max_seq=t1 - t0, kv_dtype=q3attn.KV_BF16,
                         ptr_mode=q3attn.PTR_DEVICE, device=local) as ctx:
         ctx.set_stream(st.cuda_stream)
+        ctx.set_deterministic(True)  # the repeated calls are compared bit for bit
         ctx.kv_load(0, 0, 0, t1 - t0, torch.from_numpy(kc[t0 * KV_DIM:t1 * KV_DIM]).to(dev),
                     torch.from_numpy(vc[t0 * KV_DIM:t1 * KV_DIM]).to(dev))
         dec = shard.SeqShardDecode(torch, ctx, world=world, rank=rank, device=dev,
