@@ -213,6 +213,13 @@ cudaError_t q3a::ensure_smem_attr(const void* fn, int bytes) {
         if (d.first == fn && d.second == dev) return cudaSuccess;
     e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
     if (e != cudaSuccess) return e;
+    // Every kernel of the library asks for the largest shared-memory
+    // carveout: an SM runs CTAs of different kernels side by side only in
+    // one L1/shared split, so a small kernel that preferred more L1 would
+    // keep a decode or prefill CTA off its SM until it exited.
+    e = cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout,
+                             (int)cudaSharedmemCarveoutMaxShared);
+    if (e != cudaSuccess) return e;
     done.emplace_back(fn, dev);
     return cudaSuccess;
 }

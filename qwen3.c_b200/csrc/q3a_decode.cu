@@ -760,6 +760,13 @@ __global__ void __launch_bounds__(DecCfg<KV, TC>::NTHREADS, 1)
                 while (!dead) {
                     int row0;
                     if (u < u_st_end) {
+                        // one unit streams before the dependency wait: it fills
+                        // the pipeline while the previous kernel finishes,
+                        // without flooding the memory queues its merge waits on
+                        if (!waited && u > i * C::STATIC_UNITS) {
+                            griddep_wait();
+                            waited = true;
+                        }
                         row0 = d.a0 + (u++) * C::TILE;
                         if (!acquire()) dead = true;
                     } else {
