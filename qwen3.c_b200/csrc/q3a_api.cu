@@ -149,6 +149,13 @@ static int ensure_device(const q3a_ctx* c) {
     return Q3A_OK;
 }
 
+// Host-pointer staging of n tokens: inputs [q | k | v | q gains | k gains]
+// then outputs [xb | q out | k out], every part a multiple of 4 floats.
+static size_t host_stage_floats(int n_heads, int n_kv, int n) {
+    const size_t qd = (size_t)n * n_heads * HD, kd = (size_t)n * n_kv * HD;
+    return (qd + 2 * kd + 2 * HD) + (2 * qd + kd);
+}
+
 static int grow_stage(q3a_ctx* c, size_t floats) {
     if (floats <= c->stage_floats) return Q3A_OK;
     if (c->h_stage) cudaFreeHost(c->h_stage);
@@ -359,7 +366,7 @@ extern "C" int q3a_create(q3a_ctx** out, const q3a_cfg* cfg_in) {
         destroy_ctx(c);
         return rc;
     }
-    const size_t stage = 2 * (size_t)cfg.n_heads * HD + 2 * (size_t)cfg.n_kv_heads * HD + 2 * HD;
+    const size_t stage = host_stage_floats(cfg.n_heads, cfg.n_kv_heads, 1);
     rc = grow_stage(c, stage);
     if (rc != Q3A_OK) {
         destroy_ctx(c);
@@ -632,6 +639,55 @@ static int run_decode(q3a_ctx* c, DecodeParams& p, const CUtensorMap& tk, const 
     return Q3A_OK;
 }
 
+// Host-pointer form of the fused block for n tokens: the inputs are staged in
+// pinned memory and copied to the device in one transfer; the decode kernel
+// writes xb and the rotated q and k straight into pinned memory over the bus
+// (no device-to-host copy: measured faster than staging them back); one
+// stream synchronisation, then the results go to the caller's buffers.  A context holding some KV heads only writes their
+// columns of xb: the caller's other columns are staged first and kept.
+static int host_block(q3a_ctx* c, DecodeParams& p, float* xb, float* q, float* k, const float* v,
+                      const float* qw, const float* kw, int n) {
+    const size_t qd = (size_t)n * c->cfg.n_heads * HD, kd = (size_t)n * c->cfg.n_kv_heads * HD;
+    int rc = grow_stage(c, host_stage_floats(c->cfg.n_heads, c->cfg.n_kv_heads, n));
+    if (rc) return rc;
+    const size_t n_in = qd + 2 * kd + 2 * HD;
+    float* hs = c->h_stage;
+    float* ds = c->d_stage;
+    float *h_q = hs, *h_k = h_q + qd, *h_v = h_k + kd, *h_qw = h_v + kd, *h_kw = h_qw + HD;
+    float *h_xb = hs + n_in, *h_qo = h_xb + qd, *h_ko = h_qo + qd;
+    float *d_q = ds, *d_k = d_q + qd, *d_v = d_k + kd, *d_qw = d_v + kd, *d_kw = d_qw + HD;
+    memcpy(h_q, q, qd * 4);
+    memcpy(h_k, k, kd * 4);
+    memcpy(h_v, v, kd * 4);
+    memcpy(h_qw, qw, HD * 4);
+    memcpy(h_kw, kw, HD * 4);
+    const bool partial_cols = c->nkv != c->cfg.n_kv_heads;
+    if (partial_cols) memcpy(h_xb, xb, qd * 4);
+    CUDA_TRY(cudaMemcpyAsync(d_q, h_q, n_in * 4, cudaMemcpyHostToDevice, c->stream));
+    p.q = d_q; p.k_new = d_k; p.v_new = d_v; p.q_norm_w = d_qw; p.k_norm_w = d_kw;
+    p.q_out = h_qo; p.k_out = h_ko; p.xb = h_xb;
+    rc = run_decode(c, p, c->tmK, c->tmV, c->bf16);
+    if (rc) return rc;
+    CUDA_TRY(cudaStreamSynchronize(c->stream));
+    memcpy(xb, h_xb, qd * 4);
+    // the rotated q and k: whole rows from a context holding every KV head,
+    // else the held heads' slices (the caller's rotation of the others is
+    // not this context's to give)
+    if (!partial_cols) {
+        memcpy(q, h_qo, qd * 4);
+        memcpy(k, h_ko, kd * 4);
+    } else {
+        const size_t qh = (size_t)c->nkv * GQA * HD, kh = (size_t)c->nkv * HD;
+        for (int b = 0; b < n; b++) {
+            const size_t qo = (size_t)b * c->cfg.n_heads * HD + (size_t)c->kv0 * GQA * HD;
+            const size_t ko = (size_t)b * c->cfg.n_kv_heads * HD + (size_t)c->kv0 * HD;
+            memcpy(q + qo, h_qo + qo, qh * 4);
+            memcpy(k + ko, h_ko + ko, kh * 4);
+        }
+    }
+    return Q3A_OK;
+}
+
 extern "C" int q3a_attn_layer(q3a_ctx* c, float* xb, float* q, float* k, const float* v,
                               const float* qw, const float* kw, int layer, int pos) {
     g_err[0] = 0;
@@ -643,7 +699,6 @@ extern "C" int q3a_attn_layer(q3a_ctx* c, float* xb, float* q, float* k, const f
         return fail(Q3A_ERR_INVALID, "pos %d outside [0, %d)", pos, c->cfg.max_seq);
     int rc = ensure_device(c);
     if (rc) return rc;
-    const size_t qd = (size_t)c->cfg.n_heads * HD, kd = (size_t)c->cfg.n_kv_heads * HD;
     DecodeParams p;
     base_params(c, p, layer);
     p.nb = 1;
@@ -657,30 +712,7 @@ extern "C" int q3a_attn_layer(q3a_ctx* c, float* xb, float* q, float* k, const f
         p.q_out = q; p.k_out = k; p.xb = xb;
         return run_decode(c, p, c->tmK, c->tmV, c->bf16);
     }
-    // host mode: one H2D of [q|k|v|qw|kw], one D2H of [xb|q|k]
-    float* hs = c->h_stage;
-    float* ds = c->d_stage;
-    float *h_xb = hs, *h_q = hs + qd, *h_k = h_q + qd, *h_v = h_k + kd, *h_qw = h_v + kd,
-          *h_kw = h_qw + HD;
-    float *d_xb = ds, *d_q = ds + qd, *d_k = d_q + qd, *d_v = d_k + kd, *d_qw = d_v + kd,
-          *d_kw = d_qw + HD;
-    memcpy(h_q, q, qd * 4);
-    memcpy(h_k, k, kd * 4);
-    memcpy(h_v, v, kd * 4);
-    memcpy(h_qw, qw, HD * 4);
-    memcpy(h_kw, kw, HD * 4);
-    CUDA_TRY(cudaMemcpyAsync(d_q, h_q, (qd + 2 * kd + 2 * HD) * 4, cudaMemcpyHostToDevice,
-                             c->stream));
-    p.q = d_q; p.k_new = d_k; p.v_new = d_v; p.q_norm_w = d_qw; p.k_norm_w = d_kw;
-    p.q_out = d_q; p.k_out = d_k; p.xb = d_xb;
-    rc = run_decode(c, p, c->tmK, c->tmV, c->bf16);
-    if (rc) return rc;
-    CUDA_TRY(cudaMemcpyAsync(h_xb, d_xb, (2 * qd + kd) * 4, cudaMemcpyDeviceToHost, c->stream));
-    CUDA_TRY(cudaStreamSynchronize(c->stream));
-    memcpy(xb, h_xb, qd * 4);
-    memcpy(q, h_q, qd * 4);
-    memcpy(k, h_k, kd * 4);
-    return Q3A_OK;
+    return host_block(c, p, xb, q, k, v, qw, kw, 1);
 }
 
 extern "C" int q3a_attn_layer_batched(q3a_ctx* c, float* xb, float* q, float* k, const float* v,
@@ -709,41 +741,12 @@ extern "C" int q3a_attn_layer_batched(q3a_ctx* c, float* xb, float* q, float* k,
         p.t_begin[b] = 0;
         p.t_end[b] = pos[b];
     }
-    const size_t qd = (size_t)n * c->cfg.n_heads * HD, kd = (size_t)n * c->cfg.n_kv_heads * HD;
     if (c->cfg.ptr_mode == Q3A_PTR_DEVICE) {
         p.q = q; p.k_new = k; p.v_new = v; p.q_norm_w = qw; p.k_norm_w = kw;
         p.q_out = q; p.k_out = k; p.xb = xb;
         return run_decode(c, p, c->tmK, c->tmV, c->bf16);
     }
-    rc = grow_stage(c, 2 * qd + 2 * kd + 2 * HD);
-    if (rc) return rc;
-    float* hs = c->h_stage;
-    float* ds = c->d_stage;
-    float *h_xb = hs, *h_q = hs + qd, *h_k = h_q + qd, *h_v = h_k + kd, *h_qw = h_v + kd,
-          *h_kw = h_qw + HD;
-    float *d_xb = ds, *d_q = ds + qd, *d_k = d_q + qd, *d_v = d_k + kd, *d_qw = d_v + kd,
-          *d_kw = d_qw + HD;
-    memcpy(h_q, q, qd * 4);
-    memcpy(h_k, k, kd * 4);
-    memcpy(h_v, v, kd * 4);
-    memcpy(h_qw, qw, HD * 4);
-    memcpy(h_kw, kw, HD * 4);
-    CUDA_TRY(cudaMemcpyAsync(d_q, h_q, (qd + 2 * kd + 2 * HD) * 4, cudaMemcpyHostToDevice,
-                             c->stream));
-    p.q = d_q; p.k_new = d_k; p.v_new = d_v; p.q_norm_w = d_qw; p.k_norm_w = d_kw;
-    p.q_out = d_q; p.k_out = d_k; p.xb = d_xb;
-    if (c->nkv != c->cfg.n_kv_heads)  // sharded: keep the caller's other xb slices
-        memcpy(h_xb, xb, qd * 4);
-    if (c->nkv != c->cfg.n_kv_heads)
-        CUDA_TRY(cudaMemcpyAsync(d_xb, h_xb, qd * 4, cudaMemcpyHostToDevice, c->stream));
-    rc = run_decode(c, p, c->tmK, c->tmV, c->bf16);
-    if (rc) return rc;
-    CUDA_TRY(cudaMemcpyAsync(h_xb, d_xb, (2 * qd + kd) * 4, cudaMemcpyDeviceToHost, c->stream));
-    CUDA_TRY(cudaStreamSynchronize(c->stream));
-    memcpy(xb, h_xb, qd * 4);
-    memcpy(q, h_q, qd * 4);
-    memcpy(k, h_k, kd * 4);
-    return Q3A_OK;
+    return host_block(c, p, xb, q, k, v, qw, kw, n);
 }
 
 extern "C" int q3a_attn_decode(q3a_ctx* c, float* xb, const float* q, const float* kc,
