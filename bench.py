@@ -7,8 +7,9 @@ one new token, 36 layers x (32 q heads, 8 KV heads, head_dim 128), KV length
 of q3a_attn_layer (QK-norm + RoPE + KV append + attention, one kernel each).
 `value` is HBM GB/s of algorithmic bytes with everything resident in HBM;
 `us_per_layer` is the same measurement as time per layer.  `e2e` is the same
-metric through the host-pointer C-ABI (q, k, v, norm gains copied in from
-pinned memory and xb, q, k copied out, every layer, synchronously).
+metric through the host-pointer C-ABI called from a C host
+(qwen3.c_b200/lib/q3a_harness): q, k, v and the norm gains copied in from
+host memory and xb, q, k written back, every layer, synchronously.
 
 Extra keys: `bf16` (the bf16-cache variant), `prefill` (configs[2]: causal
 prefill of 2048 tokens, TFLOP/s of the dense contraction).
@@ -20,7 +21,11 @@ the reference library is absent.
 
 Multi-GPU: one process per GPU (torchrun); every rank decodes its own
 sequence (weak scaling, no data-path collective), value = all ranks' bytes /
-max-over-ranks time.
+max-over-ranks time.  The sharded legs scale strongly and carry their own
+numbers: `long_ctx` (configs[3], sequence-sharded 128K decode; at N > 1 rank
+0 also times the same step on one GPU, so the line gives t(1)/t(N)),
+`ragged_batch` (configs[4], KV-head sharded) and `prefill` (configs[2],
+KV-head sharded).
 """
 from __future__ import annotations
 
@@ -246,10 +251,9 @@ def decode_run(args, torch, dev, local, kv_dtype, seed, world, with_e2e, with_cp
            "bytes_per_layer": algo_bytes_per_layer(esize), "esize": esize}
     del g
 
-    if with_e2e:
-        res["e2e"] = e2e_run(args, torch, dev, local, kv_dtype, seed, q_raw, k_raw, v_in, ctx,
-                             stream)
     ctx.close()
+    if with_e2e:
+        res["e2e"] = e2e_run(args, local, kv_dtype, seed)
     return res
 
 
@@ -395,6 +399,38 @@ def long_ctx_run(args, torch, dev, local, world, rank):
             "rows_local": n_loc}
 
 
+def long_ctx_single(args, torch, dev, local):
+    """configs[3] on one GPU (rank 0 alone), for t(1)/t(N) in a multi-GPU run:
+    the same per-layer launch with the whole 131072-row sequence local."""
+    import q3attn
+    import shard
+    stream = torch.cuda.Stream(device=dev)
+    ctx = q3attn.Context(n_layers=N_LAYERS, max_seq=LONG_L, kv_dtype=q3attn.KV_BF16,
+                         ptr_mode=q3attn.PTR_DEVICE, device=local)
+    ctx.set_stream(stream.cuda_stream)
+    fill_cache(ctx, torch, dev, 4242, N_LAYERS, LONG_L, stream)
+    q = torch.empty(N_LAYERS, HQ * HD, device=dev)
+    for l in range(N_LAYERS):
+        ctx.randn(q[l], q3attn.OUT_F32, HQ * HD, 4242, l * 16 + 3)
+    xb = torch.zeros(N_LAYERS, HQ * HD, device=dev)
+    stream.synchronize()
+    dec = shard.SeqShardDecode(torch, ctx, world=1, rank=0, device=dev, mode="peer")
+
+    def step():
+        for l in range(N_LAYERS):
+            dec(xb[l], q[l], 0, l, LONG_L)
+
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            step()
+    stream.synchronize()
+    K = max(2, args.steps // 10)
+    t_ms, _ = time_graph(torch, dev, local, stream, step, K, 1)
+    ctx.check_device_error()
+    ctx.close()
+    return t_ms * 1000.0 / (K * N_LAYERS)
+
+
 def ragged_lengths():
     """configs[4] KV lengths: 64 draws from U[512, 32768] (numpy PCG64, seed
     2024); sequence b attends rows 0..L_b-1, the last being its new token."""
@@ -462,54 +498,28 @@ def ragged_run(args, torch, dev, local, world, rank):
             "bytes_per_step": total_bytes, "mean_len": float(lens.mean())}
 
 
-def e2e_run(args, torch, dev, local, kv_dtype, seed, q_raw, k_raw, v_in, dctx, stream):
-    """Same step through the host-pointer API: every layer copies its inputs
-    in from host memory and its result out, synchronously."""
-    import numpy as np
-    import q3attn
-    hctx = q3attn.Context(n_layers=N_LAYERS, max_seq=L_CTX, kv_dtype=kv_dtype,
-                          ptr_mode=q3attn.PTR_HOST, device=local)
-    # same cache contents: generate on device, copy through host
-    kraw = torch.empty(POS * KV_DIM, device=dev)
-    vraw = torch.empty(POS * KV_DIM, device=dev)
-    kh = torch.empty(POS * KV_DIM, pin_memory=True)
-    vh = torch.empty(POS * KV_DIM, pin_memory=True)
-    ones = np.ones(HD, np.float32)
-    for l in range(N_LAYERS):
-        dctx.randn(kraw, q3attn.OUT_F32, kraw.numel(), seed, l * 16 + 1)
-        dctx.randn(vraw, q3attn.OUT_F32, vraw.numel(), seed, l * 16 + 2)
-        stream.synchronize()
-        kh.copy_(kraw)
-        vh.copy_(vraw)
-        hctx.kv_append(0, l, 0, POS, kh.numpy(), vh.numpy(), ones)
-    qh = q_raw.cpu().numpy()
-    khr = k_raw.cpu().numpy()
-    vhh = v_in.cpu().numpy()
-    qbuf = np.empty(HQ * HD, np.float32)
-    kbuf = np.empty(KV_DIM, np.float32)
-    xbh = np.zeros((N_LAYERS, HQ * HD), np.float32)
-    n0 = hctx.launch_count()
-
-    def step():
-        for l in range(N_LAYERS):
-            np.copyto(qbuf, qh[l])
-            np.copyto(kbuf, khr[l])
-            hctx.attn_layer(xbh[l], qbuf, kbuf, vhh[l], ones, ones, l, POS)
-
-    for _ in range(max(3, args.warmup)):
-        step()
-    K = args.steps
-    t0 = time.perf_counter()
-    for _ in range(K):
-        step()
-    t1 = time.perf_counter()
-    hctx.check_device_error()
-    launches = hctx.launch_count() - n0 - max(3, args.warmup) * N_LAYERS
-    hctx.close()
-    h2d = N_LAYERS * (HQ * HD * 4 + 2 * KV_DIM * 4 + 2 * HD * 4)
-    d2h = N_LAYERS * (2 * HQ * HD * 4 + KV_DIM * 4)
-    return {"t_ms": (t1 - t0) * 1000.0, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-            "launches": launches}
+def e2e_run(args, local, kv_dtype, seed):
+    """Same step end to end through the host-pointer C-ABI from a C host:
+    qwen3.c_b200/lib/q3a_harness (a C program built against
+    include/q3attn.h only) runs 36 layer calls of q3a_attn_layer per step on
+    this rank's GPU, every call copying q, k, v and the norm gains in from
+    host memory and xb, q, k out, synchronously, and times K steps with
+    CLOCK_MONOTONIC after W warm-up steps.  Its caches hold the same seeded
+    rows as the device-timed leg (q3a_kv_synth, streams layer*16+1/2)."""
+    import subprocess
+    exe = os.path.join(ROOT, "qwen3.c_b200", "lib", "q3a_harness")
+    if not os.path.exists(exe):
+        raise RuntimeError(f"{exe} is missing: build it (make -C qwen3.c_b200)")
+    cmd = [exe, "--layers", str(N_LAYERS), "--ctx", str(L_CTX),
+           "--kv", "bf16" if kv_dtype == 1 else "f32", "--steps", str(args.steps),
+           "--warmup", str(max(3, args.warmup)), "--seed", str(seed), "--device", str(local)]
+    r = subprocess.run(cmd, capture_output=True, text=True, timeout=600)
+    if r.returncode != 0:
+        raise RuntimeError(f"q3a_harness failed: {r.stderr[-500:]}")
+    h = json.loads(r.stdout.strip().splitlines()[-1])
+    return {"t_ms": h["t_s"] * 1000.0, "h2d_bytes_per_step": h["h2d_bytes_per_step"],
+            "d2h_bytes_per_step": h["d2h_bytes_per_step"], "launches": h["launches"],
+            "us_per_layer": h["us_per_layer"]}
 
 
 # ------------------------------------------------------------------ CPU reference
@@ -708,8 +718,10 @@ def main():
                        "h2d_bytes_per_step": e["h2d_bytes_per_step"],
                        "d2h_bytes_per_step": e["d2h_bytes_per_step"],
                        "us_per_layer": t_e * 1000.0 / (K * N_LAYERS),
-                       "api": "q3a_attn_layer, host pointers, synchronous per layer",
-                       "timer": "host perf_counter around K steps"}
+                       "api": "q3a_attn_layer, host pointers, synchronous per layer, "
+                              "called from the C host qwen3.c_b200/lib/q3a_harness",
+                       "timer": "CLOCK_MONOTONIC around K steps in the C host",
+                       "gpu_launches": e["launches"]}
     if not args.no_variants:
         b = decode_run(args, torch, dev, local, q3attn.KV_BF16, seed, world, with_e2e=False,
                        with_cpu=False)
@@ -780,6 +792,14 @@ def main():
                             "hbm_frac_per_gpu": bpl_l / world / (us_l * 1e-6) / 1e9 / hbm_peak,
                             "clocks": lc["clocks"], "gpu_launches": lc["launches"]}
         line["gpu_launches"] += lc["launches"]
+        if world > 1:
+            # t(1) of the same step, on rank 0's GPU alone (the others wait)
+            barrier(world)
+            if rank == 0:
+                t1 = long_ctx_single(args, torch, dev, local)
+                line["long_ctx"]["us_per_layer_1gpu"] = t1
+                line["long_ctx"]["speedup_vs_1gpu"] = t1 / us_l
+            barrier(world)
         rg = ragged_run(args, torch, dev, local, world, rank)
         t_r = max_over_ranks(rg["t_ms"], world, dev)
         us_s = t_r * 1000.0 / rg["steps"]
