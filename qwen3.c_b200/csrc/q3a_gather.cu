@@ -76,27 +76,31 @@ __global__ void __launch_bounds__(256) gather_cols_kernel(const __grid_constant_
     }
     __syncthreads();
     if (ok_s) {
-        // four 16-byte vectors per thread per step, loaded together so four
-        // reads are in flight before the stores to the peers
+        // GATHER_UNROLL 16-byte vectors per thread per step, loaded together
+        // (read-only path) so that many reads are in flight before the
+        // stores to the peers; consecutive threads take consecutive vectors
+        // of a row's slice, so every store to a peer is a contiguous run
+        constexpr int GATHER_UNROLL = 8;
         const long long total = P.rows * P.vecs;
         const long long stride = (long long)gridDim.x * blockDim.x;
-        for (long long i0 = (long long)blockIdx.x * blockDim.x + tid; i0 < total; i0 += 4 * stride) {
-            int4 v[4];
-            long long o[4];
+        for (long long i0 = (long long)blockIdx.x * blockDim.x + tid; i0 < total;
+             i0 += GATHER_UNROLL * stride) {
+            int4 v[GATHER_UNROLL];
+            long long o[GATHER_UNROLL];
 #pragma unroll
-            for (int u = 0; u < 4; u++) {
+            for (int u = 0; u < GATHER_UNROLL; u++) {
                 const long long i = i0 + u * stride;
                 o[u] = -1;
                 if (i < total) {
                     const long long row = i / P.vecs;
                     o[u] = row * P.row_bytes + P.col0 + (i - row * P.vecs) * 16;
-                    v[u] = *reinterpret_cast<const int4*>(P.local + o[u]);
+                    v[u] = __ldg(reinterpret_cast<const int4*>(P.local + o[u]));
                 }
             }
             for (int r = 0; r < P.world; r++) {
                 if (r == P.rank) continue;
 #pragma unroll
-                for (int u = 0; u < 4; u++)
+                for (int u = 0; u < GATHER_UNROLL; u++)
                     if (o[u] >= 0) *reinterpret_cast<int4*>(P.peer[r] + o[u]) = v[u];
             }
         }
