@@ -12,7 +12,10 @@ metric through the host-pointer C-ABI called from a C host
 host memory and xb, q, k written back, every layer, synchronously.
 
 Extra keys: `bf16` (the bf16-cache variant), `prefill` (configs[2]: causal
-prefill of 2048 tokens, TFLOP/s of the dense contraction).
+prefill of 2048 tokens, TFLOP/s of the dense contraction), `proj` (the block
+from the layer input: fp16 q/k/v projections fused with QK-norm, RoPE and
+the append, then the decode; `proj.qkv` is the projection kernel alone
+against the HBM roofline).
 
 --impl reference times the reference's own CPU code (oracle/_ref, compiled
 from the reference sources: launch_attn with OpenMP over heads, plus its
@@ -254,6 +257,68 @@ def decode_run(args, torch, dev, local, kv_dtype, seed, world, with_e2e, with_cp
     ctx.close()
     if with_e2e:
         res["e2e"] = e2e_run(args, local, kv_dtype, seed)
+    return res
+
+
+DIM = 4096               # Qwen3-8B model width (rows of the projections' input)
+
+
+def proj_bytes(esize: int) -> int:
+    """Algorithmic bytes of one projection launch (qkv_kernel): the fp16
+    weights of q, k, v ((32 + 8 + 8) x 128 rows x 4096 columns), the fp32
+    input x, the fp32 q written, and the new K/V row appended."""
+    rows = (HQ + 2 * HKV) * HD
+    return rows * DIM * 2 + DIM * 4 + HQ * HD * 4 + 2 * KV_DIM * esize
+
+
+def proj_run(args, torch, dev, local, seed, world):
+    """The attention block from the layer input (the producer
+    side): per layer q3a_qkv_proj alone, and q3a_attn_layer_proj (projection
+    kernel + decode over 8193 rows of the fp32 cache), 36 layers per step.
+    Weights N(0, 0.02^2) in fp16, 36 x 50 MB = 1.8 GB (> L2: every step
+    streams them from HBM)."""
+    import q3attn
+    stream = torch.cuda.Stream(device=dev)
+    ctx = q3attn.Context(n_layers=N_LAYERS, max_seq=L_CTX, kv_dtype=q3attn.KV_F32,
+                         ptr_mode=q3attn.PTR_DEVICE, device=local)
+    ctx.set_stream(stream.cuda_stream)
+    fill_cache(ctx, torch, dev, seed, N_LAYERS, POS, stream)
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    with torch.cuda.stream(stream):
+        wq = (torch.randn(N_LAYERS, HQ * HD, DIM, device=dev, generator=g) * 0.02).half()
+        wk = (torch.randn(N_LAYERS, KV_DIM, DIM, device=dev, generator=g) * 0.02).half()
+        wv = (torch.randn(N_LAYERS, KV_DIM, DIM, device=dev, generator=g) * 0.02).half()
+        x = torch.randn(N_LAYERS, DIM, device=dev, generator=g)
+    qw = torch.ones(HD, device=dev)
+    kw = torch.ones(HD, device=dev)
+    q = torch.zeros(N_LAYERS, HQ * HD, device=dev)
+    xb = torch.zeros(N_LAYERS, HQ * HD, device=dev)
+    stream.synchronize()
+
+    def step_proj():
+        for l in range(N_LAYERS):
+            ctx.qkv_proj(q[l], None, None, x[l], wq[l], wk[l], wv[l], qw, kw, l, POS)
+
+    def step_layer():
+        for l in range(N_LAYERS):
+            ctx.attn_layer_proj(xb[l], q[l], None, None, x[l], wq[l], wk[l], wv[l], qw, kw, l,
+                                POS)
+
+    res = {}
+    for name, step in (("qkv", step_proj), ("layer", step_layer)):
+        with torch.cuda.stream(stream):
+            for _ in range(args.warmup):
+                step()
+        stream.synchronize()
+        ctx.check_device_error()
+        n0 = ctx.launch_count()
+        t_ms, clocks = time_graph(torch, dev, local, stream, step, args.steps, world)
+        ctx.check_device_error()
+        res[name] = {"t_ms": t_ms, "clocks": clocks,
+                     "launches": ctx.launch_count() - n0}  # the K captured steps
+    ctx.close()
+    del wq, wk, wv
     return res
 
 
@@ -635,6 +700,26 @@ def ncu_case(args):
         ctx.close()
         print(f"ncu case prefill: {args.warmup + args.steps} launches ok")
         return
+    if args.ncu_case == "qkv":
+        # 2 layers of weights (2 x 50 MB) alternating
+        stream = torch.cuda.Stream(device=dev)
+        ctx = q3attn.Context(n_layers=2, max_seq=64, ptr_mode=q3attn.PTR_DEVICE)
+        ctx.set_stream(stream.cuda_stream)
+        with torch.cuda.stream(stream):
+            wq = (torch.randn(2, HQ * HD, DIM, device=dev) * 0.02).half()
+            wk = (torch.randn(2, KV_DIM, DIM, device=dev) * 0.02).half()
+            wv = (torch.randn(2, KV_DIM, DIM, device=dev) * 0.02).half()
+            x = torch.randn(2, DIM, device=dev)
+            w = torch.ones(HD, device=dev)
+            q = torch.zeros(2, HQ * HD, device=dev)
+        for i in range(args.warmup + args.steps):
+            ctx.qkv_proj(q[i % 2], None, None, x[i % 2], wq[i % 2], wk[i % 2], wv[i % 2], w, w,
+                         i % 2, 0)
+        stream.synchronize()
+        ctx.check_device_error()
+        ctx.close()
+        print(f"ncu case qkv: {args.warmup + args.steps} launches ok")
+        return
     kv = q3attn.KV_F32 if args.ncu_case == "decode-f32" else q3attn.KV_BF16
     stream = torch.cuda.Stream(device=dev)
     ctx = q3attn.Context(n_layers=2, max_seq=L_CTX, kv_dtype=kv, ptr_mode=q3attn.PTR_DEVICE)
@@ -664,7 +749,7 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-variants", action="store_true")
-    ap.add_argument("--ncu-case", default=None, choices=["decode-f32", "decode-bf16", "prefill"],
+    ap.add_argument("--ncu-case", default=None, choices=["decode-f32", "decode-bf16", "prefill", "qkv"],
                     help="small single-kernel run for ncu captures (2 layers, direct launches)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
@@ -818,6 +903,36 @@ def main():
                                 / 1e9 / hbm_peak,
                                 "clocks": rg["clocks"], "gpu_launches": rg["launches"]}
         line["gpu_launches"] += rg["launches"]
+        pj = proj_run(args, torch, dev, local, seed, world)
+        pbytes = proj_bytes(4)
+        n_lay = args.steps * N_LAYERS
+        t_q = max_over_ranks(pj["qkv"]["t_ms"], world, dev)
+        t_b = max_over_ranks(pj["layer"]["t_ms"], world, dev)
+        us_q = t_q * 1000.0 / n_lay
+        us_b = t_b * 1000.0 / n_lay
+        ach_q = pbytes / (us_q * 1e-6) / 1e9
+        lbytes = pbytes + bpl
+        line["proj"] = {"metric": "attention block from the layer input, µs/layer (KV 8K)",
+                        "value": world * lbytes * n_lay / (t_b / 1000.0) / 1e9, "unit": "GB/s",
+                        "us_per_layer": us_b, "bytes_per_layer": lbytes,
+                        "scaling": "weak", "n_gpus": world,
+                        "workload": "Qwen3-8B: x[4096] -> fp16 q/k/v projections (50.3 MB of "
+                                    "weights per layer, 1.8 GB for 36 layers) + QK-norm + "
+                                    "RoPE + append (one qkv_kernel launch), then the decode "
+                                    "over 8193 rows of the fp32 cache; 36 layers per step "
+                                    "(q3a_attn_layer_proj)",
+                        "qkv": {"us_per_layer": us_q, "bytes_per_launch": pbytes,
+                                "roofline": {"bound": "hbm", "achieved": ach_q, "peak": hbm_peak,
+                                             "unit": "GB/s", "frac": ach_q / hbm_peak,
+                                             "traffic": profile_traffic("qkv_proj"),
+                                             "kernel": "q3a::qkv_kernel<float>",
+                                             "duration_source": "graph of K x 36 q3a_qkv_proj "
+                                                                "launches between two events, "
+                                                                "/ launches"},
+                                "clocks": pj["qkv"]["clocks"], "gpu_launches": pj["qkv"]["launches"]},
+                        "hbm_frac": lbytes / (us_b * 1e-6) / 1e9 / hbm_peak,
+                        "clocks": pj["layer"]["clocks"], "gpu_launches": pj["layer"]["launches"]}
+        line["gpu_launches"] += pj["qkv"]["launches"] + pj["layer"]["launches"]
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = cpu_reference_sample(n_calls_max=400, budget_s=15.0)
         line["cpu_baseline"] = {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")}

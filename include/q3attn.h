@@ -96,7 +96,10 @@ int q3a_destroy(q3a_ctx *ctx);
 const char *q3a_last_error(void);
 
 /* Sets the CUDA stream (a cudaStream_t) the context queues work on; NULL
- * selects the context's own stream. */
+ * selects the context's own stream.  The own stream is a blocking stream: it
+ * orders with the legacy default stream (work queued there before a call
+ * completes first; work queued there after a call waits for it), not with
+ * other non-blocking streams. */
 int q3a_set_stream(q3a_ctx *ctx, void *cuda_stream);
 int q3a_sync(q3a_ctx *ctx);
 
@@ -153,6 +156,37 @@ int q3a_attn_decode_noalloc(float *xb, const float *q, const float *kc, const fl
  * noalloc launch expired (its xb is then not valid), else Q3A_OK.  No
  * counterpart in the reference, which has no device-side waits. */
 int q3a_noalloc_check_error(void *cuda_stream);
+
+/* The attention block of one token from its layer input: the q/k/v
+ * projections mm(s->q/k/v, s->xb, w->wq/wk/wv[l], dim, ...) with fp16
+ * weights (mm_f16, qwen3-8b/cpu/main.c:1206-1213 called at 1315-1317; HIP
+ * mm_f16_gemv_kernel, qwen3-8b/gpu/main.c:1495-1519), fused with the
+ * QK-RMSNorm, RoPE and the KV append of the block (main.c:1319-1329), then
+ * the attention of q3a_attn_layer over cache rows 0..pos of slot 0.
+ *   x [dim]: the normed layer input (s->xb of the reference);
+ *   wq [n_heads*hd][dim], wk, wv [n_kv*hd][dim]: fp16 weights, row-major;
+ *   q [n_heads*hd] (out): the normalised, rotated q;
+ *   k, v [n_kv*hd] (out, may be NULL): the normalised, rotated k and v;
+ *   xb [n_heads*hd] (out): the attention output.
+ * Sums are fp32 in a fixed order (per thread, over a warp, then over eight
+ * warps), not the reference's one sequential sum: results agree to fp32
+ * rounding and repeat bit for bit.  Device pointers only (Q3A_PTR_DEVICE
+ * contexts holding every KV head); dim a multiple of 8, at most 8192; every
+ * vector and weight pointer 16-byte aligned.  The weights are read before
+ * the wait on the kernel queued just before the call on the stream (they are
+ * streamed while it finishes): that kernel must not write them. */
+int q3a_attn_layer_proj(q3a_ctx *ctx, float *xb, float *q, float *k, float *v, const float *x,
+                        const void *wq, const void *wk, const void *wv, int dim,
+                        const float *q_norm_w, const float *k_norm_w, int layer, int pos);
+
+/* The projection half of q3a_attn_layer_proj alone: q, k, v of one token
+ * from the layer input x (fp16 weights, fp32 sums), QK-RMSNorm and RoPE of q
+ * and k, and the append of k and v to slot 0 at pos; the attention is left
+ * to the caller (qwen3-8b/cpu/main.c:1315-1329, which it replaces).  Same
+ * arguments, outputs and limits as q3a_attn_layer_proj. */
+int q3a_qkv_proj(q3a_ctx *ctx, float *q, float *k, float *v, const float *x, const void *wq,
+                 const void *wk, const void *wv, int dim, const float *q_norm_w,
+                 const float *k_norm_w, int layer, int pos);
 
 /* Batched ragged decode: n new tokens, token i belongs to cache slot
  * seq_ids[i] (distinct) at position pos[i] (host arrays).  The block of

@@ -267,3 +267,39 @@ void orc_attn_partial(float *o, float *lse, const float *q, const float *kc,
         free(s);
     }
 }
+
+/* fp16 -> fp32 by the IEEE 754 binary16 layout: sign, 5-bit exponent (bias
+ * 15), 10-bit mantissa; subnormals normalised, inf/NaN kept (the conversion
+ * host_f16f32 performs, qwen3-8b/cpu/main.c:437-458). */
+static float f16_to_f32(uint16_t h) {
+    uint32_t sign = (uint32_t)(h >> 15) << 31;
+    int e = (h >> 10) & 31;
+    uint32_t m = h & 1023u, bits;
+    if (e == 31) {
+        bits = sign | 0x7F800000u | (m << 13);
+    } else if (e != 0) {
+        bits = sign | ((uint32_t)(e - 15 + 127) << 23) | (m << 13);
+    } else if (m == 0) {
+        bits = sign;
+    } else {  /* subnormal: m * 2^-24, shift the leading one to bit 10 */
+        int sh = 0;
+        while (!(m & 1024u)) { m <<= 1; sh++; }
+        bits = sign | ((uint32_t)(127 - 14 - sh) << 23) | ((m & 1023u) << 13);
+    }
+    float f;
+    memcpy(&f, &bits, 4);
+    return f;
+}
+
+/* mm_f16, qwen3-8b/cpu/main.c:1206-1213 (cpu-multicore/main.c:1213-1221
+ * adds the OpenMP loop over rows): o[i] = sequential fp32 sum over j of
+ * x[j] * w[i][j], w fp16 row-major [d][n]. */
+void orc_mm_f16(float *o, const float *x, const uint16_t *w, int n, int d) {
+    #pragma omp parallel for schedule(static)
+    for (int i = 0; i < d; i++) {
+        const uint16_t *row = w + (size_t)i * n;
+        float acc = 0.0f;
+        for (int j = 0; j < n; j++) acc += x[j] * f16_to_f32(row[j]);
+        o[i] = acc;
+    }
+}

@@ -85,6 +85,10 @@ void orc_attn_partial(float *o, float *lse, const float *q, const float *kc,
                       const float *vc, size_t loff, int t0, int t1, int n_heads,
                       int kv_mul, int hd, int kv_dim);
 
+/* mm_f16 (qwen3-8b/cpu/main.c:1206-1213): o[i] = sum_j x[j] * w[i][j], fp16
+ * weights [d][n] row-major, one sequential fp32 sum per row. */
+void orc_mm_f16(float *o, const float *x, const uint16_t *w, int n, int d);
+
 #ifdef __cplusplus
 }
 #endif

@@ -52,6 +52,7 @@ def lib():
         L.orc_randn.argtypes = [_P, _SZ, _U64, _U64]
         L.orc_lse_merge.argtypes = [_P, _P, _P, _P, _I, _I, _I]
         L.orc_attn_partial.argtypes = [_P, _P, _P, _P, _P, _SZ, _I, _I, _I, _I, _I, _I]
+        L.orc_mm_f16.argtypes = [_P, _P, _P, _I, _I]
         _lib = L
     return _lib
 
@@ -75,6 +76,7 @@ def ref():
         R.q3ref_launch_rope.argtypes = [_P, _I, _I, _I, _F]
         R.q3ref_launch_kv_write.argtypes = [_P, _P, _P, _P, _I]
         R.q3ref_attn_mc.argtypes = [_P, _P, _P, _P, _P, _SZ, _I, _I, _I, _I, _I, _I]
+        R.q3ref_mm_f16.argtypes = [_P, _P, _P, _I, _I]
         _ref = R
     return _ref
 
@@ -137,6 +139,29 @@ def attn_partial(q, kc, vc, loff, t0, t1, n_heads, kv_mul, hd, kv_dim):
     lib().orc_attn_partial(_ptr(o), _ptr(lse), _ptr(q), _ptr(kc), _ptr(vc), loff, t0, t1,
                            n_heads, kv_mul, hd, kv_dim)
     return o, lse
+
+
+def mm_f16(x: np.ndarray, w: np.ndarray) -> np.ndarray:
+    """o = w @ x with fp16 weights w [d][n] (uint16 bits or float16), one
+    sequential fp32 sum per row (mm_f16)."""
+    w16 = np.ascontiguousarray(w).view(np.uint16)
+    d, n = w16.shape
+    x = np.ascontiguousarray(x, np.float32)
+    o = np.zeros(d, np.float32)
+    lib().orc_mm_f16(_ptr(o), _ptr(x), _ptr(w16), n, d)
+    return o
+
+
+def proj_weights(seed: int, d: int, n: int, scale: float = 0.02) -> np.ndarray:
+    """Seeded fp16 weights [d][n]: orc_randn (stream 200) * scale, rounded to
+    fp16 by numpy (round to nearest even)."""
+    return (randn(d * n, seed, 200) * np.float32(scale)).astype(np.float16).reshape(d, n)
+
+
+def all_f16_patterns() -> np.ndarray:
+    """Every fp16 bit pattern once, [64][1024] (zeros, subnormals, normals,
+    +-inf, NaNs)."""
+    return np.arange(65536, dtype=np.uint32).astype(np.uint16).view(np.float16).reshape(64, 1024)
 
 
 def lse_merge(o_parts: np.ndarray, lse_parts: np.ndarray, n_heads: int, hd: int):

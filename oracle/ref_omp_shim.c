@@ -53,3 +53,10 @@ void q3ref_attn_mc(float *xb, const float *q, const float *kc, const float *vc,
         }
     }
 }
+
+/* mm_f16, qwen3-8b/cpu-multicore/main.c:1213-1221: the fp16 GEMV of the
+ * q/k/v projections (called through mm() at the forward pass's
+ * projections). */
+void q3ref_mm_f16(float *o, const float *x, const uint16_t *w, int n, int d) {
+    mm_f16(o, x, w, n, d);
+}

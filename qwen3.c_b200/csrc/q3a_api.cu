@@ -123,6 +123,12 @@ struct q3a_ctx {
     cudaStream_t last_stream = nullptr;
     int last_decode_layer = -1;   // layer of the last launch if it was a decode, else -1
     int last_decode_wrote = 0;    // that decode appended a row to its layer
+    int last_qkv_layer = -1;      // layer of the last launch if it was the projection kernel
+    int last_qkv_pos = -1;        // the row that projection appended (sequence slot 0)
+    // projection scratch (q3a_attn_layer_proj): partial sums and tickets
+    float* qkv_part = nullptr;
+    int* qkv_ticket = nullptr;
+    size_t qkv_part_floats = 0;
     // peer-memory sequence shards (q3a_peer_export / q3a_peer_open)
     int peer_world = 0;
     int peer_rank = -1;
@@ -147,6 +153,14 @@ static int ensure_device(const q3a_ctx* c) {
     CUDA_TRY(cudaGetDevice(&cur));
     if (cur != c->cfg.device) CUDA_TRY(cudaSetDevice(c->cfg.device));
     return Q3A_OK;
+}
+
+// Records that the last launch was neither a decode nor the projection
+// kernel, so the next decode waits for it before reading the cache.
+static inline void forget_last(q3a_ctx* c) {
+    c->last_decode_layer = -1;
+    c->last_qkv_layer = -1;
+    c->last_qkv_pos = -1;
 }
 
 // Host-pointer staging of n tokens: inputs [q | k | v | q gains | k gains]
@@ -253,6 +267,8 @@ static void destroy_ctx(q3a_ctx* c) {
     cudaFree(c->group_epoch);
     cudaFree(c->claims);
     cudaFree(c->pf_part);
+    cudaFree(c->qkv_part);
+    cudaFree(c->qkv_ticket);
     cudaFree(c->err);
     cudaFree(c->d_inv_freq);
     cudaFree(c->d_stage);
@@ -338,7 +354,10 @@ extern "C" int q3a_create(q3a_ctx** out, const q3a_cfg* cfg_in) {
         destroy_ctx(c);
         return fail(Q3A_ERR_OOM, "context scratch");
     }
-    if (cudaStreamCreateWithFlags(&c->own_stream, cudaStreamNonBlocking) != cudaSuccess) {
+    // a blocking stream: it orders with the legacy default stream, so device
+    // buffers that default-stream work wrote before a call are ready for it,
+    // and default-stream work queued after a call sees its results
+    if (cudaStreamCreateWithFlags(&c->own_stream, cudaStreamDefault) != cudaSuccess) {
         destroy_ctx(c);
         return fail(Q3A_ERR_CUDA, "stream creation");
     }
@@ -627,14 +646,22 @@ static int run_decode(q3a_ctx* c, DecodeParams& p, const CUtensorMap& tk, const 
                (c->last_decode_layer != p.layer || !c->last_decode_wrote))
                   ? 1
                   : 0;
+    p.early_rows = INT_MAX;
+    // after this context's projection kernel, which appends one row: the
+    // balanced schedule streams the rows below it early (rows of another
+    // layer are all safe)
+    if (p.cache_mode == CACHE_PAGED && p.dyn && c->last_qkv_pos >= 0 &&
+        c->last_stream == c->stream) {
+        p.early = 1;
+        p.early_rows = c->last_qkv_layer == p.layer ? c->last_qkv_pos : INT_MAX;
+    }
     CUDA_TRY(launch_decode(p, tk, tv, bf16, c->stream));
     c->launches++;
+    forget_last(c);
     if (p.cache_mode == CACHE_PAGED) {
         c->last_stream = c->stream;
         c->last_decode_layer = p.layer;
         c->last_decode_wrote = p.fused;
-    } else {
-        c->last_decode_layer = -1;
     }
     return Q3A_OK;
 }
@@ -713,6 +740,116 @@ extern "C" int q3a_attn_layer(q3a_ctx* c, float* xb, float* q, float* k, const f
         return run_decode(c, p, c->tmK, c->tmV, c->bf16);
     }
     return host_block(c, p, xb, q, k, v, qw, kw, 1);
+}
+
+// Validates and launches the projection kernel (qkv_kernel) of one token at
+// slot 0: q, k, v fp16 GEMVs fused with QK-RMSNorm, RoPE and the KV append.
+static int launch_proj(q3a_ctx* c, float* q, float* k, float* v, const float* x, const void* wq,
+                       const void* wk, const void* wv, int dim, const float* qw, const float* kw,
+                       int layer, int pos) {
+    if (!c || !q || !x || !wq || !wk || !wv || !qw || !kw)
+        return fail(Q3A_ERR_INVALID, "null argument");
+    if (c->cfg.ptr_mode != Q3A_PTR_DEVICE)
+        return fail(Q3A_ERR_UNSUPPORTED, "the projection entry points take device pointers only");
+    if (c->nkv != c->cfg.n_kv_heads)
+        return fail(Q3A_ERR_INVALID, "the projection entry points need a context holding all KV heads");
+    if (dim <= 0 || dim % 8 != 0 || dim > 8192)
+        return fail(Q3A_ERR_UNSUPPORTED, "dim %d: multiples of 8 up to 8192 are implemented", dim);
+    if (layer < 0 || layer >= c->cfg.n_layers) return fail(Q3A_ERR_INVALID, "layer %d", layer);
+    if (pos < 0 || pos >= c->cfg.max_seq)
+        return fail(Q3A_ERR_INVALID, "pos %d outside [0, %d)", pos, c->cfg.max_seq);
+    const uintptr_t align = (uintptr_t)x | (uintptr_t)wq | (uintptr_t)wk | (uintptr_t)wv |
+                            (uintptr_t)q | (uintptr_t)k | (uintptr_t)v | (uintptr_t)qw |
+                            (uintptr_t)kw;
+    if (align & 15) return fail(Q3A_ERR_INVALID, "the vectors and weights must be 16-byte aligned");
+    int rc = ensure_device(c);
+    if (rc) return rc;
+    const int nq = c->cfg.n_heads, nkv = c->cfg.n_kv_heads;
+    const int rows_total = (nq + 2 * nkv) * HD;
+    const size_t part_floats = (size_t)rows_total;
+    if (part_floats > c->qkv_part_floats) {
+        if (c->qkv_part) {
+            cudaStreamSynchronize(c->stream);
+            cudaFree(c->qkv_part);
+            c->qkv_part = nullptr;
+            c->qkv_part_floats = 0;
+        }
+        if (!c->qkv_ticket) {
+            if (cudaMalloc(&c->qkv_ticket, (size_t)(nq + 2 * nkv) * sizeof(int)) != cudaSuccess)
+                return fail(Q3A_ERR_OOM, "projection tickets");
+            CUDA_TRY(cudaMemsetAsync(c->qkv_ticket, 0, (size_t)(nq + 2 * nkv) * sizeof(int), c->stream));
+        }
+        if (cudaMalloc(&c->qkv_part, part_floats * 4) != cudaSuccess)
+            return fail(Q3A_ERR_OOM, "projection partials of %zu bytes", part_floats * 4);
+        c->qkv_part_floats = part_floats;
+        forget_last(c);  // the memset above is a launch on the stream
+    }
+    QkvParams qp;
+    memset(&qp, 0, sizeof(qp));
+    qp.x = x;
+    qp.wq = reinterpret_cast<const __half*>(wq);
+    qp.wk = reinterpret_cast<const __half*>(wk);
+    qp.wv = reinterpret_cast<const __half*>(wv);
+    qp.q_norm_w = qw;
+    qp.k_norm_w = kw;
+    qp.q_out = q;
+    qp.k_out = k;
+    qp.v_out = v;
+    qp.kcache = c->kcache;
+    qp.vcache = c->vcache;
+    qp.part = c->qkv_part;
+    qp.ticket = c->qkv_ticket;
+    qp.err = c->err;
+    qp.inv_freq = c->d_inv_freq;
+    qp.eps = c->cfg.norm_eps;
+    qp.dim = dim;
+    qp.rows_total = rows_total;
+    qp.nq = nq;
+    qp.nkv = nkv;
+    qp.layer = layer;
+    qp.pos = pos;
+    qp.slot = 0;
+    qp.pages_per_seq = c->pages_per_seq;
+    qp.page_tokens = c->cfg.page_tokens;
+    qp.n_pages = c->n_pages;
+    // one CTA per SM; at least one per head, so that a CTA's rows (fewer
+    // than 128) touch at most two heads
+    const int n_ctas = std::min(rows_total, std::max(c->num_sms, nq + 2 * nkv));
+    CUDA_TRY(launch_qkv(qp, c->bf16 != 0, n_ctas, c->stream));
+    c->launches++;
+    forget_last(c);
+    c->last_stream = c->stream;
+    c->last_qkv_layer = layer;
+    c->last_qkv_pos = pos;
+    return Q3A_OK;
+}
+
+extern "C" int q3a_qkv_proj(q3a_ctx* c, float* q, float* k, float* v, const float* x,
+                            const void* wq, const void* wk, const void* wv, int dim,
+                            const float* qw, const float* kw, int layer, int pos) {
+    g_err[0] = 0;
+    return launch_proj(c, q, k, v, x, wq, wk, wv, dim, qw, kw, layer, pos);
+}
+
+// The projections (launch_proj), then the decode of the layer over rows
+// [0, pos] with the prepared q.  Device pointers only.
+extern "C" int q3a_attn_layer_proj(q3a_ctx* c, float* xb, float* q, float* k, float* v,
+                                   const float* x, const void* wq, const void* wk, const void* wv,
+                                   int dim, const float* qw, const float* kw, int layer, int pos) {
+    g_err[0] = 0;
+    if (!xb) return fail(Q3A_ERR_INVALID, "null argument");
+    int rc = launch_proj(c, q, k, v, x, wq, wk, wv, dim, qw, kw, layer, pos);
+    if (rc) return rc;
+    DecodeParams p;
+    base_params(c, p, layer);
+    p.nb = 1;
+    p.fused = 0;
+    p.t_begin[0] = 0;
+    p.t_end[0] = pos + 1;
+    p.slot[0] = 0;
+    p.q = q;
+    p.xb = xb;
+    return run_decode(c, p, c->tmK, c->tmV, c->bf16);
 }
 
 extern "C" int q3a_attn_layer_batched(q3a_ctx* c, float* xb, float* q, float* k, const float* v,
@@ -886,7 +1023,7 @@ extern "C" int q3a_lse_combine(q3a_ctx* c, float* xb, const float* o_parts, cons
     if (c->cfg.ptr_mode == Q3A_PTR_DEVICE) {
         CUDA_TRY(launch_lse_combine(xb, o_parts, qd, lse_parts, nh, n_parts, nh, c->stream));
         c->launches++;
-        c->last_decode_layer = -1;
+        forget_last(c);
         return Q3A_OK;
     }
     rc = grow_scratch(c, ((size_t)n_parts * (qd + nh) + qd) * 4);
@@ -897,7 +1034,7 @@ extern "C" int q3a_lse_combine(q3a_ctx* c, float* xb, const float* o_parts, cons
     CUDA_TRY(cudaMemcpyAsync(d_l, lse_parts, (size_t)n_parts * nh * 4, cudaMemcpyHostToDevice, c->stream));
     CUDA_TRY(launch_lse_combine(d_x, d_o, qd, d_l, nh, n_parts, nh, c->stream));
     c->launches++;
-    c->last_decode_layer = -1;
+    forget_last(c);
     CUDA_TRY(cudaMemcpyAsync(xb, d_x, qd * 4, cudaMemcpyDeviceToHost, c->stream));
     CUDA_TRY(cudaStreamSynchronize(c->stream));
     return Q3A_OK;
@@ -1132,7 +1269,7 @@ extern "C" int q3a_gather_cols(q3a_ctx* c, size_t off, long long rows, size_t ro
     const int n_ctas = (int)std::min<long long>(c->num_sms, std::max<long long>(1, (work + 255) / 256));
     CUDA_TRY(launch_gather_cols(p, n_ctas, c->stream));
     c->launches++;
-    c->last_decode_layer = -1;
+    forget_last(c);
     return Q3A_OK;
 }
 
@@ -1175,7 +1312,7 @@ extern "C" int q3a_lse_combine_packed(q3a_ctx* c, float* xb, const float* parts,
     if (c->cfg.ptr_mode == Q3A_PTR_DEVICE) {
         CUDA_TRY(launch_lse_combine(xb, parts, pw, parts + qd, pw, n_parts, nh, c->stream));
         c->launches++;
-        c->last_decode_layer = -1;
+        forget_last(c);
         return Q3A_OK;
     }
     rc = grow_scratch(c, ((size_t)n_parts * pw + qd) * 4);
@@ -1185,7 +1322,7 @@ extern "C" int q3a_lse_combine_packed(q3a_ctx* c, float* xb, const float* parts,
     CUDA_TRY(cudaMemcpyAsync(d_p, parts, (size_t)n_parts * pw * 4, cudaMemcpyHostToDevice, c->stream));
     CUDA_TRY(launch_lse_combine(d_x, d_p, pw, d_p + qd, pw, n_parts, nh, c->stream));
     c->launches++;
-    c->last_decode_layer = -1;
+    forget_last(c);
     CUDA_TRY(cudaMemcpyAsync(xb, d_x, qd * 4, cudaMemcpyDeviceToHost, c->stream));
     CUDA_TRY(cudaStreamSynchronize(c->stream));
     return Q3A_OK;
@@ -1242,7 +1379,7 @@ static int append_common(q3a_ctx* c, int seq, int layer, int pos0, int n, const 
     }
     CUDA_TRY(launch_append(a, c->stream));
     c->launches++;
-    c->last_decode_layer = -1;
+    forget_last(c);
     if (c->cfg.ptr_mode == Q3A_PTR_HOST) CUDA_TRY(cudaStreamSynchronize(c->stream));
     return Q3A_OK;
 }
@@ -1286,7 +1423,7 @@ extern "C" int q3a_kv_synth(q3a_ctx* c, int seq, int layer, int pos0, int n, uin
     a.k_norm_w = s + 2 * kd;
     CUDA_TRY(launch_append(a, c->stream));
     c->launches += 3;
-    c->last_decode_layer = -1;
+    forget_last(c);
     if (c->cfg.ptr_mode == Q3A_PTR_HOST) CUDA_TRY(cudaStreamSynchronize(c->stream));
     return Q3A_OK;
 }
@@ -1304,7 +1441,7 @@ extern "C" int q3a_kv_read(q3a_ctx* c, int seq, int layer, int pos0, int n, floa
     if (c->cfg.ptr_mode == Q3A_PTR_DEVICE) {
         CUDA_TRY(launch_kv_read(a, k, v, c->stream));
         c->launches++;
-        c->last_decode_layer = -1;
+        forget_last(c);
         return Q3A_OK;
     }
     rc = grow_scratch(c, 2 * kd * 4);
@@ -1312,7 +1449,7 @@ extern "C" int q3a_kv_read(q3a_ctx* c, int seq, int layer, int pos0, int n, floa
     float* s = reinterpret_cast<float*>(c->d_scratch);
     CUDA_TRY(launch_kv_read(a, s, s + kd, c->stream));
     c->launches++;
-    c->last_decode_layer = -1;
+    forget_last(c);
     CUDA_TRY(cudaMemcpyAsync(k, s, kd * 4, cudaMemcpyDeviceToHost, c->stream));
     CUDA_TRY(cudaMemcpyAsync(v, s + kd, kd * 4, cudaMemcpyDeviceToHost, c->stream));
     CUDA_TRY(cudaStreamSynchronize(c->stream));
@@ -1330,7 +1467,7 @@ extern "C" int q3a_randn(q3a_ctx* c, void* dst, int out_dtype, size_t n, uint64_
     CUDA_TRY(launch_randn(dst, out_dtype == Q3A_OUT_BF16, n, stream_key(seed, stream_id), offset,
                           c->stream));
     c->launches++;
-    c->last_decode_layer = -1;
+    forget_last(c);
     return Q3A_OK;
 }
 
@@ -1391,14 +1528,14 @@ extern "C" int q3a_prefill(q3a_ctx* c, void* out, int out_dtype, const float* q,
     pp.inv_freq = c->d_inv_freq;
     CUDA_TRY(launch_prep_rows(pp, c->stream));
     c->launches++;
-    c->last_decode_layer = -1;
+    forget_last(c);
     a.k = dk;
     a.v = dv;
     a.k_norm_w = dkw;
     a.do_norm_rope = 1;
     CUDA_TRY(launch_append(a, c->stream));
     c->launches++;
-    c->last_decode_layer = -1;
+    forget_last(c);
     // run the attention in device mode on the staged operands
     const int saved_mode = c->cfg.ptr_mode;
     c->cfg.ptr_mode = Q3A_PTR_DEVICE;
@@ -1547,7 +1684,7 @@ extern "C" int q3a_prefill_attn(q3a_ctx* c, void* out, int out_dtype, const void
     pp.vcache = reinterpret_cast<const __nv_bfloat16*>(c->vcache);
     CUDA_TRY(launch_prefill(pp, tq, c->stream));
     c->launches += pf_launches;
-    c->last_decode_layer = -1;
+    forget_last(c);
     if (c->cfg.ptr_mode == Q3A_PTR_HOST) {
         CUDA_TRY(cudaMemcpyAsync(out, dout, out_bytes, cudaMemcpyDeviceToHost, c->stream));
         CUDA_TRY(cudaStreamSynchronize(c->stream));

@@ -195,6 +195,45 @@ __device__ __forceinline__ void rope_pair(float& v0, float& v1, int pos, float i
     v1 = b;
 }
 
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(FULL, v, o);
+    return v;
+}
+
+// QK-RMSNorm + RoPE of one 128-wide head held by a warp (lane: dims
+// 4*lane..4*lane+3, i.e. RoPE pairs 2*lane and 2*lane+1), as in
+// rmsnorm_head_inplace + apply_rope (qwen3-8b/cpu/main.c:1175-1183,
+// 1282-1295): v *= (1/sqrtf(mean(v^2)+eps)) * w, then pair rotation.
+__device__ __forceinline__ float4 norm_rope_lane(float4 x, float4 w, float eps, int pos,
+                                                 float2 inv_freq) {
+    float ss = __fadd_rn(__fadd_rn(__fmul_rn(x.x, x.x), __fmul_rn(x.y, x.y)),
+                         __fadd_rn(__fmul_rn(x.z, x.z), __fmul_rn(x.w, x.w)));
+    ss = warp_sum(ss);
+    const float sc = 1.0f / sqrtf(__fadd_rn(ss / (float)HD, eps));
+    float v0 = __fmul_rn(x.x, __fmul_rn(sc, w.x));
+    float v1 = __fmul_rn(x.y, __fmul_rn(sc, w.y));
+    float v2 = __fmul_rn(x.z, __fmul_rn(sc, w.z));
+    float v3 = __fmul_rn(x.w, __fmul_rn(sc, w.w));
+    rope_pair(v0, v1, pos, inv_freq.x);
+    rope_pair(v2, v3, pos, inv_freq.y);
+    return make_float4(v0, v1, v2, v3);
+}
+
+template <typename KV>
+__device__ __forceinline__ void store4(KV* dst, float4 v) {
+    if constexpr (sizeof(KV) == 4) {
+        *reinterpret_cast<float4*>(dst) = v;
+    } else {
+        __nv_bfloat162 a = __floats2bfloat162_rn(v.x, v.y);
+        __nv_bfloat162 b = __floats2bfloat162_rn(v.z, v.w);
+        uint2 u;
+        u.x = *reinterpret_cast<uint32_t*>(&a);
+        u.y = *reinterpret_cast<uint32_t*>(&b);
+        *reinterpret_cast<uint2*>(dst) = u;
+    }
+}
+
 // Named barrier that also returns the AND of a predicate over its threads.
 __device__ __forceinline__ bool named_bar_red_and(int id, int nthreads, bool v) {
     int r;

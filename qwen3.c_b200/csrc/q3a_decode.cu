@@ -450,45 +450,6 @@ __device__ __forceinline__ void process_rows(const KV* Kt, const KV* Vt, int lo,
     __syncwarp();
 }
 
-__device__ __forceinline__ float warp_sum(float v) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(FULL, v, o);
-    return v;
-}
-
-// QK-RMSNorm + RoPE of one 128-wide head held by a warp (lane: dims
-// 4*lane..4*lane+3, i.e. RoPE pairs 2*lane and 2*lane+1), as in
-// rmsnorm_head_inplace + apply_rope (qwen3-8b/cpu/main.c:1175-1183,
-// 1282-1295): v *= (1/sqrtf(mean(v^2)+eps)) * w, then pair rotation.
-__device__ __forceinline__ float4 norm_rope_lane(float4 x, float4 w, float eps, int pos,
-                                                 float2 inv_freq) {
-    float ss = __fadd_rn(__fadd_rn(__fmul_rn(x.x, x.x), __fmul_rn(x.y, x.y)),
-                         __fadd_rn(__fmul_rn(x.z, x.z), __fmul_rn(x.w, x.w)));
-    ss = warp_sum(ss);
-    const float sc = 1.0f / sqrtf(__fadd_rn(ss / (float)HD, eps));
-    float v0 = __fmul_rn(x.x, __fmul_rn(sc, w.x));
-    float v1 = __fmul_rn(x.y, __fmul_rn(sc, w.y));
-    float v2 = __fmul_rn(x.z, __fmul_rn(sc, w.z));
-    float v3 = __fmul_rn(x.w, __fmul_rn(sc, w.w));
-    rope_pair(v0, v1, pos, inv_freq.x);
-    rope_pair(v2, v3, pos, inv_freq.y);
-    return make_float4(v0, v1, v2, v3);
-}
-
-template <typename KV>
-__device__ __forceinline__ void store4(KV* dst, float4 v) {
-    if constexpr (sizeof(KV) == 4) {
-        *reinterpret_cast<float4*>(dst) = v;
-    } else {
-        __nv_bfloat162 a = __floats2bfloat162_rn(v.x, v.y);
-        __nv_bfloat162 b = __floats2bfloat162_rn(v.z, v.w);
-        uint2 u;
-        u.x = *reinterpret_cast<uint32_t*>(&a);
-        u.y = *reinterpret_cast<uint32_t*>(&b);
-        *reinterpret_cast<uint2*>(dst) = u;
-    }
-}
-
 // ---- peer-memory exchange words: each 8-byte word carries a 32-bit value
 // and the call number it belongs to, stored and loaded as one naturally
 // aligned 64-bit access, so a reader that sees the call number also sees the
@@ -697,7 +658,10 @@ __global__ void __launch_bounds__(DecCfg<KV, TC>::NTHREADS, 1)
             // it first waits for that kernel's writes to be visible; with
             // `early` the stream starts at once, overlapping the previous
             // kernel's tail.
-            if (!P.early) griddep_wait();
+            // A bound on the early rows (`early_rows`) is kept by the
+            // balanced schedule only; the static schedules then wait first.
+            const bool early = P.early && (P.dyn || P.early_rows == INT_MAX);
+            if (!early) griddep_wait();
             const uint64_t pol = l2_policy_evict_first();
             int it = 0;
             bool dead = false;
@@ -712,7 +676,7 @@ __global__ void __launch_bounds__(DecCfg<KV, TC>::NTHREADS, 1)
                 const int i = s.slot - s.slot0, k = s.ncontrib;
                 int u = i * C::STATIC_UNITS;
                 const int u_st_end = min(u + C::STATIC_UNITS, d.n_claim);
-                bool waited = !P.early, held = false;
+                bool waited = !early, held = false;
                 constexpr int ESZ = (int)sizeof(KV);
                 // the next ring slot, once the consumers have freed it
                 auto acquire = [&]() -> bool {
@@ -763,11 +727,13 @@ __global__ void __launch_bounds__(DecCfg<KV, TC>::NTHREADS, 1)
                         // one unit streams before the dependency wait: it fills
                         // the pipeline while the previous kernel finishes,
                         // without flooding the memory queues its merge waits on
-                        if (!waited && u > i * C::STATIC_UNITS) {
+                        row0 = d.a0 + u * C::TILE;
+                        if (!waited && (u > i * C::STATIC_UNITS ||
+                                        row0 + unit_rows(row0) > P.early_rows)) {
                             griddep_wait();
                             waited = true;
                         }
-                        row0 = d.a0 + (u++) * C::TILE;
+                        u++;
                         if (!acquire()) dead = true;
                     } else {
                         if (!waited) {  // the counters are reset by the kernel before

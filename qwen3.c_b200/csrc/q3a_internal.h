@@ -3,7 +3,9 @@
 #pragma once
 
 #include <cuda.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
+#include <limits.h>
 #include <stdint.h>
 
 #include "../../include/q3attn.h"
@@ -87,6 +89,8 @@ struct DecodeParams {
     int tc;                  // 1: tensor-core consumer (bf16 paged cache; 16-row swizzled maps)
     int early;               // 1: the producer streams cache rows before the dependency wait
                              //    (the host checked that the kernel depended on cannot write them)
+    int early_rows;          // with `early`: only rows below this may stream before the wait
+                             //    (the balanced schedule; INT_MAX when every row may)
     int dyn;                 // 1 (piece mode, paged cache, spread merge): each range streams a
                              //    few static units of its group, then claims the group's other
                              //    units from claim[group] (balances ranges on slower SMs)
@@ -140,6 +144,33 @@ struct AppendParams {
     int bf16;
     const float* inv_freq;   // [64] device table
 };
+
+// The q/k/v projections of one token with fp16 weights, fused with the
+// QK-RMSNorm, RoPE and KV append of the block (qkv_kernel).
+struct QkvParams {
+    const float* x;          // [dim] input (the normed layer input)
+    const __half* wq;        // [nq*128][dim] row-major
+    const __half* wk;        // [nkv*128][dim]
+    const __half* wv;        // [nkv*128][dim]
+    const float* q_norm_w;   // [128]
+    const float* k_norm_w;
+    float* q_out;            // [nq*128] normalised, rotated q
+    float* k_out;            // [nkv*128] normalised, rotated k, may be null
+    float* v_out;            // [nkv*128] v, may be null
+    void* kcache;            // the context's paged caches (append at pos)
+    void* vcache;
+    float* part;             // scratch [rows_total]: the row sums
+    int* ticket;             // scratch [nq + 2 nkv] rows summed per head, zero between launches
+    int* err;                // device error flag (a wait that expired)
+    const float* inv_freq;   // [64] RoPE inverse frequencies
+    float eps;
+    int dim;                 // columns (multiple of 8, at most 8192)
+    int nq, nkv;
+    int rows_total;          // (nq + 2 nkv) * 128
+    int layer, pos, slot, pages_per_seq, page_tokens, n_pages;
+};
+// n_ctas >= nq + 2 nkv (a CTA's rows then touch at most two heads)
+cudaError_t launch_qkv(const QkvParams& p, bool bf16, int n_ctas, cudaStream_t st);
 
 // Raises the dynamic shared-memory limit of kernel `fn` to `bytes` on the
 // current device.  The attribute is per device, so it is set once per

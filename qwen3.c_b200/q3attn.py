@@ -25,7 +25,8 @@ MAX_BATCH = 256
 EXPORTS = [
     "q3a_cfg_default", "q3a_create", "q3a_destroy", "q3a_last_error", "q3a_set_stream",
     "q3a_sync", "q3a_check_device_error", "q3a_attn_layer", "q3a_attn_decode",
-    "q3a_attn_layer_batched", "q3a_kv_append", "q3a_kv_load", "q3a_kv_read", "q3a_prefill",
+    "q3a_attn_layer_batched", "q3a_attn_layer_proj", "q3a_qkv_proj",
+    "q3a_kv_append", "q3a_kv_load", "q3a_kv_read", "q3a_prefill",
     "q3a_prefill_attn", "q3a_attn_partial", "q3a_lse_combine", "q3a_lse_combine_packed",
     "q3a_peer_export", "q3a_peer_open", "q3a_attn_seqshard",
     "q3a_peer_buffer", "q3a_peer_open_ptrs",
@@ -77,6 +78,8 @@ def load():
         L.q3a_attn_layer.argtypes = [_P, _P, _P, _P, _P, _P, _P, _I, _I]
         L.q3a_attn_decode.argtypes = [_P, _P, _P, _P, _P, _P, _SZ, _I, _I, _I, _I, _I, _I]
         L.q3a_attn_layer_batched.argtypes = [_P, _P, _P, _P, _P, _P, _P, _I, _P, _P, _I]
+        L.q3a_attn_layer_proj.argtypes = [_P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _P, _P, _I, _I]
+        L.q3a_qkv_proj.argtypes = [_P, _P, _P, _P, _P, _P, _P, _P, _I, _P, _P, _I, _I]
         L.q3a_kv_append.argtypes = [_P, _I, _I, _I, _I, _P, _P, _P]
         L.q3a_kv_load.argtypes = [_P, _I, _I, _I, _I, _P, _P]
         L.q3a_kv_read.argtypes = [_P, _I, _I, _I, _I, _P, _P]
@@ -189,6 +192,18 @@ class Context:
     def attn_layer(self, xb, q, k, v, qw, kw, layer, pos):
         check(self.lib.q3a_attn_layer(self.h, ptr(xb), ptr(q), ptr(k), ptr(v), ptr(qw), ptr(kw),
                                       layer, pos))
+
+    def attn_layer_proj(self, xb, q, k, v, x, wq, wk, wv, qw, kw, layer, pos):
+        """Projections (fp16 weights) + QK-norm + RoPE + append + attention of
+        one token from its layer input x; device tensors; k, v may be None."""
+        check(self.lib.q3a_attn_layer_proj(self.h, ptr(xb), ptr(q), ptr(k), ptr(v), ptr(x),
+                                           ptr(wq), ptr(wk), ptr(wv), int(x.numel()), ptr(qw),
+                                           ptr(kw), layer, pos))
+
+    def qkv_proj(self, q, k, v, x, wq, wk, wv, qw, kw, layer, pos):
+        """The projection half of attn_layer_proj (no attention)."""
+        check(self.lib.q3a_qkv_proj(self.h, ptr(q), ptr(k), ptr(v), ptr(x), ptr(wq), ptr(wk),
+                                    ptr(wv), int(x.numel()), ptr(qw), ptr(kw), layer, pos))
 
     def attn_layer_batched(self, xb, q, k, v, qw, kw, layer, seq_ids, pos):
         import numpy as np

@@ -178,10 +178,53 @@ def main():
                 "(qwen3-8b/cpu/main.c:1481-1499), bf16-rounded q/k/v, heads subset",
         "cases": pre_cases}
 
+    proj_golden(meta)
     with open(os.path.join(HERE, "manifest.json"), "w") as f:
         json.dump(meta, f, indent=1)
     print("wrote golden vectors to", HERE)
 
 
+def proj_golden(meta):
+    """4. The fp16 GEMV of the q/k/v projections (mm_f16,
+    qwen3-8b/cpu-multicore/main.c:1213-1221) run by the reference."""
+    R = orc.ref()
+    arrays = {}
+    cases = []
+    for i, (n, d) in enumerate([(4096, 64), (1024, 48)]):
+        seed = SEED + 2000 + i
+        w = orc.proj_weights(seed, d, n)
+        x = orc.randn(n, seed, 201)
+        o = np.zeros(d, np.float32)
+        R.q3ref_mm_f16(_p(o), _p(x), _p(w.view(np.uint16)), n, d)
+        arrays[f"m{i}_out"] = o
+        arrays[f"m{i}_inputs_checksum"] = np.float64(checksum(x, w.astype(np.float32)))
+        cases.append({"seed": seed, "n": n, "d": d, "scale": 0.02})
+    # every fp16 value: rows of all 65536 patterns against x = 1, and the
+    # conversion alone (n = 1, x = [1])
+    w = orc.all_f16_patterns()
+    o = np.zeros(64, np.float32)
+    R.q3ref_mm_f16(_p(o), _p(np.ones(1024, np.float32)), _p(w.view(np.uint16)), 1024, 64)
+    arrays["patterns_rowsum"] = o
+    conv = np.zeros(65536, np.float32)
+    R.q3ref_mm_f16(_p(conv), _p(np.ones(1, np.float32)),
+                   _p(np.ascontiguousarray(w.reshape(65536, 1)).view(np.uint16)), 1, 65536)
+    arrays["patterns_value"] = conv
+    np.savez(os.path.join(HERE, "projection.npz"), **arrays)
+    meta["files"]["projection.npz"] = {
+        "what": "mm_f16 (qwen3-8b/cpu-multicore/main.c:1213-1221) run by the reference: "
+                "seeded weights (orc_randn * scale rounded to fp16) and x = orc_randn, and "
+                "every fp16 bit pattern (row sums against x = 1; each value alone)",
+        "cases": cases}
+
+
 if __name__ == "__main__":
-    main()
+    if sys.argv[1:] == ["projection"]:  # only the projection fixture
+        if not orc.ref_available():
+            raise SystemExit("oracle/_ref/libq3ref.so is not built (make -C oracle ref REF=...)")
+        with open(os.path.join(HERE, "manifest.json")) as f:
+            m = json.load(f)
+        proj_golden(m)
+        with open(os.path.join(HERE, "manifest.json"), "w") as f:
+            json.dump(m, f, indent=1)
+    else:
+        main()

@@ -168,3 +168,28 @@ def test_oracle_vs_compiled_reference_random(pos):
                     HQ, KV_MUL, HD, KV_DIM, max_seq)
     xo = orc.attn_decode(q, kc, vc, 0, pos, HQ, KV_MUL, HD, KV_DIM, max_seq)
     assert np.array_equal(xo, xr)
+
+
+def test_mm_f16_matches_reference():
+    """mm_f16 (the projections' fp16 GEMV) bit for bit against the reference's
+    own outputs: seeded weights, and every fp16 bit pattern."""
+    g = _load("projection.npz")
+    for i, case in enumerate(_manifest()["files"]["projection.npz"]["cases"]):
+        w = orc.proj_weights(case["seed"], case["d"], case["n"], case["scale"])
+        x = orc.randn(case["n"], case["seed"], 201)
+        ck = sum(np.float64(a).sum() + np.abs(np.float64(a)).sum()
+                 for a in (x, w.astype(np.float32)))
+        assert ck == float(g[f"m{i}_inputs_checksum"])
+        o = orc.mm_f16(x, w)
+        assert np.array_equal(o.view(np.uint32), g[f"m{i}_out"].view(np.uint32))
+    w = orc.all_f16_patterns()
+    o = orc.mm_f16(np.ones(1024, np.float32), w)
+    assert np.array_equal(o.view(np.uint32), g["patterns_rowsum"].view(np.uint32))
+    conv = orc.mm_f16(np.ones(1, np.float32), w.reshape(65536, 1))
+    assert np.array_equal(conv.view(np.uint32), g["patterns_value"].view(np.uint32))
+    # the conversion alone agrees with numpy's fp16 -> fp32 on every number
+    # (by value: the sum starts at +0, so -0 comes out as +0)
+    ref = w.reshape(-1).astype(np.float32)
+    fin = ~np.isnan(ref)
+    assert np.array_equal(conv[fin], ref[fin])
+    assert np.isnan(conv[~fin]).all()
