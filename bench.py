@@ -12,10 +12,12 @@ metric through the host-pointer C-ABI called from a C host
 host memory and xb, q, k written back, every layer, synchronously.
 
 Extra keys: `bf16` (the bf16-cache variant), `prefill` (configs[2]: causal
-prefill of 2048 tokens, TFLOP/s of the dense contraction), `proj` (the block
-from the layer input: fp16 q/k/v projections fused with QK-norm, RoPE and
-the append, then the decode; `proj.qkv` is the projection kernel alone
-against the HBM roofline).
+prefill of 2048 tokens, TFLOP/s of the dense contraction), `sublayer` (the
+attention sublayer from the residual stream: input RMSNorm fused into the
+fp16 q/k/v projections with QK-norm, RoPE and the append, the decode, the
+wo projection with the residual add; `sublayer.qkv` and `sublayer.wo` are
+the two projection kernels alone against the HBM roofline; at N > 1 the
+sublayer runs tensor-parallel over KV heads).
 
 --impl reference times the reference's own CPU code (oracle/_ref, compiled
 from the reference sources: launch_attn with OpenMP over heads, plus its
@@ -261,27 +263,45 @@ def decode_run(args, torch, dev, local, kv_dtype, seed, world, with_e2e, with_cp
 
 
 DIM = 4096               # Qwen3-8B model width (rows of the projections' input)
+GQA_MUL = HQ // HKV      # query heads per KV head
 
 
-def proj_bytes(esize: int) -> int:
-    """Algorithmic bytes of one projection launch (qkv_kernel): the fp16
-    weights of q, k, v ((32 + 8 + 8) x 128 rows x 4096 columns), the fp32
-    input x, the fp32 q written, and the new K/V row appended."""
-    rows = (HQ + 2 * HKV) * HD
-    return rows * DIM * 2 + DIM * 4 + HQ * HD * 4 + 2 * KV_DIM * esize
+def proj_bytes(esize: int, nkv: int = HKV) -> int:
+    """Algorithmic bytes of one projection launch (qkv_kernel) for nkv held
+    KV heads: the fp16 weights of their q, k, v rows ((4 + 1 + 1) x nkv x
+    128 rows x 4096 columns), the fp32 input x, the fp32 q written, and the
+    new K/V row appended."""
+    rows = (GQA_MUL + 2) * nkv * HD
+    return rows * DIM * 2 + DIM * 4 + GQA_MUL * nkv * HD * 4 + 2 * nkv * HD * esize
 
 
-def proj_run(args, torch, dev, local, seed, world):
-    """The attention block from the layer input (the producer
-    side): per layer q3a_qkv_proj alone, and q3a_attn_layer_proj (projection
-    kernel + decode over 8193 rows of the fp32 cache), 36 layers per step.
-    Weights N(0, 0.02^2) in fp16, 36 x 50 MB = 1.8 GB (> L2: every step
-    streams them from HBM)."""
+def wo_bytes(nkv: int = HKV) -> int:
+    """Algorithmic bytes of one wo launch (wo_kernel) for nkv held KV heads:
+    the fp16 columns of their query heads (4096 rows x 4 x nkv x 128), the
+    fp32 xb slice read, x read and written."""
+    cols = GQA_MUL * nkv * HD
+    return DIM * cols * 2 + cols * 4 + 2 * DIM * 4
+
+
+def sublayer_run(args, torch, dev, local, seed, world, rank):
+    """The attention sublayer from the residual stream (the rows after the
+    path: producer and consumer of the block): per layer q3a_qkv_proj alone,
+    q3a_wo_residual alone, and q3a_attn_sublayer (input RMSNorm fused into the
+    q/k/v projections + QK-norm + RoPE + append, decode over 8193 rows of the
+    fp32 cache, wo + residual), 36 layers per step.  Weights N(0, 0.02^2) in
+    fp16, 36 x 84 MB = 3.0 GB (> L2).  At N > 1 rank r holds KV heads
+    kv_heads(8, N, r): its q/k/v rows, its cache heads and its wo columns;
+    the wo kernel sums the ranks' partial products over NVLink."""
     import q3attn
+    import shard
+    kv0, nkv = shard.kv_heads(HKV, world, rank)
     stream = torch.cuda.Stream(device=dev)
     ctx = q3attn.Context(n_layers=N_LAYERS, max_seq=L_CTX, kv_dtype=q3attn.KV_F32,
-                         ptr_mode=q3attn.PTR_DEVICE, device=local)
+                         ptr_mode=q3attn.PTR_DEVICE, device=local, kv_head_begin=kv0,
+                         kv_head_count=nkv)
     ctx.set_stream(stream.cuda_stream)
+    if world > 1:
+        shard.open_peer_set(ctx, world=world, rank=rank)
     fill_cache(ctx, torch, dev, seed, N_LAYERS, POS, stream)
     g = torch.Generator(device=dev)
     g.manual_seed(seed)
@@ -289,36 +309,42 @@ def proj_run(args, torch, dev, local, seed, world):
         wq = (torch.randn(N_LAYERS, HQ * HD, DIM, device=dev, generator=g) * 0.02).half()
         wk = (torch.randn(N_LAYERS, KV_DIM, DIM, device=dev, generator=g) * 0.02).half()
         wv = (torch.randn(N_LAYERS, KV_DIM, DIM, device=dev, generator=g) * 0.02).half()
-        x = torch.randn(N_LAYERS, DIM, device=dev, generator=g)
+        wo = (torch.randn(N_LAYERS, DIM, HQ * HD, device=dev, generator=g) * 0.02).half()
+        att = 1.0 + 0.1 * torch.randn(N_LAYERS, DIM, device=dev, generator=g)
+        x_in = torch.randn(N_LAYERS, DIM, device=dev, generator=g)
+    x = x_in[0].clone()
     qw = torch.ones(HD, device=dev)
     kw = torch.ones(HD, device=dev)
     q = torch.zeros(N_LAYERS, HQ * HD, device=dev)
-    xb = torch.zeros(N_LAYERS, HQ * HD, device=dev)
+    xb = torch.randn(N_LAYERS, HQ * HD, device=dev, generator=g)
     stream.synchronize()
 
-    def step_proj():
+    def step_qkv():
         for l in range(N_LAYERS):
-            ctx.qkv_proj(q[l], None, None, x[l], wq[l], wk[l], wv[l], qw, kw, l, POS)
+            ctx.qkv_proj(q[l], None, None, x_in[l], wq[l], wk[l], wv[l], qw, kw, l, POS)
 
-    def step_layer():
+    def step_wo():
         for l in range(N_LAYERS):
-            ctx.attn_layer_proj(xb[l], q[l], None, None, x[l], wq[l], wk[l], wv[l], qw, kw, l,
-                                POS)
+            ctx.wo_residual(x, xb[l], wo[l])
 
-    res = {}
-    for name, step in (("qkv", step_proj), ("layer", step_layer)):
+    def step_sub():
+        for l in range(N_LAYERS):
+            ctx.attn_sublayer(x, att[l], wq[l], wk[l], wv[l], qw, kw, wo[l], l, POS)
+
+    res = {"nkv": nkv}
+    for name, step in (("qkv", step_qkv), ("wo", step_wo), ("sublayer", step_sub)):
         with torch.cuda.stream(stream):
             for _ in range(args.warmup):
                 step()
         stream.synchronize()
         ctx.check_device_error()
+        barrier(world)
         n0 = ctx.launch_count()
         t_ms, clocks = time_graph(torch, dev, local, stream, step, args.steps, world)
         ctx.check_device_error()
-        res[name] = {"t_ms": t_ms, "clocks": clocks,
-                     "launches": ctx.launch_count() - n0}  # the K captured steps
+        res[name] = {"t_ms": t_ms, "clocks": clocks, "launches": ctx.launch_count() - n0}
     ctx.close()
-    del wq, wk, wv
+    del wq, wk, wv, wo
     return res
 
 
@@ -700,6 +726,22 @@ def ncu_case(args):
         ctx.close()
         print(f"ncu case prefill: {args.warmup + args.steps} launches ok")
         return
+    if args.ncu_case == "wo":
+        # 2 layers of wo (2 x 34 MB) alternating
+        stream = torch.cuda.Stream(device=dev)
+        ctx = q3attn.Context(n_layers=1, max_seq=64, ptr_mode=q3attn.PTR_DEVICE)
+        ctx.set_stream(stream.cuda_stream)
+        with torch.cuda.stream(stream):
+            wo = (torch.randn(2, DIM, HQ * HD, device=dev) * 0.02).half()
+            xb = torch.randn(2, HQ * HD, device=dev)
+            x = torch.randn(DIM, device=dev)
+        for i in range(args.warmup + args.steps):
+            ctx.wo_residual(x, xb[i % 2], wo[i % 2])
+        stream.synchronize()
+        ctx.check_device_error()
+        ctx.close()
+        print(f"ncu case wo: {args.warmup + args.steps} launches ok")
+        return
     if args.ncu_case == "qkv":
         # 2 layers of weights (2 x 50 MB) alternating
         stream = torch.cuda.Stream(device=dev)
@@ -749,7 +791,7 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-variants", action="store_true")
-    ap.add_argument("--ncu-case", default=None, choices=["decode-f32", "decode-bf16", "prefill", "qkv"],
+    ap.add_argument("--ncu-case", default=None, choices=["decode-f32", "decode-bf16", "prefill", "qkv", "wo"],
                     help="small single-kernel run for ncu captures (2 layers, direct launches)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
@@ -903,36 +945,49 @@ def main():
                                 / 1e9 / hbm_peak,
                                 "clocks": rg["clocks"], "gpu_launches": rg["launches"]}
         line["gpu_launches"] += rg["launches"]
-        pj = proj_run(args, torch, dev, local, seed, world)
-        pbytes = proj_bytes(4)
+        sb = sublayer_run(args, torch, dev, local, seed, world, rank)
+        nkv = sb["nkv"]
         n_lay = args.steps * N_LAYERS
-        t_q = max_over_ranks(pj["qkv"]["t_ms"], world, dev)
-        t_b = max_over_ranks(pj["layer"]["t_ms"], world, dev)
-        us_q = t_q * 1000.0 / n_lay
-        us_b = t_b * 1000.0 / n_lay
-        ach_q = pbytes / (us_q * 1e-6) / 1e9
-        lbytes = pbytes + bpl
-        line["proj"] = {"metric": "attention block from the layer input, µs/layer (KV 8K)",
-                        "value": world * lbytes * n_lay / (t_b / 1000.0) / 1e9, "unit": "GB/s",
-                        "us_per_layer": us_b, "bytes_per_layer": lbytes,
-                        "scaling": "weak", "n_gpus": world,
-                        "workload": "Qwen3-8B: x[4096] -> fp16 q/k/v projections (50.3 MB of "
-                                    "weights per layer, 1.8 GB for 36 layers) + QK-norm + "
-                                    "RoPE + append (one qkv_kernel launch), then the decode "
-                                    "over 8193 rows of the fp32 cache; 36 layers per step "
-                                    "(q3a_attn_layer_proj)",
-                        "qkv": {"us_per_layer": us_q, "bytes_per_launch": pbytes,
-                                "roofline": {"bound": "hbm", "achieved": ach_q, "peak": hbm_peak,
-                                             "unit": "GB/s", "frac": ach_q / hbm_peak,
-                                             "traffic": profile_traffic("qkv_proj"),
-                                             "kernel": "q3a::qkv_kernel<float>",
-                                             "duration_source": "graph of K x 36 q3a_qkv_proj "
-                                                                "launches between two events, "
-                                                                "/ launches"},
-                                "clocks": pj["qkv"]["clocks"], "gpu_launches": pj["qkv"]["launches"]},
-                        "hbm_frac": lbytes / (us_b * 1e-6) / 1e9 / hbm_peak,
-                        "clocks": pj["layer"]["clocks"], "gpu_launches": pj["layer"]["launches"]}
-        line["gpu_launches"] += pj["qkv"]["launches"] + pj["layer"]["launches"]
+        t_q = max_over_ranks(sb["qkv"]["t_ms"], world, dev)
+        t_w = max_over_ranks(sb["wo"]["t_ms"], world, dev)
+        t_s = max_over_ranks(sb["sublayer"]["t_ms"], world, dev)
+        us_q, us_w, us_s = (t * 1000.0 / n_lay for t in (t_q, t_w, t_s))
+        qb, wb = proj_bytes(4, nkv), wo_bytes(nkv)
+        cache_b = 2 * (POS + 1) * nkv * HD * 4
+        sub_b = qb + cache_b + wb                      # per GPU per layer
+        ach_q = qb / (us_q * 1e-6) / 1e9
+        ach_w = wb / (us_w * 1e-6) / 1e9
+        line["sublayer"] = {
+            "metric": "attention sublayer x -> x + attn(x), µs/layer (KV 8K, fp32 cache)",
+            "value": world * sub_b * n_lay / (t_s / 1000.0) / 1e9, "unit": "GB/s",
+            "us_per_layer": us_s, "bytes_per_layer_per_gpu": sub_b, "n_gpus": world,
+            "scaling": "strong",
+            "parallelism": f"kvhead{world}" if world > 1 else "single",
+            "workload": "Qwen3-8B attention sublayer of one token: rmsnorm fused into the fp16 "
+                        "q/k/v projections + QK-norm + RoPE + append (qkv_kernel), decode over "
+                        "8193 rows of the fp32 cache, wo + residual (wo_kernel; at N > 1 the "
+                        "ranks' partial products summed over NVLink inside it); 36 layers per "
+                        "step (q3a_attn_sublayer)",
+            "hbm_frac_per_gpu": sub_b / (us_s * 1e-6) / 1e9 / hbm_peak,
+            "qkv": {"us_per_layer": us_q, "bytes_per_launch": qb,
+                    "roofline": {"bound": "hbm", "achieved": ach_q, "peak": hbm_peak,
+                                 "unit": "GB/s", "frac": ach_q / hbm_peak,
+                                 "traffic": profile_traffic("qkv_proj") if world == 1 else None,
+                                 "kernel": "q3a::qkv_kernel<float,1>",
+                                 "duration_source": "graph of K x 36 q3a_qkv_proj launches "
+                                                    "between two events, / launches"},
+                    "clocks": sb["qkv"]["clocks"], "gpu_launches": sb["qkv"]["launches"]},
+            "wo": {"us_per_layer": us_w, "bytes_per_launch": wb,
+                   "roofline": {"bound": "hbm", "achieved": ach_w, "peak": hbm_peak,
+                                "unit": "GB/s", "frac": ach_w / hbm_peak,
+                                "traffic": profile_traffic("wo_residual") if world == 1 else None,
+                                "kernel": "q3a::wo_kernel<1>",
+                                "duration_source": "graph of K x 36 q3a_wo_residual launches "
+                                                   "between two events, / launches"},
+                   "clocks": sb["wo"]["clocks"], "gpu_launches": sb["wo"]["launches"]},
+            "clocks": sb["sublayer"]["clocks"], "gpu_launches": sb["sublayer"]["launches"]}
+        line["gpu_launches"] += (sb["qkv"]["launches"] + sb["wo"]["launches"] +
+                                 sb["sublayer"]["launches"])
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = cpu_reference_sample(n_calls_max=400, budget_s=15.0)
         line["cpu_baseline"] = {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")}

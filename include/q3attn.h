@@ -168,13 +168,17 @@ int q3a_noalloc_check_error(void *cuda_stream);
  *   q [n_heads*hd] (out): the normalised, rotated q;
  *   k, v [n_kv*hd] (out, may be NULL): the normalised, rotated k and v;
  *   xb [n_heads*hd] (out): the attention output.
- * Sums are fp32 in a fixed order (per thread, over a warp, then over eight
- * warps), not the reference's one sequential sum: results agree to fp32
- * rounding and repeat bit for bit.  Device pointers only (Q3A_PTR_DEVICE
- * contexts holding every KV head); dim a multiple of 8, at most 8192; every
- * vector and weight pointer 16-byte aligned.  The weights are read before
- * the wait on the kernel queued just before the call on the stream (they are
- * streamed while it finishes): that kernel must not write them. */
+ * Sums are fp32 in a fixed order (per thread, over a warp, then over the
+ * consumer warps), not the reference's one sequential sum: results agree to
+ * fp32 rounding and repeat bit for bit.  A context holding KV heads
+ * [b, b + n) (kv_head_begin/count) projects only their rows: q heads 4b ..
+ * 4(b+n)-1 and KV heads b .. b+n-1, written at their places in the
+ * full-width q, k, v (column-parallel), and attends over them (xb: their
+ * columns).  Device pointers only (Q3A_PTR_DEVICE); dim a multiple of 8, at
+ * most 8192; every vector and weight pointer 16-byte aligned.  The weights
+ * are read before the wait on the kernel queued just before the call on the
+ * stream (they are streamed while it finishes): that kernel must not write
+ * them. */
 int q3a_attn_layer_proj(q3a_ctx *ctx, float *xb, float *q, float *k, float *v, const float *x,
                         const void *wq, const void *wk, const void *wv, int dim,
                         const float *q_norm_w, const float *k_norm_w, int layer, int pos);
@@ -187,6 +191,34 @@ int q3a_attn_layer_proj(q3a_ctx *ctx, float *xb, float *q, float *k, float *v, c
 int q3a_qkv_proj(q3a_ctx *ctx, float *q, float *k, float *v, const float *x, const void *wq,
                  const void *wk, const void *wv, int dim, const float *q_norm_w,
                  const float *k_norm_w, int layer, int pos);
+
+/* The consumer of xb: x += wo . xb, the o-projection and residual add of
+ * the attention sublayer (mm(s->xb2, s->xb, w->wo[l], dim, dim) and
+ * x[i] += xb2[i], qwen3-8b/cpu/main.c:1355-1356; HIP mm_f16_gemv_kernel +
+ * vec_add_kernel, qwen3-8b/gpu/main.c:2131-2135).  wo is fp16
+ * [dim][n_heads*hd] row-major, x [dim] and xb [n_heads*hd] fp32 device
+ * buffers; x is updated in place.  A context holding KV heads [b, b + n)
+ * multiplies only their query heads' xb columns (row-parallel) and needs a
+ * peer set (q3a_peer_export / q3a_peer_open over the ranks that hold the
+ * other heads): each rank stores its partial sums into every rank's peer
+ * buffer over NVLink inside the kernel and adds all ranks' partials in rank
+ * order, so every rank's x gets the same bits; every rank of the set makes
+ * the same calls in the same order.  dim at most 8192.  Device pointers only. */
+int q3a_wo_residual(q3a_ctx *ctx, float *x, const float *xb, const void *wo, int dim);
+
+/* The attention sublayer of one token at pos (slot 0), from the residual
+ * stream x to x + attention: rmsnorm(x, att_norm_w) fused into the q/k/v
+ * projections (q3a_qkv_proj), the decode of the held heads over rows 0..pos,
+ * then q3a_wo_residual (qwen3-8b/cpu/main.c:1313-1356; HIP forward_gpu
+ * qwen3-8b/gpu/main.c:2095-2135).  Three kernels, stream-ordered with
+ * programmatic dependent launch (the weights of each stream in while the
+ * kernel before finishes).  Weights and limits as q3a_attn_layer_proj and
+ * q3a_wo_residual; q and xb live in the context.  Over KV-head shards (a
+ * peer set of the ranks holding the other heads) every rank passes the same
+ * x and weights and ends with the same x. */
+int q3a_attn_sublayer(q3a_ctx *ctx, float *x, const float *att_norm_w, const void *wq,
+                      const void *wk, const void *wv, const float *q_norm_w,
+                      const float *k_norm_w, const void *wo, int dim, int layer, int pos);
 
 /* Batched ragged decode: n new tokens, token i belongs to cache slot
  * seq_ids[i] (distinct) at position pos[i] (host arrays).  The block of

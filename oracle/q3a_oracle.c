@@ -303,3 +303,12 @@ void orc_mm_f16(float *o, const float *x, const uint16_t *w, int n, int d) {
         o[i] = acc;
     }
 }
+
+/* rmsnorm, qwen3-8b/cpu/main.c:1168-1173: sequential sum of squares,
+ * ss = 1/sqrtf(ss/n + eps), o[i] = x[i] * ss * w[i] (left to right). */
+void orc_rmsnorm(float *o, const float *x, const float *w, int n, float eps) {
+    float ss = 0.0f;
+    for (int i = 0; i < n; i++) ss += x[i] * x[i];
+    ss = 1.0f / sqrtf(ss / n + eps);
+    for (int i = 0; i < n; i++) o[i] = x[i] * ss * w[i];
+}

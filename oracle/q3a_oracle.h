@@ -89,6 +89,10 @@ void orc_attn_partial(float *o, float *lse, const float *q, const float *kc,
  * weights [d][n] row-major, one sequential fp32 sum per row. */
 void orc_mm_f16(float *o, const float *x, const uint16_t *w, int n, int d);
 
+/* rmsnorm (qwen3-8b/cpu/main.c:1168-1173): the layer input's RMSNorm, one
+ * sequential sum of squares. */
+void orc_rmsnorm(float *o, const float *x, const float *w, int n, float eps);
+
 #ifdef __cplusplus
 }
 #endif

@@ -53,6 +53,7 @@ def lib():
         L.orc_lse_merge.argtypes = [_P, _P, _P, _P, _I, _I, _I]
         L.orc_attn_partial.argtypes = [_P, _P, _P, _P, _P, _SZ, _I, _I, _I, _I, _I, _I]
         L.orc_mm_f16.argtypes = [_P, _P, _P, _I, _I]
+        L.orc_rmsnorm.argtypes = [_P, _P, _P, _I, _F]
         _lib = L
     return _lib
 
@@ -77,6 +78,7 @@ def ref():
         R.q3ref_launch_kv_write.argtypes = [_P, _P, _P, _P, _I]
         R.q3ref_attn_mc.argtypes = [_P, _P, _P, _P, _P, _SZ, _I, _I, _I, _I, _I, _I]
         R.q3ref_mm_f16.argtypes = [_P, _P, _P, _I, _I]
+        R.q3ref_rmsnorm.argtypes = [_P, _P, _P, _I, _F]
         _ref = R
     return _ref
 
@@ -162,6 +164,14 @@ def all_f16_patterns() -> np.ndarray:
     """Every fp16 bit pattern once, [64][1024] (zeros, subnormals, normals,
     +-inf, NaNs)."""
     return np.arange(65536, dtype=np.uint32).astype(np.uint16).view(np.float16).reshape(64, 1024)
+
+
+def rmsnorm(x: np.ndarray, w: np.ndarray, eps: float = 1e-6) -> np.ndarray:
+    """The layer input's RMSNorm (rmsnorm), a new array."""
+    x = np.ascontiguousarray(x, np.float32)
+    o = np.zeros_like(x)
+    lib().orc_rmsnorm(_ptr(o), _ptr(x), _ptr(np.ascontiguousarray(w, np.float32)), x.size, eps)
+    return o
 
 
 def lse_merge(o_parts: np.ndarray, lse_parts: np.ndarray, n_heads: int, hd: int):

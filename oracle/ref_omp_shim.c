@@ -60,3 +60,13 @@ void q3ref_attn_mc(float *xb, const float *q, const float *kc, const float *vc,
 void q3ref_mm_f16(float *o, const float *x, const uint16_t *w, int n, int d) {
     mm_f16(o, x, w, n, d);
 }
+
+/* rmsnorm, qwen3-8b/cpu-multicore/main.c:1171-1178, run on one OpenMP
+ * thread: its sum-of-squares reduction then adds in index order, the order
+ * of the single-core build (qwen3-8b/cpu/main.c:1168-1173). */
+void q3ref_rmsnorm(float *o, const float *x, const float *w, int n, float eps) {
+    int saved = omp_get_max_threads();
+    omp_set_num_threads(1);
+    rmsnorm(o, x, w, n, eps);
+    omp_set_num_threads(saved);
+}

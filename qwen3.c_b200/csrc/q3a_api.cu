@@ -129,12 +129,15 @@ struct q3a_ctx {
     float* qkv_part = nullptr;
     int* qkv_ticket = nullptr;
     size_t qkv_part_floats = 0;
+    float* sub_q = nullptr;               // q3a_attn_sublayer: prepared q and xb [n_heads*128]
+    float* sub_xb = nullptr;
     // peer-memory sequence shards (q3a_peer_export / q3a_peer_open)
     int peer_world = 0;
     int peer_rank = -1;
     float* peer_buf = nullptr;            // this rank's receive buffer
     float* peer_ptrs[PEER_MAX] = {};      // every rank's buffer, mapped here
     unsigned* peer_epoch = nullptr;       // call counter + finisher ticket
+    unsigned* wo_epoch = nullptr;         // wo exchange: per-CTA call numbers [WO_MAX_CTAS]
     bool peer_ipc = false;                // peer_ptrs are IPC mappings (closed on destroy)
     // registered caller buffer for column all-gathers (q3a_peer_register)
     uint8_t* reg_buf = nullptr;           // the caller's buffer
@@ -161,6 +164,14 @@ static inline void forget_last(q3a_ctx* c) {
     c->last_decode_layer = -1;
     c->last_qkv_layer = -1;
     c->last_qkv_pos = -1;
+}
+
+// Peer receive buffer: words per rank row of the sequence-shard region,
+// words of the whole buffer, and the offset of its wo region.
+static size_t peer_row(const q3a_ctx* c) { return (size_t)c->cfg.n_heads * HD + c->cfg.n_heads; }
+static size_t peer_wo_offset(const q3a_ctx* c, int world) { return (size_t)2 * world * peer_row(c); }
+static size_t peer_words(const q3a_ctx* c, int world) {
+    return peer_wo_offset(c, world) + (size_t)2 * world * WO_MAX_ROWS;
 }
 
 // Host-pointer staging of n tokens: inputs [q | k | v | q gains | k gains]
@@ -269,6 +280,9 @@ static void destroy_ctx(q3a_ctx* c) {
     cudaFree(c->pf_part);
     cudaFree(c->qkv_part);
     cudaFree(c->qkv_ticket);
+    cudaFree(c->sub_q);
+    cudaFree(c->sub_xb);
+    cudaFree(c->wo_epoch);
     cudaFree(c->err);
     cudaFree(c->d_inv_freq);
     cudaFree(c->d_stage);
@@ -743,50 +757,43 @@ extern "C" int q3a_attn_layer(q3a_ctx* c, float* xb, float* q, float* k, const f
 }
 
 // Validates and launches the projection kernel (qkv_kernel) of one token at
-// slot 0: q, k, v fp16 GEMVs fused with QK-RMSNorm, RoPE and the KV append.
-static int launch_proj(q3a_ctx* c, float* q, float* k, float* v, const float* x, const void* wq,
-                       const void* wk, const void* wv, int dim, const float* qw, const float* kw,
-                       int layer, int pos) {
+// slot 0: the q, k, v fp16 GEMVs of the held KV heads (with the layer's
+// input RMSNorm first when norm_w is given) fused with QK-RMSNorm, RoPE and
+// the KV append.
+static int launch_proj(q3a_ctx* c, float* q, float* k, float* v, const float* x, const float* norm_w,
+                       const void* wq, const void* wk, const void* wv, int dim, const float* qw,
+                       const float* kw, int layer, int pos) {
     if (!c || !q || !x || !wq || !wk || !wv || !qw || !kw)
         return fail(Q3A_ERR_INVALID, "null argument");
     if (c->cfg.ptr_mode != Q3A_PTR_DEVICE)
         return fail(Q3A_ERR_UNSUPPORTED, "the projection entry points take device pointers only");
-    if (c->nkv != c->cfg.n_kv_heads)
-        return fail(Q3A_ERR_INVALID, "the projection entry points need a context holding all KV heads");
-    if (dim <= 0 || dim % 8 != 0 || dim > 8192)
-        return fail(Q3A_ERR_UNSUPPORTED, "dim %d: multiples of 8 up to 8192 are implemented", dim);
+    if (dim <= 0 || dim % 8 != 0 || dim > WO_MAX_ROWS)
+        return fail(Q3A_ERR_UNSUPPORTED, "dim %d: multiples of 8 up to %d are implemented", dim,
+                    WO_MAX_ROWS);
     if (layer < 0 || layer >= c->cfg.n_layers) return fail(Q3A_ERR_INVALID, "layer %d", layer);
     if (pos < 0 || pos >= c->cfg.max_seq)
         return fail(Q3A_ERR_INVALID, "pos %d outside [0, %d)", pos, c->cfg.max_seq);
-    const uintptr_t align = (uintptr_t)x | (uintptr_t)wq | (uintptr_t)wk | (uintptr_t)wv |
-                            (uintptr_t)q | (uintptr_t)k | (uintptr_t)v | (uintptr_t)qw |
-                            (uintptr_t)kw;
+    const uintptr_t align = (uintptr_t)x | (uintptr_t)norm_w | (uintptr_t)wq | (uintptr_t)wk |
+                            (uintptr_t)wv | (uintptr_t)q | (uintptr_t)k | (uintptr_t)v |
+                            (uintptr_t)qw | (uintptr_t)kw;
     if (align & 15) return fail(Q3A_ERR_INVALID, "the vectors and weights must be 16-byte aligned");
     int rc = ensure_device(c);
     if (rc) return rc;
-    const int nq = c->cfg.n_heads, nkv = c->cfg.n_kv_heads;
+    const int nkv = c->nkv, nq = nkv * GQA;
+    const int heads_all = c->cfg.n_heads + 2 * c->cfg.n_kv_heads;
     const int rows_total = (nq + 2 * nkv) * HD;
-    const size_t part_floats = (size_t)rows_total;
-    if (part_floats > c->qkv_part_floats) {
-        if (c->qkv_part) {
-            cudaStreamSynchronize(c->stream);
-            cudaFree(c->qkv_part);
-            c->qkv_part = nullptr;
-            c->qkv_part_floats = 0;
-        }
-        if (!c->qkv_ticket) {
-            if (cudaMalloc(&c->qkv_ticket, (size_t)(nq + 2 * nkv) * sizeof(int)) != cudaSuccess)
-                return fail(Q3A_ERR_OOM, "projection tickets");
-            CUDA_TRY(cudaMemsetAsync(c->qkv_ticket, 0, (size_t)(nq + 2 * nkv) * sizeof(int), c->stream));
-        }
-        if (cudaMalloc(&c->qkv_part, part_floats * 4) != cudaSuccess)
-            return fail(Q3A_ERR_OOM, "projection partials of %zu bytes", part_floats * 4);
-        c->qkv_part_floats = part_floats;
+    if (!c->qkv_part) {
+        if (cudaMalloc(&c->qkv_ticket, (size_t)heads_all * sizeof(int)) != cudaSuccess ||
+            cudaMalloc(&c->qkv_part, (size_t)heads_all * HD * sizeof(float)) != cudaSuccess)
+            return fail(Q3A_ERR_OOM, "projection scratch");
+        CUDA_TRY(cudaMemsetAsync(c->qkv_ticket, 0, (size_t)heads_all * sizeof(int), c->stream));
+        c->qkv_part_floats = (size_t)heads_all * HD;
         forget_last(c);  // the memset above is a launch on the stream
     }
     QkvParams qp;
     memset(&qp, 0, sizeof(qp));
     qp.x = x;
+    qp.norm_w = norm_w;
     qp.wq = reinterpret_cast<const __half*>(wq);
     qp.wk = reinterpret_cast<const __half*>(wk);
     qp.wv = reinterpret_cast<const __half*>(wv);
@@ -803,9 +810,10 @@ static int launch_proj(q3a_ctx* c, float* q, float* k, float* v, const float* x,
     qp.inv_freq = c->d_inv_freq;
     qp.eps = c->cfg.norm_eps;
     qp.dim = dim;
-    qp.rows_total = rows_total;
     qp.nq = nq;
     qp.nkv = nkv;
+    qp.kv0 = c->kv0;
+    qp.rows_total = rows_total;
     qp.layer = layer;
     qp.pos = pos;
     qp.slot = 0;
@@ -828,18 +836,12 @@ extern "C" int q3a_qkv_proj(q3a_ctx* c, float* q, float* k, float* v, const floa
                             const void* wq, const void* wk, const void* wv, int dim,
                             const float* qw, const float* kw, int layer, int pos) {
     g_err[0] = 0;
-    return launch_proj(c, q, k, v, x, wq, wk, wv, dim, qw, kw, layer, pos);
+    return launch_proj(c, q, k, v, x, nullptr, wq, wk, wv, dim, qw, kw, layer, pos);
 }
 
-// The projections (launch_proj), then the decode of the layer over rows
-// [0, pos] with the prepared q.  Device pointers only.
-extern "C" int q3a_attn_layer_proj(q3a_ctx* c, float* xb, float* q, float* k, float* v,
-                                   const float* x, const void* wq, const void* wk, const void* wv,
-                                   int dim, const float* qw, const float* kw, int layer, int pos) {
-    g_err[0] = 0;
-    if (!xb) return fail(Q3A_ERR_INVALID, "null argument");
-    int rc = launch_proj(c, q, k, v, x, wq, wk, wv, dim, qw, kw, layer, pos);
-    if (rc) return rc;
+// The decode of the held heads over rows [0, pos] of slot 0 with the
+// prepared q (after launch_proj).
+static int decode_after_proj(q3a_ctx* c, float* xb, const float* q, int layer, int pos) {
     DecodeParams p;
     base_params(c, p, layer);
     p.nb = 1;
@@ -850,6 +852,88 @@ extern "C" int q3a_attn_layer_proj(q3a_ctx* c, float* xb, float* q, float* k, fl
     p.q = q;
     p.xb = xb;
     return run_decode(c, p, c->tmK, c->tmV, c->bf16);
+}
+
+// The projections (launch_proj), then the decode of the layer over rows
+// [0, pos] with the prepared q.  Device pointers only.
+extern "C" int q3a_attn_layer_proj(q3a_ctx* c, float* xb, float* q, float* k, float* v,
+                                   const float* x, const void* wq, const void* wk, const void* wv,
+                                   int dim, const float* qw, const float* kw, int layer, int pos) {
+    g_err[0] = 0;
+    if (!xb) return fail(Q3A_ERR_INVALID, "null argument");
+    int rc = launch_proj(c, q, k, v, x, nullptr, wq, wk, wv, dim, qw, kw, layer, pos);
+    if (rc) return rc;
+    return decode_after_proj(c, xb, q, layer, pos);
+}
+
+// x += wo[:, held columns] . xb[held columns], summed over the peer set when
+// one is open with more than one rank.
+static int launch_wo_residual(q3a_ctx* c, float* x, const float* xb, const void* wo, int dim) {
+    if (!c || !x || !xb || !wo) return fail(Q3A_ERR_INVALID, "null argument");
+    if (c->cfg.ptr_mode != Q3A_PTR_DEVICE)
+        return fail(Q3A_ERR_UNSUPPORTED, "the projection entry points take device pointers only");
+    if (dim <= 0 || dim > WO_MAX_ROWS)
+        return fail(Q3A_ERR_UNSUPPORTED, "dim %d: up to %d rows are implemented", dim, WO_MAX_ROWS);
+    if (((uintptr_t)x | (uintptr_t)xb | (uintptr_t)wo) & 15)
+        return fail(Q3A_ERR_INVALID, "x, xb and wo must be 16-byte aligned");
+    const bool peers = c->peer_rank >= 0 && c->peer_world > 1;
+    if (c->nkv != c->cfg.n_kv_heads && !peers)
+        return fail(Q3A_ERR_INVALID,
+                    "a context holding some KV heads sums the ranks' wo partials over its peer set "
+                    "(q3a_peer_export / q3a_peer_open first)");
+    int rc = ensure_device(c);
+    if (rc) return rc;
+    WoParams wp;
+    memset(&wp, 0, sizeof(wp));
+    wp.w = reinterpret_cast<const __half*>(wo);
+    wp.ld = c->cfg.n_heads * HD;
+    wp.col0 = c->kv0 * GQA * HD;
+    wp.ncols = c->nkv * GQA * HD;
+    wp.xb = xb;
+    wp.x = x;
+    wp.rows = dim;
+    wp.world = peers ? c->peer_world : 1;
+    wp.rank = peers ? c->peer_rank : 0;
+    if (peers) {
+        const size_t off = peer_wo_offset(c, c->peer_world);
+        for (int r = 0; r < c->peer_world; r++)
+            wp.recv[r] = reinterpret_cast<unsigned long long*>(c->peer_ptrs[r]) + off;
+        wp.epoch = c->wo_epoch;
+    }
+    wp.wait_limit = c->wait_limit;
+    wp.err = c->err;
+    // one CTA per SM; every rank uses the same count (its CTA c exchanges
+    // with CTA c of the others)
+    const int n_ctas = std::min(std::min(dim, c->num_sms), WO_MAX_CTAS);
+    CUDA_TRY(launch_wo(wp, n_ctas, c->stream));
+    c->launches++;
+    forget_last(c);
+    return Q3A_OK;
+}
+
+extern "C" int q3a_wo_residual(q3a_ctx* c, float* x, const float* xb, const void* wo, int dim) {
+    g_err[0] = 0;
+    return launch_wo_residual(c, x, xb, wo, dim);
+}
+
+extern "C" int q3a_attn_sublayer(q3a_ctx* c, float* x, const float* att_norm_w, const void* wq,
+                                 const void* wk, const void* wv, const float* q_norm_w,
+                                 const float* k_norm_w, const void* wo, int dim, int layer, int pos) {
+    g_err[0] = 0;
+    if (!c || !x || !att_norm_w) return fail(Q3A_ERR_INVALID, "null argument");
+    int rc = ensure_device(c);
+    if (rc) return rc;
+    if (!c->sub_q) {
+        const size_t n = (size_t)c->cfg.n_heads * HD;
+        if (cudaMalloc(&c->sub_q, n * 4) != cudaSuccess || cudaMalloc(&c->sub_xb, n * 4) != cudaSuccess)
+            return fail(Q3A_ERR_OOM, "sublayer scratch");
+    }
+    rc = launch_proj(c, c->sub_q, nullptr, nullptr, x, att_norm_w, wq, wk, wv, dim, q_norm_w,
+                     k_norm_w, layer, pos);
+    if (rc) return rc;
+    rc = decode_after_proj(c, c->sub_xb, c->sub_q, layer, pos);
+    if (rc) return rc;
+    return launch_wo_residual(c, x, c->sub_xb, wo, dim);
 }
 
 extern "C" int q3a_attn_layer_batched(q3a_ctx* c, float* xb, float* q, float* k, const float* v,
@@ -1041,27 +1125,29 @@ extern "C" int q3a_lse_combine(q3a_ctx* c, float* xb, const float* o_parts, cons
 }
 
 // ------------------------------------------------ peer-memory sequence shards
-static size_t peer_row(const q3a_ctx* c) { return (size_t)c->cfg.n_heads * HD + c->cfg.n_heads; }
 
 extern "C" int q3a_peer_export(q3a_ctx* c, int world, void* handle) {
     g_err[0] = 0;
     if (!c || !handle) return fail(Q3A_ERR_INVALID, "null argument");
     if (world < 1 || world > PEER_MAX) return fail(Q3A_ERR_INVALID, "world %d outside [1, %d]", world, PEER_MAX);
-    if (c->nkv != c->cfg.n_kv_heads || c->cfg.n_kv_heads > PEER_MAXG)
-        return fail(Q3A_ERR_INVALID, "peer shards need a context holding all (<= %d) KV heads", PEER_MAXG);
+    if (c->cfg.n_kv_heads > PEER_MAXG)
+        return fail(Q3A_ERR_INVALID, "peer shards support at most %d KV heads", PEER_MAXG);
     if (c->cfg.ptr_mode != Q3A_PTR_DEVICE) return fail(Q3A_ERR_UNSUPPORTED, "peer shards run in device-pointer mode");
     if (c->peer_world && c->peer_world != world)
         return fail(Q3A_ERR_INVALID, "already exported for %d ranks", c->peer_world);
     int rc = ensure_device(c);
     if (rc) return rc;
     if (!c->peer_buf) {
-        // [2 parities][world][row] words of 8 bytes (value, call number)
-        const size_t bytes = (size_t)2 * world * peer_row(c) * 8;
+        // words of 8 bytes (value, call number): the sequence-shard region
+        // [2 parities][world][row], then the wo region [2][world][WO_MAX_ROWS]
+        const size_t bytes = peer_words(c, world) * 8;
         if (cudaMalloc(&c->peer_buf, bytes) != cudaSuccess) return fail(Q3A_ERR_OOM, "peer buffer of %zu bytes", bytes);
-        if (cudaMalloc(&c->peer_epoch, PEER_MAXG * sizeof(unsigned)) != cudaSuccess)
+        if (cudaMalloc(&c->peer_epoch, PEER_MAXG * sizeof(unsigned)) != cudaSuccess ||
+            cudaMalloc(&c->wo_epoch, WO_MAX_CTAS * sizeof(unsigned)) != cudaSuccess)
             return fail(Q3A_ERR_OOM, "peer counters");
         CUDA_TRY(cudaMemset(c->peer_buf, 0, bytes));
         CUDA_TRY(cudaMemset(c->peer_epoch, 0, PEER_MAXG * sizeof(unsigned)));
+        CUDA_TRY(cudaMemset(c->wo_epoch, 0, WO_MAX_CTAS * sizeof(unsigned)));
         CUDA_TRY(cudaDeviceSynchronize());
         c->peer_world = world;
     }
@@ -1278,6 +1364,8 @@ extern "C" int q3a_attn_seqshard(q3a_ctx* c, float* xb, const float* q, int seq,
     g_err[0] = 0;
     if (!c || !xb || !q) return fail(Q3A_ERR_INVALID, "null argument");
     if (c->peer_rank < 0) return fail(Q3A_ERR_INVALID, "q3a_peer_open must come first");
+    if (c->nkv != c->cfg.n_kv_heads)
+        return fail(Q3A_ERR_INVALID, "sequence shards need a context holding all KV heads");
     if (seq < 0 || seq >= c->cfg.n_seqs) return fail(Q3A_ERR_INVALID, "seq %d", seq);
     if (layer < 0 || layer >= c->cfg.n_layers) return fail(Q3A_ERR_INVALID, "layer %d", layer);
     if (n_local < 1 || n_local > c->cfg.max_seq)

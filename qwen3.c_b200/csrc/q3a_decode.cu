@@ -450,35 +450,6 @@ __device__ __forceinline__ void process_rows(const KV* Kt, const KV* Vt, int lo,
     __syncwarp();
 }
 
-// ---- peer-memory exchange words: each 8-byte word carries a 32-bit value
-// and the call number it belongs to, stored and loaded as one naturally
-// aligned 64-bit access, so a reader that sees the call number also sees the
-// value -- no flag and no fence are needed on either side.
-__device__ __forceinline__ void st_word_sys(unsigned long long* p, float v, unsigned ep) {
-    const unsigned long long w = ((unsigned long long)ep << 32) | __float_as_uint(v);
-    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
-}
-__device__ __forceinline__ unsigned long long ld_word_sys(const unsigned long long* p) {
-    unsigned long long w;
-    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
-    return w;
-}
-// Bounded wait (`limit` SM clocks) for the word of call `ep`; false on
-// timeout.
-__device__ __forceinline__ bool wait_word(const unsigned long long* p, unsigned ep, float& v,
-                                          long long limit) {
-    unsigned long long w = ld_word_sys(p);
-    if ((unsigned)(w >> 32) != ep) {
-        const long long t0 = clock64();
-        do {
-            if (clock64() - t0 > limit) return false;
-            w = ld_word_sys(p);
-        } while ((unsigned)(w >> 32) != ep);
-    }
-    v = __uint_as_float((unsigned)w);
-    return true;
-}
-
 // Same word format inside one GPU (the spread merge of split-KV ranges).
 __device__ __forceinline__ void st_word_gpu(unsigned long long* p, float v, unsigned tag) {
     const unsigned long long w = ((unsigned long long)tag << 32) | __float_as_uint(v);

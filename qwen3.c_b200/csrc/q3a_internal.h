@@ -145,18 +145,20 @@ struct AppendParams {
     const float* inv_freq;   // [64] device table
 };
 
-// The q/k/v projections of one token with fp16 weights, fused with the
-// QK-RMSNorm, RoPE and KV append of the block (qkv_kernel).
+// The q/k/v projections of one token with fp16 weights for the KV heads a
+// context holds, fused with the layer's input RMSNorm (optional) and the
+// block's QK-RMSNorm, RoPE and KV append (qkv_kernel, q3a_proj.cu).
 struct QkvParams {
-    const float* x;          // [dim] input (the normed layer input)
-    const __half* wq;        // [nq*128][dim] row-major
-    const __half* wk;        // [nkv*128][dim]
-    const __half* wv;        // [nkv*128][dim]
+    const float* x;          // [dim] input: the layer input (normed in-kernel when norm_w)
+    const float* norm_w;     // [dim] input RMSNorm gains, or null (x already normed)
+    const __half* wq;        // [n_heads*128][dim] row-major (all heads)
+    const __half* wk;        // [n_kv*128][dim]
+    const __half* wv;        // [n_kv*128][dim]
     const float* q_norm_w;   // [128]
     const float* k_norm_w;
-    float* q_out;            // [nq*128] normalised, rotated q
-    float* k_out;            // [nkv*128] normalised, rotated k, may be null
-    float* v_out;            // [nkv*128] v, may be null
+    float* q_out;            // [n_heads*128] normalised, rotated q (held heads written)
+    float* k_out;            // [n_kv*128] normalised, rotated k, may be null
+    float* v_out;            // [n_kv*128] v, may be null
     void* kcache;            // the context's paged caches (append at pos)
     void* vcache;
     float* part;             // scratch [rows_total]: the row sums
@@ -165,12 +167,34 @@ struct QkvParams {
     const float* inv_freq;   // [64] RoPE inverse frequencies
     float eps;
     int dim;                 // columns (multiple of 8, at most 8192)
-    int nq, nkv;
+    int nq, nkv;             // held q heads (nkv * 4) and KV heads
+    int kv0;                 // global index of the first held KV head
     int rows_total;          // (nq + 2 nkv) * 128
     int layer, pos, slot, pages_per_seq, page_tokens, n_pages;
 };
 // n_ctas >= nq + 2 nkv (a CTA's rows then touch at most two heads)
 cudaError_t launch_qkv(const QkvParams& p, bool bf16, int n_ctas, cudaStream_t st);
+
+// Rows per rank in the wo exchange region of the peer buffer (the largest
+// model width supported).
+constexpr int WO_MAX_ROWS = 8192;
+constexpr int WO_MAX_CTAS = 256;
+
+// x += wo[:, col0:col0+ncols] . xb[col0:col0+ncols] (wo_kernel, q3a_proj.cu);
+// with world > 1 the ranks' partial sums are exchanged and added in rank order.
+struct WoParams {
+    const __half* w;         // wo [rows][ld] row-major
+    int ld, col0, ncols;     // this context's columns (its held heads' xb slice)
+    const float* xb;         // [ld] (columns col0.. valid)
+    float* x;                // [rows] residual stream, updated in place
+    int rows;
+    int world, rank;
+    unsigned long long* recv[PEER_MAX];  // every rank's wo exchange region, as mapped here
+    unsigned* epoch;         // [WO_MAX_CTAS] per-CTA call numbers of this rank
+    long long wait_limit;
+    int* err;
+};
+cudaError_t launch_wo(const WoParams& p, int n_ctas, cudaStream_t st);
 
 // Raises the dynamic shared-memory limit of kernel `fn` to `bytes` on the
 // current device.  The attribute is per device, so it is set once per

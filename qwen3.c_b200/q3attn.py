@@ -26,6 +26,7 @@ EXPORTS = [
     "q3a_cfg_default", "q3a_create", "q3a_destroy", "q3a_last_error", "q3a_set_stream",
     "q3a_sync", "q3a_check_device_error", "q3a_attn_layer", "q3a_attn_decode",
     "q3a_attn_layer_batched", "q3a_attn_layer_proj", "q3a_qkv_proj",
+    "q3a_wo_residual", "q3a_attn_sublayer",
     "q3a_kv_append", "q3a_kv_load", "q3a_kv_read", "q3a_prefill",
     "q3a_prefill_attn", "q3a_attn_partial", "q3a_lse_combine", "q3a_lse_combine_packed",
     "q3a_peer_export", "q3a_peer_open", "q3a_attn_seqshard",
@@ -80,6 +81,8 @@ def load():
         L.q3a_attn_layer_batched.argtypes = [_P, _P, _P, _P, _P, _P, _P, _I, _P, _P, _I]
         L.q3a_attn_layer_proj.argtypes = [_P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _P, _P, _I, _I]
         L.q3a_qkv_proj.argtypes = [_P, _P, _P, _P, _P, _P, _P, _P, _I, _P, _P, _I, _I]
+        L.q3a_wo_residual.argtypes = [_P, _P, _P, _P, _I]
+        L.q3a_attn_sublayer.argtypes = [_P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I]
         L.q3a_kv_append.argtypes = [_P, _I, _I, _I, _I, _P, _P, _P]
         L.q3a_kv_load.argtypes = [_P, _I, _I, _I, _I, _P, _P]
         L.q3a_kv_read.argtypes = [_P, _I, _I, _I, _I, _P, _P]
@@ -204,6 +207,16 @@ class Context:
         """The projection half of attn_layer_proj (no attention)."""
         check(self.lib.q3a_qkv_proj(self.h, ptr(q), ptr(k), ptr(v), ptr(x), ptr(wq), ptr(wk),
                                     ptr(wv), int(x.numel()), ptr(qw), ptr(kw), layer, pos))
+
+    def wo_residual(self, x, xb, wo):
+        """x += wo . xb (the held heads' columns; summed over the peer set)."""
+        check(self.lib.q3a_wo_residual(self.h, ptr(x), ptr(xb), ptr(wo), int(x.numel())))
+
+    def attn_sublayer(self, x, att_norm_w, wq, wk, wv, qw, kw, wo, layer, pos):
+        """x += attention sublayer of one token at pos (device tensors)."""
+        check(self.lib.q3a_attn_sublayer(self.h, ptr(x), ptr(att_norm_w), ptr(wq), ptr(wk),
+                                         ptr(wv), ptr(qw), ptr(kw), ptr(wo), int(x.numel()),
+                                         layer, pos))
 
     def attn_layer_batched(self, xb, q, k, v, qw, kw, layer, seq_ids, pos):
         import numpy as np

@@ -63,6 +63,21 @@ def _all_gather(dist, out, inp, group):
         dist.all_gather(list(out.unbind(0)), inp, group=group)
 
 
+def open_peer_set(ctx, *, world: int, rank: int, group=None) -> None:
+    """Exports this rank's peer buffer and maps every rank's
+    (``q3a_peer_export`` / ``q3a_peer_open``; the IPC handles travel through
+    one ``all_gather_object``).  Sequence shards exchange their (o, lse)
+    words in it; KV-head shards their partial wo products
+    (``q3a_wo_residual`` / ``q3a_attn_sublayer``)."""
+    import torch.distributed as dist
+    handle = ctx.peer_export(world)
+    handles = [handle]
+    if world > 1:
+        handles = [None] * world
+        dist.all_gather_object(handles, handle, group=group)
+    ctx.peer_open(rank, world, handles)
+
+
 class SeqShardDecode:
     """One decode step of a sequence sharded over the ranks of ``group``.
 
@@ -83,12 +98,7 @@ class SeqShardDecode:
         self.mode = mode
         self.ctx = ctx
         if mode == "peer":
-            handle = ctx.peer_export(world)
-            handles = [handle]
-            if world > 1:
-                handles = [None] * world
-                dist.all_gather_object(handles, handle, group=group)
-            ctx.peer_open(rank, world, handles)
+            open_peer_set(ctx, world=world, rank=rank, group=group)
         self.nq = n_heads * hd
         self.width = packed_width(n_heads, hd)
         self.send = torch.zeros(self.width, dtype=torch.float32, device=device)

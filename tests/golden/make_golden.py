@@ -209,11 +209,21 @@ def proj_golden(meta):
     R.q3ref_mm_f16(_p(conv), _p(np.ones(1, np.float32)),
                    _p(np.ascontiguousarray(w.reshape(65536, 1)).view(np.uint16)), 1, 65536)
     arrays["patterns_value"] = conv
+    # the layer input's RMSNorm (rmsnorm, run on one OpenMP thread)
+    seed = SEED + 2100
+    x = (orc.randn(4096, seed, 202) * 3.0).astype(np.float32)
+    w = (1.0 + 0.25 * orc.randn(4096, seed, 203)).astype(np.float32)
+    o = np.zeros(4096, np.float32)
+    R.q3ref_rmsnorm(_p(o), _p(x), _p(w), 4096, EPS)
+    arrays["rmsnorm_seed"] = np.int64(seed)
+    arrays["rmsnorm_out"] = o
     np.savez(os.path.join(HERE, "projection.npz"), **arrays)
     meta["files"]["projection.npz"] = {
         "what": "mm_f16 (qwen3-8b/cpu-multicore/main.c:1213-1221) run by the reference: "
                 "seeded weights (orc_randn * scale rounded to fp16) and x = orc_randn, and "
-                "every fp16 bit pattern (row sums against x = 1; each value alone)",
+                "every fp16 bit pattern (row sums against x = 1; each value alone); rmsnorm "
+                "(cpu-multicore/main.c:1171-1178 on one OpenMP thread) of x = 3 orc_randn "
+                "(stream 202) with gains 1 + 0.25 orc_randn (stream 203)",
         "cases": cases}
 
 

@@ -193,3 +193,14 @@ def test_mm_f16_matches_reference():
     fin = ~np.isnan(ref)
     assert np.array_equal(conv[fin], ref[fin])
     assert np.isnan(conv[~fin]).all()
+
+
+def test_rmsnorm_matches_reference():
+    """The layer input's RMSNorm bit for bit against the reference's rmsnorm
+    (run on one thread: the single-core build's summation order)."""
+    g = _load("projection.npz")
+    seed = int(g["rmsnorm_seed"])
+    x = (orc.randn(4096, seed, 202) * 3.0).astype(np.float32)
+    w = (1.0 + 0.25 * orc.randn(4096, seed, 203)).astype(np.float32)
+    o = orc.rmsnorm(x, w, EPS)
+    assert np.array_equal(o.view(np.uint32), g["rmsnorm_out"].view(np.uint32))

@@ -245,3 +245,26 @@ def test_peer_head_gather(tmp_path, world):
     for rank in range(world):
         bad = int(open(os.path.join(tmp_path, f"rank{rank}.txt")).read())
         assert bad == 0, f"rank {rank}: {bad} slices differ"
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_sublayer_over_kv_head_shards(tmp_path, world):
+    """The attention sublayer over `world` GPUs holding 8/world KV heads each
+    (torchrun, one process per GPU): column-parallel projections and
+    attention, row-parallel wo whose partial sums the ranks exchange over
+    NVLink inside the kernel.  Every rank's increments match the oracle and
+    every rank's x equals rank 0's bit for bit."""
+    import subprocess
+    import torch
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", SHARD_TEST_OUT=str(tmp_path))
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node",
+           str(world), "--master-addr", "127.0.0.1", "--master-port", str(_free_port()),
+           os.path.join(ROOT, "tests", "tp_sublayer_worker.py")]
+    r = subprocess.run(cmd, env=env, timeout=300, capture_output=True, text=True)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
+    for rank in range(world):
+        err, same = open(os.path.join(tmp_path, f"rank{rank}.txt")).read().split()
+        assert float(err) <= 3e-2, f"rank {rank}: normwise {err}"
+        assert same == "1", f"rank {rank}: x differs from rank 0's"
