@@ -782,6 +782,9 @@ def ncu_case(args):
 
 
 # ------------------------------------------------------------------ main
+_LINE_OUT = None  # the stream of the one JSON line (the saved stdout at N > 1)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -796,6 +799,12 @@ def main():
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     world, rank, local = dist_setup()
+    global _LINE_OUT
+    if world > 1:
+        # libraries (NCCL) may print to stdout; everything but the JSON line
+        # goes to stderr, the line to the saved stdout
+        _LINE_OUT = os.fdopen(os.dup(1), "w")
+        os.dup2(2, 1)
     if args.ncu_case:
         ncu_case(args)
         return
@@ -993,7 +1002,7 @@ def main():
         line["cpu_baseline"] = {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")}
         line["cpu_baseline"]["us_per_layer"] = cpu["us_per_layer"]
     if rank == 0:
-        print(json.dumps(line), flush=True)
+        print(json.dumps(line), file=_LINE_OUT or sys.stdout, flush=True)
     if world > 1:
         import torch.distributed as dist
         dist.barrier()

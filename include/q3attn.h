@@ -243,6 +243,58 @@ int q3a_kv_append(q3a_ctx *ctx, int seq, int layer, int pos0, int n, const float
 int q3a_kv_load(q3a_ctx *ctx, int seq, int layer, int pos0, int n, const float *k,
                 const float *v);
 
+/* ---- KV-cache wire format: a sequence's cache rows as one self-checking
+ * blob, for handing a prompt's KV pages from a prefill GPU to a decode GPU
+ * (or to disk).  No counterpart in the reference, whose caches never leave
+ * the process.  Blob = this 64-byte header (little-endian) + payload: for
+ * each layer of [layer0, layer0 + n_layers), each KV head of
+ * [kv_head_begin, + kv_head_count), K then V, the rows of positions
+ * [pos0, pos0 + n_tok), head_dim values each, in the cache dtype (fp32, or
+ * bf16 as rounded on append), row-major.  checksum = sum over the payload's
+ * 64-bit words w_i of mix(w_i + i * 0x9E3779B97F4A7C15) mod 2^64, mix being
+ * the splitmix64 output function. */
+#define Q3A_KV_WIRE_MAGIC 0x564B3351u /* "Q3KV" */
+#define Q3A_KV_WIRE_VERSION 1
+typedef struct q3a_kv_wire_header {
+    uint32_t magic;
+    uint16_t version;
+    uint16_t dtype;          /* Q3A_KV_F32 / Q3A_KV_BF16 */
+    uint16_t head_dim;
+    uint16_t n_kv_heads;     /* the model's KV heads */
+    uint16_t kv_head_begin;  /* heads in this blob */
+    uint16_t kv_head_count;
+    uint16_t layer0;
+    uint16_t n_layers;
+    uint32_t pos0;
+    uint32_t n_tok;
+    uint32_t reserved0;
+    uint64_t payload_bytes;
+    uint64_t checksum;
+    uint8_t reserved[16];
+} q3a_kv_wire_header;
+
+/* Bytes of the blob q3a_kv_pack writes for n_layers layers and n_tok
+ * positions of the context's held KV heads (0 on bad arguments). */
+size_t q3a_kv_wire_bytes(const q3a_ctx *ctx, int n_layers, int n_tok);
+
+/* Packs rows [pos0, pos0 + n_tok) of layers [layer0, layer0 + n_layers) of
+ * slot `seq` (the context's held KV heads) into dst (dst_bytes >=
+ * q3a_kv_wire_bytes; host or device memory per the pointer mode). */
+int q3a_kv_pack(q3a_ctx *ctx, int seq, int layer0, int n_layers, int pos0, int n_tok, void *dst,
+                size_t dst_bytes);
+
+/* Unpacks a blob into slot `seq`: the header must match the context (dtype,
+ * head_dim, n_kv_heads; the blob's heads must include the context's; layers
+ * and positions inside the cache) and the payload's checksum must match;
+ * otherwise Q3A_ERR_INVALID and the cache is not touched.  The context's
+ * held heads are written at the blob's layers and positions. */
+int q3a_kv_unpack(q3a_ctx *ctx, int seq, const void *src, size_t src_bytes);
+
+/* Checks a blob in host memory without a GPU: header fields and the
+ * payload's checksum.  Q3A_OK, or Q3A_ERR_INVALID with the reason in
+ * q3a_last_error(). */
+int q3a_kv_wire_check(const void *blob, size_t bytes);
+
 /* Seeded synthetic cache rows, for harnesses and benchmarks that have no
  * model data: raw k and v rows [n][n_kv*hd] ~ N(0,1) from the generator of
  * q3a_randn (seed; streams stream_k, stream_v), stored at pos0.. exactly as

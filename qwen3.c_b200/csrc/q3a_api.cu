@@ -129,6 +129,7 @@ struct q3a_ctx {
     float* qkv_part = nullptr;
     int* qkv_ticket = nullptr;
     size_t qkv_part_floats = 0;
+    unsigned long long* wire_sum = nullptr;  // KV wire format: the payload checksum
     float* sub_q = nullptr;               // q3a_attn_sublayer: prepared q and xb [n_heads*128]
     float* sub_xb = nullptr;
     // peer-memory sequence shards (q3a_peer_export / q3a_peer_open)
@@ -280,6 +281,7 @@ static void destroy_ctx(q3a_ctx* c) {
     cudaFree(c->pf_part);
     cudaFree(c->qkv_part);
     cudaFree(c->qkv_ticket);
+    cudaFree(c->wire_sum);
     cudaFree(c->sub_q);
     cudaFree(c->sub_xb);
     cudaFree(c->wo_epoch);
@@ -1480,6 +1482,189 @@ extern "C" int q3a_kv_append(q3a_ctx* c, int seq, int layer, int pos0, int n, co
 extern "C" int q3a_kv_load(q3a_ctx* c, int seq, int layer, int pos0, int n, const float* k,
                            const float* v) {
     return append_common(c, seq, layer, pos0, n, k, v, nullptr, 0);
+}
+
+// ------------------------------------------------------------------ KV wire format
+static_assert(sizeof(q3a_kv_wire_header) == 64, "the wire header is 64 bytes");
+
+static size_t wire_payload_bytes(int n_layers, int n_heads, int n_tok, size_t esize) {
+    return (size_t)n_layers * n_heads * 2 * n_tok * HD * esize;
+}
+
+// Header fields that do not depend on a context; reason in `why` when bad.
+static bool wire_header_ok(const q3a_kv_wire_header& h, size_t bytes, char* why, size_t why_n) {
+    if (h.magic != Q3A_KV_WIRE_MAGIC) return snprintf(why, why_n, "not a KV wire blob (magic %08x)", h.magic), false;
+    if (h.version != Q3A_KV_WIRE_VERSION) return snprintf(why, why_n, "wire version %u", h.version), false;
+    if (h.dtype != Q3A_KV_F32 && h.dtype != Q3A_KV_BF16) return snprintf(why, why_n, "dtype %u", h.dtype), false;
+    if (h.head_dim != HD) return snprintf(why, why_n, "head_dim %u", h.head_dim), false;
+    if (h.kv_head_count == 0 || h.kv_head_begin + h.kv_head_count > h.n_kv_heads)
+        return snprintf(why, why_n, "heads [%u, +%u) of %u", h.kv_head_begin, h.kv_head_count, h.n_kv_heads), false;
+    if (h.n_layers == 0 || h.n_tok == 0) return snprintf(why, why_n, "empty blob"), false;
+    const size_t want = wire_payload_bytes(h.n_layers, h.kv_head_count, (int)h.n_tok, h.dtype == Q3A_KV_BF16 ? 2 : 4);
+    if (h.payload_bytes != want) return snprintf(why, why_n, "payload of %llu bytes, the fields give %zu", (unsigned long long)h.payload_bytes, want), false;
+    if (bytes < sizeof(h) + want) return snprintf(why, why_n, "blob of %zu bytes, needs %zu", bytes, sizeof(h) + want), false;
+    return true;
+}
+
+extern "C" size_t q3a_kv_wire_bytes(const q3a_ctx* c, int n_layers, int n_tok) {
+    if (!c || n_layers <= 0 || n_tok <= 0) return 0;
+    return sizeof(q3a_kv_wire_header) + wire_payload_bytes(n_layers, c->nkv, n_tok, c->esize);
+}
+
+static int wire_sum_buffer(q3a_ctx* c) {
+    if (!c->wire_sum && cudaMalloc(&c->wire_sum, sizeof(unsigned long long)) != cudaSuccess)
+        return fail(Q3A_ERR_OOM, "checksum scratch");
+    return Q3A_OK;
+}
+
+static void wire_params(q3a_ctx* c, WireParams& w, int seq, int layer0, int n_layers, int pos0, int n_tok) {
+    memset(&w, 0, sizeof(w));
+    w.kcache = c->kcache;
+    w.vcache = c->vcache;
+    w.layer0 = layer0;
+    w.n_layers = n_layers;
+    w.nkv = c->nkv;
+    w.ctx_nkv = c->nkv;
+    w.pos0 = pos0;
+    w.n_tok = n_tok;
+    w.slot = seq;
+    w.pages_per_seq = c->pages_per_seq;
+    w.page_tokens = c->cfg.page_tokens;
+    w.n_pages = c->n_pages;
+}
+
+extern "C" int q3a_kv_pack(q3a_ctx* c, int seq, int layer0, int n_layers, int pos0, int n_tok,
+                           void* dst, size_t dst_bytes) {
+    g_err[0] = 0;
+    if (!c || !dst) return fail(Q3A_ERR_INVALID, "null argument");
+    if (seq < 0 || seq >= c->cfg.n_seqs) return fail(Q3A_ERR_INVALID, "seq %d", seq);
+    if (layer0 < 0 || n_layers < 1 || layer0 + n_layers > c->cfg.n_layers)
+        return fail(Q3A_ERR_INVALID, "layers [%d, +%d) of %d", layer0, n_layers, c->cfg.n_layers);
+    if (pos0 < 0 || n_tok < 1 || pos0 + n_tok > c->cfg.max_seq)
+        return fail(Q3A_ERR_INVALID, "positions [%d, +%d) of %d", pos0, n_tok, c->cfg.max_seq);
+    const size_t need = q3a_kv_wire_bytes(c, n_layers, n_tok);
+    if (dst_bytes < need) return fail(Q3A_ERR_INVALID, "dst of %zu bytes, needs %zu", dst_bytes, need);
+    const bool dev = c->cfg.ptr_mode == Q3A_PTR_DEVICE;
+    if (dev && ((uintptr_t)dst & 15)) return fail(Q3A_ERR_INVALID, "dst must be 16-byte aligned");
+    int rc = ensure_device(c);
+    if (rc) return rc;
+    if ((rc = wire_sum_buffer(c))) return rc;
+    const size_t pay = need - sizeof(q3a_kv_wire_header);
+    uint8_t* payload;
+    if (dev) {
+        payload = reinterpret_cast<uint8_t*>(dst) + sizeof(q3a_kv_wire_header);
+    } else {
+        if ((rc = grow_scratch(c, pay))) return rc;
+        payload = reinterpret_cast<uint8_t*>(c->d_scratch);
+    }
+    WireParams w;
+    wire_params(c, w, seq, layer0, n_layers, pos0, n_tok);
+    w.payload = payload;
+    w.pay_nkv = c->nkv;
+    CUDA_TRY(launch_wire_copy(w, c->bf16 != 0, true, c->stream));
+    CUDA_TRY(launch_wire_checksum(payload, pay, c->wire_sum, c->stream));
+    c->launches += 2;
+    forget_last(c);
+    q3a_kv_wire_header h;
+    memset(&h, 0, sizeof(h));
+    h.magic = Q3A_KV_WIRE_MAGIC;
+    h.version = Q3A_KV_WIRE_VERSION;
+    h.dtype = (uint16_t)(c->bf16 ? Q3A_KV_BF16 : Q3A_KV_F32);
+    h.head_dim = HD;
+    h.n_kv_heads = (uint16_t)c->cfg.n_kv_heads;
+    h.kv_head_begin = (uint16_t)c->kv0;
+    h.kv_head_count = (uint16_t)c->nkv;
+    h.layer0 = (uint16_t)layer0;
+    h.n_layers = (uint16_t)n_layers;
+    h.pos0 = (uint32_t)pos0;
+    h.n_tok = (uint32_t)n_tok;
+    h.payload_bytes = pay;
+    unsigned long long sum = 0;
+    CUDA_TRY(cudaMemcpyAsync(&sum, c->wire_sum, sizeof(sum), cudaMemcpyDeviceToHost, c->stream));
+    if (!dev)
+        CUDA_TRY(cudaMemcpyAsync(reinterpret_cast<uint8_t*>(dst) + sizeof(h), payload, pay,
+                                 cudaMemcpyDeviceToHost, c->stream));
+    CUDA_TRY(cudaStreamSynchronize(c->stream));
+    h.checksum = sum;
+    if (dev)
+        CUDA_TRY(cudaMemcpy(dst, &h, sizeof(h), cudaMemcpyHostToDevice));
+    else
+        memcpy(dst, &h, sizeof(h));
+    return Q3A_OK;
+}
+
+extern "C" int q3a_kv_unpack(q3a_ctx* c, int seq, const void* src, size_t src_bytes) {
+    g_err[0] = 0;
+    if (!c || !src) return fail(Q3A_ERR_INVALID, "null argument");
+    if (seq < 0 || seq >= c->cfg.n_seqs) return fail(Q3A_ERR_INVALID, "seq %d", seq);
+    if (src_bytes < sizeof(q3a_kv_wire_header)) return fail(Q3A_ERR_INVALID, "blob of %zu bytes", src_bytes);
+    const bool dev = c->cfg.ptr_mode == Q3A_PTR_DEVICE;
+    if (dev && ((uintptr_t)src & 15)) return fail(Q3A_ERR_INVALID, "src must be 16-byte aligned");
+    int rc = ensure_device(c);
+    if (rc) return rc;
+    q3a_kv_wire_header h;
+    if (dev) {
+        CUDA_TRY(cudaMemcpyAsync(&h, src, sizeof(h), cudaMemcpyDeviceToHost, c->stream));
+        CUDA_TRY(cudaStreamSynchronize(c->stream));
+    } else {
+        memcpy(&h, src, sizeof(h));
+    }
+    char why[160];
+    if (!wire_header_ok(h, src_bytes, why, sizeof(why))) return fail(Q3A_ERR_INVALID, "%s", why);
+    if (h.dtype != (c->bf16 ? Q3A_KV_BF16 : Q3A_KV_F32))
+        return fail(Q3A_ERR_INVALID, "blob dtype %u, context dtype %d", h.dtype, c->cfg.kv_dtype);
+    if (h.n_kv_heads != c->cfg.n_kv_heads)
+        return fail(Q3A_ERR_INVALID, "blob of a model with %u KV heads", h.n_kv_heads);
+    if (c->kv0 < h.kv_head_begin || c->kv0 + c->nkv > h.kv_head_begin + h.kv_head_count)
+        return fail(Q3A_ERR_INVALID, "blob holds KV heads [%u, +%u), the context [%d, +%d)",
+                    h.kv_head_begin, h.kv_head_count, c->kv0, c->nkv);
+    if (h.layer0 + h.n_layers > c->cfg.n_layers)
+        return fail(Q3A_ERR_INVALID, "blob layers [%u, +%u) of %d", h.layer0, h.n_layers, c->cfg.n_layers);
+    if ((long long)h.pos0 + h.n_tok > c->cfg.max_seq)
+        return fail(Q3A_ERR_INVALID, "blob positions [%u, +%u) beyond %d", h.pos0, h.n_tok, c->cfg.max_seq);
+    if ((rc = wire_sum_buffer(c))) return rc;
+    const size_t pay = h.payload_bytes;
+    const uint8_t* payload;
+    if (dev) {
+        payload = reinterpret_cast<const uint8_t*>(src) + sizeof(h);
+    } else {
+        if ((rc = grow_scratch(c, pay))) return rc;
+        CUDA_TRY(cudaMemcpyAsync(c->d_scratch, reinterpret_cast<const uint8_t*>(src) + sizeof(h), pay,
+                                 cudaMemcpyHostToDevice, c->stream));
+        payload = reinterpret_cast<const uint8_t*>(c->d_scratch);
+    }
+    CUDA_TRY(launch_wire_checksum(payload, pay, c->wire_sum, c->stream));
+    c->launches++;
+    forget_last(c);
+    unsigned long long sum = 0;
+    CUDA_TRY(cudaMemcpyAsync(&sum, c->wire_sum, sizeof(sum), cudaMemcpyDeviceToHost, c->stream));
+    CUDA_TRY(cudaStreamSynchronize(c->stream));
+    if (sum != h.checksum)
+        return fail(Q3A_ERR_INVALID, "checksum mismatch (blob %016llx, payload %016llx)",
+                    (unsigned long long)h.checksum, sum);
+    WireParams w;
+    wire_params(c, w, seq, h.layer0, h.n_layers, (int)h.pos0, (int)h.n_tok);
+    w.payload = const_cast<uint8_t*>(payload);
+    w.pay_nkv = h.kv_head_count;
+    w.pay_head0 = c->kv0 - h.kv_head_begin;
+    CUDA_TRY(launch_wire_copy(w, c->bf16 != 0, false, c->stream));
+    c->launches++;
+    if (!dev) CUDA_TRY(cudaStreamSynchronize(c->stream));  // the scratch is reused by later calls
+    return Q3A_OK;
+}
+
+extern "C" int q3a_kv_wire_check(const void* blob, size_t bytes) {
+    g_err[0] = 0;
+    if (!blob || bytes < sizeof(q3a_kv_wire_header)) return fail(Q3A_ERR_INVALID, "blob of %zu bytes", bytes);
+    q3a_kv_wire_header h;
+    memcpy(&h, blob, sizeof(h));
+    char why[160];
+    if (!wire_header_ok(h, bytes, why, sizeof(why))) return fail(Q3A_ERR_INVALID, "%s", why);
+    const uint64_t sum = wire_checksum_host(reinterpret_cast<const uint8_t*>(blob) + sizeof(h), h.payload_bytes);
+    if (sum != h.checksum)
+        return fail(Q3A_ERR_INVALID, "checksum mismatch (blob %016llx, payload %016llx)",
+                    (unsigned long long)h.checksum, (unsigned long long)sum);
+    return Q3A_OK;
 }
 
 extern "C" int q3a_kv_synth(q3a_ctx* c, int seq, int layer, int pos0, int n, uint64_t seed,

@@ -261,6 +261,25 @@ constexpr int PF_PART_FLOATS = 128 * 128 + 128;  // o [128 rows][128] + lse [128
 cudaError_t launch_prefill(const PrefillParams& p, const CUtensorMap& tmQ, cudaStream_t st);
 int prefill_smem_bytes();
 
+// KV-cache wire format (q3a_wire.cu): copies between a blob's payload and
+// the paged cache.  Copied heads h < nkv are payload heads pay_head0 + h and
+// context-local cache heads head_off + h.
+struct WireParams {
+    void* payload;           // the blob's payload (device memory)
+    void* kcache;
+    void* vcache;
+    int layer0, n_layers;
+    int nkv;                 // heads copied
+    int pay_nkv, pay_head0;  // heads per layer in the payload, first one copied
+    int ctx_nkv, head_off;   // the context's heads (cache layout), first one copied
+    int pos0, n_tok, slot;
+    int pages_per_seq, page_tokens, n_pages;
+};
+cudaError_t launch_wire_copy(const WireParams& p, bool bf16, bool pack, cudaStream_t st);
+cudaError_t launch_wire_checksum(const void* payload, size_t bytes, unsigned long long* out,
+                                 cudaStream_t st);
+uint64_t wire_checksum_host(const void* payload, size_t bytes);
+
 uint64_t stream_key(uint64_t seed, uint64_t stream);
 
 // Sets the message q3a_last_error() returns on this thread; returns code.

@@ -36,7 +36,12 @@ EXPORTS = [
     "q3a_set_deterministic",
     "q3a_randn", "q3a_kv_synth",
     "q3a_launch_count", "q3a_attn_decode_noalloc", "q3a_noalloc_check_error",
+    "q3a_kv_wire_bytes", "q3a_kv_pack", "q3a_kv_unpack", "q3a_kv_wire_check",
 ]
+
+KV_WIRE_MAGIC = 0x564B3351
+KV_WIRE_VERSION = 1
+KV_WIRE_HEADER_BYTES = 64
 
 
 class Cfg(ctypes.Structure):
@@ -110,6 +115,11 @@ def load():
         L.q3a_noalloc_check_error.argtypes = [_P]
         L.q3a_launch_count.argtypes = [_P]
         L.q3a_launch_count.restype = _U64
+        L.q3a_kv_wire_bytes.argtypes = [_P, _I, _I]
+        L.q3a_kv_wire_bytes.restype = _SZ
+        L.q3a_kv_pack.argtypes = [_P, _I, _I, _I, _I, _I, _P, _SZ]
+        L.q3a_kv_unpack.argtypes = [_P, _I, _P, _SZ]
+        L.q3a_kv_wire_check.argtypes = [_P, _SZ]
         _lib = L
     return _lib
 
@@ -136,6 +146,21 @@ def attn_decode_noalloc(xb, q, kc, vc, loff, pos, n_heads, kv_mul, hd, kv_dim, m
     allocated; queued on the given CUDA stream handle."""
     check(load().q3a_attn_decode_noalloc(ptr(xb), ptr(q), ptr(kc), ptr(vc), loff, pos, n_heads,
                                          kv_mul, hd, kv_dim, max_seq, stream_handle))
+
+
+def kv_wire_check(blob) -> None:
+    """q3a_kv_wire_check on a blob in host memory (bytes, bytearray or a
+    uint8 numpy array): header fields and payload checksum, no GPU."""
+    import numpy as np
+    a = np.frombuffer(blob, dtype=np.uint8) if isinstance(blob, (bytes, bytearray)) else blob
+    a = np.ascontiguousarray(a)
+    check(load().q3a_kv_wire_check(a.ctypes.data, a.nbytes))
+
+
+def _nbytes(t) -> int:
+    if hasattr(t, "element_size"):
+        return t.numel() * t.element_size()
+    return t.nbytes
 
 
 def noalloc_check_error(stream_handle=None):
@@ -315,6 +340,18 @@ class Context:
 
     def gather_cols(self, off, rows, row_bytes, col0, col_bytes):
         check(self.lib.q3a_gather_cols(self.h, off, rows, row_bytes, col0, col_bytes))
+
+    def kv_wire_bytes(self, n_layers, n_tok) -> int:
+        return int(self.lib.q3a_kv_wire_bytes(self.h, n_layers, n_tok))
+
+    def kv_pack(self, seq, layer0, n_layers, pos0, n_tok, dst):
+        """Packs the held heads' rows into dst (a byte buffer: numpy uint8
+        in host mode, a torch uint8 device tensor in device mode)."""
+        check(self.lib.q3a_kv_pack(self.h, seq, layer0, n_layers, pos0, n_tok, ptr(dst),
+                                   _nbytes(dst)))
+
+    def kv_unpack(self, seq, src):
+        check(self.lib.q3a_kv_unpack(self.h, seq, ptr(src), _nbytes(src)))
 
     def kv_synth(self, seq, layer, pos0, n, seed, stream_k, stream_v):
         check(self.lib.q3a_kv_synth(self.h, seq, layer, pos0, n, seed, stream_k, stream_v))

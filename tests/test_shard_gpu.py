@@ -268,3 +268,24 @@ def test_sublayer_over_kv_head_shards(tmp_path, world):
         err, same = open(os.path.join(tmp_path, f"rank{rank}.txt")).read().split()
         assert float(err) <= 3e-2, f"rank {rank}: normwise {err}"
         assert same == "1", f"rank {rank}: x differs from rank 0's"
+
+
+def test_prefill_to_decode_handoff(tmp_path):
+    """Disaggregated prefill and decode on two GPUs: the prompt's KV rows
+    travel as one wire blob (q3a_kv_pack -> NCCL send -> q3a_kv_unpack); the
+    next token's attention on the decode GPU equals the prefill GPU's bit for
+    bit."""
+    import subprocess
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", SHARD_TEST_OUT=str(tmp_path))
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2",
+           "--master-addr", "127.0.0.1", "--master-port", str(_free_port()),
+           os.path.join(ROOT, "tests", "wire_handoff_worker.py")]
+    r = subprocess.run(cmd, env=env, timeout=240, capture_output=True, text=True)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
+    a = np.load(os.path.join(tmp_path, "xb0.npy"))
+    b = np.load(os.path.join(tmp_path, "xb1.npy"))
+    assert np.isfinite(a).all() and np.abs(a).max() > 0
+    assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
