@@ -878,6 +878,9 @@ static int launch_wo_residual(q3a_ctx* c, float* x, const float* xb, const void*
         return fail(Q3A_ERR_UNSUPPORTED, "dim %d: up to %d rows are implemented", dim, WO_MAX_ROWS);
     if (((uintptr_t)x | (uintptr_t)xb | (uintptr_t)wo) & 15)
         return fail(Q3A_ERR_INVALID, "x, xb and wo must be 16-byte aligned");
+    if (c->cfg.n_heads * HD > WO_MAX_ROWS)
+        return fail(Q3A_ERR_UNSUPPORTED, "wo with %d columns: up to %d are implemented",
+                    c->cfg.n_heads * HD, WO_MAX_ROWS);
     const bool peers = c->peer_rank >= 0 && c->peer_world > 1;
     if (c->nkv != c->cfg.n_kv_heads && !peers)
         return fail(Q3A_ERR_INVALID,

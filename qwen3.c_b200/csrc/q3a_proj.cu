@@ -46,7 +46,10 @@ constexpr int NTHREADS = NCONS + 32;            // + the producer warp
 constexpr int OFF_BAR = STAGES * STAGE_BYTES;   // full[STAGES], empty[STAGES]
 constexpr int OFF_MISC = OFF_BAR + 2 * STAGES * 8;  // 16 ints
 constexpr int OFF_WRED = OFF_MISC + 64;         // [CWARPS] floats: block reductions
-constexpr int OFF_RED = OFF_WRED + 64;          // [rows of the range][CWARPS] warp sums
+constexpr int MAX_STAGES_T = 64;                // stages of one CTA's range, at most (wo)
+constexpr int OFF_CNT = OFF_WRED + 64;          // [MAX_STAGES_T] warps done per stage (wo)
+constexpr int OFF_RED = OFF_CNT + MAX_STAGES_T * 4;  // [rows of the range][CWARPS] warp sums
+constexpr int WO_THREADS = NTHREADS + 32;       // wo: + a sender warp
 }  // namespace proj
 
 __device__ __forceinline__ float2 h2f2(uint32_t u) {
@@ -194,7 +197,8 @@ __device__ __forceinline__ void load_x(float2 (&xv)[NP][4], const float* x, int 
 template <int NP>
 __device__ void ring_consume(const uint8_t* smem, uint64_t* full, uint64_t* empty, float* red,
                              int n_rows, int row_bytes, int SR, int n_pieces,
-                             const float2 (&xv)[NP][4], int tid, int* err) {
+                             const float2 (&xv)[NP][4], int tid, int* err,
+                             int* stage_done = nullptr) {
     const int warp = tid >> 5, lane = tid & 31;
     const int n_stages = (n_rows + SR - 1) / SR;
     bool ok = true;
@@ -229,7 +233,13 @@ __device__ void ring_consume(const uint8_t* smem, uint64_t* full, uint64_t* empt
             }
         }
         __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[st]);
+        if (lane == 0) {
+            mbar_arrive(&empty[st]);
+            if (stage_done) {  // this warp's sums of stage k are in red
+                __threadfence_block();
+                atomicAdd(&stage_done[k], 1);
+            }
+        }
     }
 }
 
@@ -373,12 +383,17 @@ __global__ void __launch_bounds__(proj::NTHREADS, 1) qkv_kernel(const __grid_con
 }
 
 // ---------------------------------------------------------------- wo
+// A sender warp takes each stage's rows as soon as the 16 consumer warps
+// have summed them: it adds the warp sums and either adds the row into x
+// (one rank) or stores it, tagged with the call number, into its row of
+// every rank's exchange buffer (several ranks), so the exchange overlaps the
+// weight stream; then it adds the ranks' partials in rank order.
 template <int NP>
-__global__ void __launch_bounds__(proj::NTHREADS, 1) wo_kernel(const __grid_constant__ WoParams P) {
+__global__ void __launch_bounds__(proj::WO_THREADS, 1) wo_kernel(const __grid_constant__ WoParams P) {
     extern __shared__ __align__(128) uint8_t smem[];
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + proj::OFF_BAR);
     uint64_t* empty = full + proj::STAGES;
-    volatile int* misc = reinterpret_cast<volatile int*>(smem + proj::OFF_MISC);
+    int* cnt = reinterpret_cast<int*>(smem + proj::OFF_CNT);
     float* red = reinterpret_cast<float*>(smem + proj::OFF_RED);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -387,8 +402,10 @@ __global__ void __launch_bounds__(proj::NTHREADS, 1) wo_kernel(const __grid_cons
     const int n_rows = r_end - r_begin;
     const int row_bytes = P.ncols * 2;
     const int SR = proj::STAGE_BYTES / row_bytes;
+    const int n_stages = (n_rows + SR - 1) / SR;
 
     if (tid == 0) ring_init(full, empty);
+    for (int k = tid; k < proj::MAX_STAGES_T; k += blockDim.x) cnt[k] = 0;
     __syncthreads();
 
     if (warp == proj::CWARPS) {
@@ -402,53 +419,71 @@ __global__ void __launch_bounds__(proj::NTHREADS, 1) wo_kernel(const __grid_cons
         }
         return;
     }
-
-    griddep_wait();  // xb (the decode's output) is visible
-    if (tid == 0) {
-        griddep_launch_dependents();
-        misc[0] = P.world > 1 ? (int)(P.epoch[c] + 1u) : 0;  // this call's tag
+    if (warp == proj::CWARPS + 1) {
+        // ============================================ sender
+        griddep_wait();  // x may be read by the kernel before: write it after
+        const bool multi = P.world > 1;
+        unsigned tag = 0;
+        if (multi) tag = __shfl_sync(FULL, lane == 0 ? P.epoch[c] + 1u : 0u, 0);
+        const size_t half = (size_t)(tag & 1u) * P.world * WO_MAX_ROWS;
+        bool ok = true;
+        for (int k = 0; k < n_stages && ok; k++) {
+            // the consumers' sums of stage k (bounded wait; they count a
+            // stage even when their own wait gave up)
+            const long long t0 = clock64();
+            while (*reinterpret_cast<volatile int*>(&cnt[k]) < proj::CWARPS) {
+                if (clock64() - t0 > P.wait_limit) {
+                    ok = false;
+                    break;
+                }
+            }
+            if (!ok) break;
+            __threadfence_block();
+            const int n = min(SR, n_rows - k * SR);
+            for (int j = lane; j < n; j += 32) {
+                const int t = k * SR + j, r = r_begin + t;
+                const float s = row_sum(red, t);
+                if (!multi) {
+                    P.x[r] = P.x[r] + s;  // x += xb2 (qwen3-8b/cpu/main.c:1356)
+                } else {
+                    for (int q = 0; q < P.world; q++)
+                        st_word_sys(P.recv[q] + half + (size_t)P.rank * WO_MAX_ROWS + r, s, tag);
+                }
+            }
+        }
+        if (!ok) {
+            if (lane == 0) atomicExch(P.err, DEV_ERR_TIMEOUT);
+            return;
+        }
+        if (!multi) return;
+        // every rank's partial of each row, added in rank order
+        for (int t = lane; t < n_rows; t += 32) {
+            const int r = r_begin + t;
+            float tot = 0.0f;
+            bool got = true;
+            for (int q = 0; q < P.world && got; q++) {
+                float v;
+                got = wait_word(P.recv[P.rank] + half + (size_t)q * WO_MAX_ROWS + r, tag, v,
+                                P.wait_limit);
+                tot += v;
+            }
+            if (got)
+                P.x[r] = P.x[r] + tot;
+            else
+                atomicExch(P.err, DEV_ERR_TIMEOUT);
+        }
+        __syncwarp();
+        if (lane == 0) P.epoch[c] = tag;
+        return;
     }
+
+    // ================================================ consumers (16 warps)
+    griddep_wait();  // xb (the decode's output) is visible
+    if (tid == 0) griddep_launch_dependents();
     const int n_pieces = P.ncols >> 3;
     float2 xv[NP][4];
     load_x<NP>(xv, P.xb + P.col0, n_pieces, tid);
-    ring_consume<NP>(smem, full, empty, red, n_rows, row_bytes, SR, n_pieces, xv, tid, P.err);
-    named_bar_sync(1, proj::NCONS);
-    if (P.world <= 1) {
-        // x += xb2 (qwen3-8b/cpu/main.c:1356)
-        for (int t = tid; t < n_rows; t += proj::NCONS) {
-            const int r = r_begin + t;
-            P.x[r] = P.x[r] + row_sum(red, t);
-        }
-        return;
-    }
-    // Row-parallel shards: every rank stores its partial row sums, tagged
-    // with the call number, into its row of every rank's buffer (half
-    // tag & 1: a rank is at most one call ahead of another, since finishing
-    // a call needs every rank's words of it); then each rank adds the ranks'
-    // partials in rank order, so every rank gets the same bits.
-    const unsigned tag = (unsigned)misc[0];
-    const size_t half = (size_t)(tag & 1u) * P.world * WO_MAX_ROWS;
-    for (int t = tid; t < n_rows; t += proj::NCONS) {
-        const float s = row_sum(red, t);
-        for (int q = 0; q < P.world; q++)
-            st_word_sys(P.recv[q] + half + (size_t)P.rank * WO_MAX_ROWS + r_begin + t, s, tag);
-    }
-    for (int t = tid; t < n_rows; t += proj::NCONS) {
-        const int r = r_begin + t;
-        float tot = 0.0f;
-        bool ok = true;
-        for (int q = 0; q < P.world && ok; q++) {
-            float v;
-            ok = wait_word(P.recv[P.rank] + half + (size_t)q * WO_MAX_ROWS + r, tag, v, P.wait_limit);
-            tot += v;
-        }
-        if (ok)
-            P.x[r] = P.x[r] + tot;
-        else
-            atomicExch(P.err, DEV_ERR_TIMEOUT);
-    }
-    named_bar_sync(1, proj::NCONS);
-    if (tid == 0) P.epoch[c] = tag;
+    ring_consume<NP>(smem, full, empty, red, n_rows, row_bytes, SR, n_pieces, xv, tid, P.err, cnt);
 }
 
 // ---------------------------------------------------------------- launch
@@ -457,12 +492,13 @@ int proj_smem_bytes(int rows, int n_ctas) {
     return proj::OFF_RED + max_rows * proj::CWARPS * 4;
 }
 
-static cudaError_t launch_pdl(const void* fn, int n_ctas, int smem, cudaStream_t st, void* arg) {
+static cudaError_t launch_pdl(const void* fn, int n_ctas, int threads, int smem, cudaStream_t st,
+                              void* arg) {
     cudaError_t e = ensure_smem_attr(fn, smem);
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(n_ctas);
-    cfg.blockDim = dim3(proj::NTHREADS);
+    cfg.blockDim = dim3(threads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
@@ -482,14 +518,15 @@ cudaError_t launch_qkv(const QkvParams& p, bool bf16, int n_ctas, cudaStream_t s
                     : reinterpret_cast<const void*>(qkv_kernel<__nv_bfloat16, 1>))
              : (two ? reinterpret_cast<const void*>(qkv_kernel<float, 2>)
                     : reinterpret_cast<const void*>(qkv_kernel<float, 1>));
-    return launch_pdl(fn, n_ctas, proj_smem_bytes(p.rows_total, n_ctas), st,
+    return launch_pdl(fn, n_ctas, proj::NTHREADS, proj_smem_bytes(p.rows_total, n_ctas), st,
                       const_cast<QkvParams*>(&p));
 }
 
 cudaError_t launch_wo(const WoParams& p, int n_ctas, cudaStream_t st) {
     const void* fn = p.ncols > 4096 ? reinterpret_cast<const void*>(wo_kernel<2>)
                                     : reinterpret_cast<const void*>(wo_kernel<1>);
-    return launch_pdl(fn, n_ctas, proj_smem_bytes(p.rows, n_ctas), st, const_cast<WoParams*>(&p));
+    return launch_pdl(fn, n_ctas, proj::WO_THREADS, proj_smem_bytes(p.rows, n_ctas), st,
+                      const_cast<WoParams*>(&p));
 }
 
 }  // namespace q3a
