@@ -103,6 +103,25 @@ const char *q3a_last_error(void);
 int q3a_set_stream(q3a_ctx *ctx, void *cuda_stream);
 int q3a_sync(q3a_ctx *ctx);
 
+/* ---- Recording a token step as one CUDA graph, for C hosts without the
+ * CUDA runtime headers (the reference's forward_gpu launches its ~20 kernels
+ * per layer one by one, qwen3-8b/gpu/main.c:2069-2161).  q3a_graph_begin
+ * starts recording the context's stream (device-pointer mode; a stream set
+ * with q3a_set_stream must not be the legacy NULL stream); the library calls
+ * made until q3a_graph_end are recorded, not run, and q3a_graph_end returns
+ * them as a replayable graph; q3a_graph_launch replays it on the context's
+ * stream (same pointers, layers and positions as recorded; the kernels'
+ * chaining is kept).  Make one ordinary call of each entry point before
+ * recording it (first calls allocate their scratch) and no call that waits
+ * for the stream (q3a_sync, host-pointer calls, q3a_kv_pack / unpack) while
+ * recording.  The host's own kernels may be recorded in between on the same
+ * stream.  q3a_graph_destroy frees a graph. */
+typedef struct q3a_graph q3a_graph;
+int q3a_graph_begin(q3a_ctx *ctx);
+int q3a_graph_end(q3a_ctx *ctx, q3a_graph **graph);
+int q3a_graph_launch(q3a_ctx *ctx, q3a_graph *graph);
+int q3a_graph_destroy(q3a_graph *graph);
+
 /* Reads and clears the device error flag set by bounded waits in the kernels
  * (Q3A_ERR_TIMEOUT when one expired, else Q3A_OK). */
 int q3a_check_device_error(q3a_ctx *ctx);

@@ -432,6 +432,67 @@ extern "C" int q3a_sync(q3a_ctx* c) {
     return Q3A_OK;
 }
 
+// ------------------------------------------------------------------ graphs
+struct q3a_graph {
+    cudaGraphExec_t exec = nullptr;
+    int device = 0;
+};
+
+extern "C" int q3a_graph_begin(q3a_ctx* c) {
+    g_err[0] = 0;
+    if (!c) return fail(Q3A_ERR_INVALID, "null context");
+    if (c->cfg.ptr_mode != Q3A_PTR_DEVICE)
+        return fail(Q3A_ERR_UNSUPPORTED, "graphs record device-pointer calls only");
+    int rc = ensure_device(c);
+    if (rc) return rc;
+    CUDA_TRY(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
+    // the first recorded decode must not assume which kernel runs before the
+    // graph when it is replayed
+    forget_last(c);
+    return Q3A_OK;
+}
+
+extern "C" int q3a_graph_end(q3a_ctx* c, q3a_graph** out) {
+    g_err[0] = 0;
+    if (!c || !out) return fail(Q3A_ERR_INVALID, "null argument");
+    *out = nullptr;
+    int rc = ensure_device(c);
+    if (rc) return rc;
+    cudaGraph_t g = nullptr;
+    CUDA_TRY(cudaStreamEndCapture(c->stream, &g));
+    cudaGraphExec_t e = nullptr;
+    const cudaError_t ie = cudaGraphInstantiate(&e, g, 0);
+    cudaGraphDestroy(g);
+    if (ie != cudaSuccess) return fail(Q3A_ERR_CUDA, "graph instantiation: %s", cudaGetErrorString(ie));
+    q3a_graph* h = new q3a_graph;
+    h->exec = e;
+    h->device = c->cfg.device;
+    *out = h;
+    forget_last(c);
+    return Q3A_OK;
+}
+
+extern "C" int q3a_graph_launch(q3a_ctx* c, q3a_graph* g) {
+    g_err[0] = 0;
+    if (!c || !g) return fail(Q3A_ERR_INVALID, "null argument");
+    if (g->device != c->cfg.device) return fail(Q3A_ERR_INVALID, "graph of device %d", g->device);
+    int rc = ensure_device(c);
+    if (rc) return rc;
+    CUDA_TRY(cudaGraphLaunch(g->exec, c->stream));
+    forget_last(c);
+    return Q3A_OK;
+}
+
+extern "C" int q3a_graph_destroy(q3a_graph* g) {
+    if (!g) return Q3A_OK;
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (cur != g->device) cudaSetDevice(g->device);
+    cudaGraphExecDestroy(g->exec);
+    delete g;
+    return Q3A_OK;
+}
+
 extern "C" int q3a_check_device_error(q3a_ctx* c) {
     if (!c) return fail(Q3A_ERR_INVALID, "null context");
     int rc = ensure_device(c);
@@ -843,9 +904,16 @@ extern "C" int q3a_qkv_proj(q3a_ctx* c, float* q, float* k, float* v, const floa
 
 // The decode of the held heads over rows [0, pos] of slot 0 with the
 // prepared q (after launch_proj).
-static int decode_after_proj(q3a_ctx* c, float* xb, const float* q, int layer, int pos) {
+static int decode_after_proj(q3a_ctx* c, float* xb, const float* q, int layer, int pos,
+                             const void* wo_next = nullptr, int wo_rows = 0) {
     DecodeParams p;
     base_params(c, p, layer);
+    if (wo_next) {  // the wo kernel's rows (held columns) into L2 meanwhile
+        p.pf_base = reinterpret_cast<const uint8_t*>(wo_next) + (size_t)c->kv0 * GQA * HD * 2;
+        p.pf_rows = wo_rows;
+        p.pf_row_bytes = c->nkv * GQA * HD * 2;
+        p.pf_ld_bytes = (long long)c->cfg.n_heads * HD * 2;
+    }
     p.nb = 1;
     p.fused = 0;
     p.t_begin[0] = 0;
@@ -936,7 +1004,7 @@ extern "C" int q3a_attn_sublayer(q3a_ctx* c, float* x, const float* att_norm_w, 
     rc = launch_proj(c, c->sub_q, nullptr, nullptr, x, att_norm_w, wq, wk, wv, dim, q_norm_w,
                      k_norm_w, layer, pos);
     if (rc) return rc;
-    rc = decode_after_proj(c, c->sub_xb, c->sub_q, layer, pos);
+    rc = decode_after_proj(c, c->sub_xb, c->sub_q, layer, pos, wo, dim);
     if (rc) return rc;
     return launch_wo_residual(c, x, c->sub_xb, wo, dim);
 }

@@ -123,6 +123,14 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
         : "memory");
 }
 
+// Bulk prefetch of global memory into L2 (a hint; 16-byte aligned address,
+// size a multiple of 16).
+__device__ __forceinline__ void l2_prefetch(const void* src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(src)),
+                 "r"(bytes)
+                 : "memory");
+}
+
 __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar,
                                             int x, int y, int z, uint64_t policy) {
     asm volatile(

@@ -840,6 +840,21 @@ __global__ void __launch_bounds__(DecCfg<KV, TC>::NTHREADS, 1)
                 }
             }
             }
+            // The next kernel's weights into L2 while this CTA's last stages
+            // and the merge run (HBM is otherwise idle then).
+            if (P.pf_base) {
+                const int r0 = (int)(((long long)c * P.pf_rows) / gridDim.x);
+                const int r1 = (int)(((long long)(c + 1) * P.pf_rows) / gridDim.x);
+                if ((long long)P.pf_row_bytes == P.pf_ld_bytes) {
+                    const uint8_t* a = P.pf_base + (long long)r0 * P.pf_ld_bytes;
+                    long long left = (long long)(r1 - r0) * P.pf_row_bytes;
+                    for (; left > 0; left -= 32768, a += 32768)
+                        l2_prefetch(a, (uint32_t)min(left, 32768LL));
+                } else {
+                    for (int r = r0; r < r1; r++)
+                        l2_prefetch(P.pf_base + (long long)r * P.pf_ld_bytes, (uint32_t)P.pf_row_bytes);
+                }
+            }
             // Drain: the CTA never exits with a bulk copy still writing its
             // shared memory (bounded, like every wait here).
             const int first = it > C::STAGES ? it - C::STAGES : 0;

@@ -99,6 +99,13 @@ struct DecodeParams {
     unsigned* group_epoch;   // spread merge: call number per group [MAX_PIECES]
     const float* inv_freq;   // [64] RoPE inverse frequencies (host powf, reference formula)
     long long wait_limit;    // SM clocks a wait on another CTA or rank may take
+    // Optional L2 prefetch of the next kernel's weights (the wo rows of the
+    // sublayer), issued by each CTA's producer once its cache rows are all
+    // requested: rows [c R / G, (c+1) R / G) of pf_rows rows, pf_row_bytes
+    // from pf_base + r * pf_ld_bytes (null pf_base: none).
+    const uint8_t* pf_base;
+    int pf_rows, pf_row_bytes;
+    long long pf_ld_bytes;
     Piece pieces[MAX_PIECES];
     short cta_piece[MAX_PIECES];  // piece mode: piece processed by CTA c (groups interleaved)
     int t_begin[MAX_B];      // first cache position attended per sequence

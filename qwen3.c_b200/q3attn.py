@@ -37,6 +37,7 @@ EXPORTS = [
     "q3a_randn", "q3a_kv_synth",
     "q3a_launch_count", "q3a_attn_decode_noalloc", "q3a_noalloc_check_error",
     "q3a_kv_wire_bytes", "q3a_kv_pack", "q3a_kv_unpack", "q3a_kv_wire_check",
+    "q3a_graph_begin", "q3a_graph_end", "q3a_graph_launch", "q3a_graph_destroy",
 ]
 
 KV_WIRE_MAGIC = 0x564B3351
@@ -120,6 +121,10 @@ def load():
         L.q3a_kv_pack.argtypes = [_P, _I, _I, _I, _I, _I, _P, _SZ]
         L.q3a_kv_unpack.argtypes = [_P, _I, _P, _SZ]
         L.q3a_kv_wire_check.argtypes = [_P, _SZ]
+        L.q3a_graph_begin.argtypes = [_P]
+        L.q3a_graph_end.argtypes = [_P, ctypes.POINTER(_P)]
+        L.q3a_graph_launch.argtypes = [_P, _P]
+        L.q3a_graph_destroy.argtypes = [_P]
         _lib = L
     return _lib
 
@@ -340,6 +345,21 @@ class Context:
 
     def gather_cols(self, off, rows, row_bytes, col0, col_bytes):
         check(self.lib.q3a_gather_cols(self.h, off, rows, row_bytes, col0, col_bytes))
+
+    def graph_begin(self):
+        check(self.lib.q3a_graph_begin(self.h))
+
+    def graph_end(self):
+        """The recorded calls as a graph handle (q3a_graph_destroy frees it)."""
+        g = _P()
+        check(self.lib.q3a_graph_end(self.h, ctypes.byref(g)))
+        return g
+
+    def graph_launch(self, g):
+        check(self.lib.q3a_graph_launch(self.h, g))
+
+    def graph_destroy(self, g):
+        check(self.lib.q3a_graph_destroy(g))
 
     def kv_wire_bytes(self, n_layers, n_tok) -> int:
         return int(self.lib.q3a_kv_wire_bytes(self.h, n_layers, n_tok))
