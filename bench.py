@@ -726,6 +726,29 @@ def ncu_case(args):
         ctx.close()
         print(f"ncu case prefill: {args.warmup + args.steps} launches ok")
         return
+    if args.ncu_case == "sublayer":
+        # 2 layers of the attention sublayer at KV 8192 (fp32 cache),
+        # alternating: the three kernels of q3a_attn_sublayer per call
+        stream = torch.cuda.Stream(device=dev)
+        ctx = q3attn.Context(n_layers=2, max_seq=L_CTX, ptr_mode=q3attn.PTR_DEVICE)
+        ctx.set_stream(stream.cuda_stream)
+        fill_cache(ctx, torch, dev, 1234, 2, POS, stream)
+        with torch.cuda.stream(stream):
+            wq = (torch.randn(2, HQ * HD, DIM, device=dev) * 0.02).half()
+            wk = (torch.randn(2, KV_DIM, DIM, device=dev) * 0.02).half()
+            wv = (torch.randn(2, KV_DIM, DIM, device=dev) * 0.02).half()
+            wo = (torch.randn(2, DIM, HQ * HD, device=dev) * 0.02).half()
+            att = torch.ones(2, DIM, device=dev)
+            x = torch.randn(DIM, device=dev)
+            w = torch.ones(HD, device=dev)
+        for i in range(args.warmup + args.steps):
+            l = i % 2
+            ctx.attn_sublayer(x, att[l], wq[l], wk[l], wv[l], w, w, wo[l], l, POS)
+        stream.synchronize()
+        ctx.check_device_error()
+        ctx.close()
+        print(f"ncu case sublayer: {args.warmup + args.steps} calls ok")
+        return
     if args.ncu_case == "wo":
         # 2 layers of wo (2 x 34 MB) alternating
         stream = torch.cuda.Stream(device=dev)
@@ -794,7 +817,7 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-variants", action="store_true")
-    ap.add_argument("--ncu-case", default=None, choices=["decode-f32", "decode-bf16", "prefill", "qkv", "wo"],
+    ap.add_argument("--ncu-case", default=None, choices=["decode-f32", "decode-bf16", "prefill", "qkv", "wo", "sublayer"],
                     help="small single-kernel run for ncu captures (2 layers, direct launches)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
