@@ -219,3 +219,46 @@ def test_qkv_proj_alone_matches_oracle(weights, dim):
                 tol = 1e-2 if bf16 else 1e-5
                 assert normwise(rk.cpu().numpy(), k_r) <= tol
                 assert normwise(rv.cpu().numpy(), v_r) <= tol
+
+
+def test_qkv_proj_sharded_context(weights):
+    """A context holding KV heads [2, 5) projects only their rows: q heads
+    8..19 and KV heads 2..4 at their places in the full-width outputs (the
+    other entries untouched), and appends only its heads' rows."""
+    import torch
+    dev = torch.device("cuda:0")
+    (wq, wk, wv), (dq, dk, dv) = weights
+    b, n = 2, 3
+    qw = (1.0 + 0.25 * orc.randn(HD, 7900, 6)).astype(np.float32)
+    kw = (1.0 + 0.25 * orc.randn(HD, 7900, 7)).astype(np.float32)
+    pos, layer = 777, 1
+    x = orc.randn(DIM, 7901, 8)
+    q_r = orc.mm_f16(x, wq)
+    k_r = orc.mm_f16(x, wk)
+    v_r = orc.mm_f16(x, wv)
+    orc.rmsnorm_head(q_r, qw, HQ, HD, EPS)
+    orc.rmsnorm_head(k_r, kw, HKV, HD, EPS)
+    orc.rope(q_r, HQ, HD, pos, THETA)
+    orc.rope(k_r, HKV, HD, pos, THETA)
+    with q3attn.Context(n_layers=2, max_seq=1024, ptr_mode=q3attn.PTR_DEVICE,
+                        kv_head_begin=b, kv_head_count=n) as ctx:
+        q = torch.full((HQ * HD,), 7.0, device=dev)
+        k = torch.full((KV_DIM,), 7.0, device=dev)
+        v = torch.full((KV_DIM,), 7.0, device=dev)
+        ctx.qkv_proj(q, k, v, torch.from_numpy(x).to(dev), dq, dk, dv,
+                     torch.from_numpy(qw).to(dev), torch.from_numpy(kw).to(dev), layer, pos)
+        rk = torch.zeros(n * HD, device=dev)
+        rv = torch.zeros(n * HD, device=dev)
+        ctx.kv_read(0, layer, pos, 1, rk, rv)
+        ctx.sync()
+        ctx.check_device_error()
+        qh, kh, vh = q.cpu().numpy(), k.cpu().numpy(), v.cpu().numpy()
+    qs = slice(b * KV_MUL * HD, (b + n) * KV_MUL * HD)
+    ks = slice(b * HD, (b + n) * HD)
+    assert normwise(qh[qs], q_r[qs]) <= TOL_PROJ
+    assert normwise(kh[ks], k_r[ks]) <= TOL_PROJ
+    assert normwise(vh[ks], v_r[ks]) <= TOL_PROJ
+    for a in (np.delete(qh, np.r_[qs]), np.delete(kh, np.r_[ks]), np.delete(vh, np.r_[ks])):
+        assert (a == 7.0).all()
+    assert normwise(rk.cpu().numpy(), k_r[ks]) <= 1e-5
+    assert normwise(rv.cpu().numpy(), v_r[ks]) <= 1e-5
