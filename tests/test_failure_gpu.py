@@ -117,3 +117,57 @@ def test_wait_limit_rejects_bad_values():
             assert e.value.code == q3attn.ERR_INVALID
         a.set_wait_limit(0.5)
         a.set_wait_limit(0)
+
+
+def test_wo_exchange_rank_that_never_arrives():
+    """Row-parallel wo over two KV-head shards where rank 1 never calls: rank
+    0's wo kernel stores its partial sums, waits (bounded) for rank 1's,
+    gives up, reports Q3A_ERR_TIMEOUT and leaves x as it was."""
+    import torch
+    dev = torch.device("cuda:0")
+    L = 1000
+    kc, vc, _, _ = orc.make_cache(33, 0, L, HKV, HD, L)
+    q = orc.randn(HQ * HD, 33, 9)
+    dim = 4096
+    wo = (torch.randn(dim, HQ * HD, device=dev) * 0.02).half()
+    with q3attn.Context(n_layers=1, max_seq=L, ptr_mode=q3attn.PTR_DEVICE,
+                        kv_head_begin=0, kv_head_count=4) as a, \
+            q3attn.Context(n_layers=1, max_seq=64, ptr_mode=q3attn.PTR_DEVICE,
+                           kv_head_begin=4, kv_head_count=4) as b, \
+            q3attn.Context(n_layers=1, max_seq=L, ptr_mode=q3attn.PTR_DEVICE) as full:
+        a.peer_export(2)
+        b.peer_export(2)
+        a.peer_open_ptrs(0, 2, [a.peer_buffer(), b.peer_buffer()])
+        a.set_wait_limit(LIMIT_S)
+        x = torch.randn(dim, device=dev)
+        x0 = x.clone()
+        xb = torch.randn(HQ * HD, device=dev)
+        torch.cuda.synchronize(dev)
+        t0 = time.perf_counter()
+        a.wo_residual(x, xb, wo)
+        a.sync()
+        waited = time.perf_counter() - t0
+        with pytest.raises(q3attn.Q3AError) as e:
+            a.check_device_error()
+        assert e.value.code == q3attn.ERR_TIMEOUT
+        assert waited < 0.5, waited
+        assert torch.equal(x, x0)
+        a.set_wait_limit(0)
+        full.kv_load(0, 0, 0, L, torch.from_numpy(kc).to(dev), torch.from_numpy(vc).to(dev))
+        _decode_still_works(full, torch, dev, kc, vc, q, L, False)
+        # the context that timed out still runs its own kernels: the fused
+        # block of one token on its KV heads, against the oracle
+        from test_decode_gpu import oracle_block, oracle_inputs
+        pos = L - 1
+        kc2, vc2, q2, k2, v2, qw, kw = oracle_inputs(34, pos, L, False)
+        xr, _, _ = oracle_block(kc2, vc2, q2, k2, v2, qw, kw, pos, L, False)
+        a.kv_load(0, 0, 0, pos, torch.from_numpy(kc2[:pos * KV_DIM]).to(dev),
+                  torch.from_numpy(vc2[:pos * KV_DIM]).to(dev))
+        xbd = torch.zeros(1, HQ * HD, device=dev)
+        t = lambda arr: torch.from_numpy(arr).to(dev)  # noqa: E731
+        a.attn_layer_batched(xbd, t(q2).reshape(1, -1).contiguous(), t(k2).reshape(1, -1).contiguous(),
+                             t(v2).reshape(1, -1).contiguous(), t(qw), t(kw), 0, [0], [pos])
+        a.sync()
+        a.check_device_error()
+        held = slice(0, 4 * KV_MUL * HD)
+        _check(xbd.cpu().numpy()[0, held], xr[held], False)
