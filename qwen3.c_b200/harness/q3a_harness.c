@@ -4,8 +4,8 @@
  * headers), generates the decode shapes of the benchmark configurations and
  * times the full-depth step end to end through the host-pointer API.
  *
- * The per-layer call is the binding a Qwen3.c maintainer adds to forward()
- * (INTEGRATION.md): attn_init() after the config is known, then one
+ * The per-layer call is the binding a Qwen3.c maintainer adds to forward():
+ * attn_init() after the config is known, then one
  * q3a_attn_layer() per layer in place of the inline block of
  * qwen3-8b/cpu-multicore/main.c:1331-1369, on run-state buffers laid out like
  * the reference's State (qwen3-8b/cpu/main.c:646-650).
@@ -41,7 +41,7 @@ typedef struct {
     float *q, *k, *v, *xb;
 } State;
 
-/* ---- the binding */
+/* ---- the binding a maintainer adds to forward() */
 static q3a_ctx *g_attn;
 
 static void attn_init(const Config *c, int kv_dtype, int device) {

@@ -1,6 +1,6 @@
 """The C host harness (qwen3.c_b200/lib/q3a_harness): a C program built
-against include/q3attn.h alone, whose per-layer call is the forward()
-binding INTEGRATION.md gives, runs the block on the GPU through the
+against include/q3attn.h alone, whose per-layer call is the binding a
+maintainer adds to the reference's forward(), runs the block on the GPU through the
 host-pointer API.  Its layer-0 call is checked against the oracle and
 against the reference's own compiled launch_attn (oracle/_ref) on the cache
 rows the library holds, read back by the harness with q3a_kv_read.
