@@ -1,6 +1,5 @@
-// q3a_gemv.cuh -- the streaming fp16 GEMV engine of the projections, shared
-// by the projection kernels (q3a_proj.cu) and by the decode kernel's
-// projection prologue (q3a_decode.cu).
+// q3a_gemv.cuh -- the streaming fp16 GEMV engine of the projection kernels
+// (q3a_proj.cu), parameterised by the number of consumer warps.
 //
 // The rows of a projection form one list; CTA c of G takes rows
 // [c R / G, (c+1) R / G).  A producer thread streams the range with bulk
@@ -19,6 +18,8 @@
 namespace q3a {
 namespace gemv {
 
+// 12 stages of 16 KB (two rows at width 4096) measured slower: the
+// consumers' four-row groups run half empty
 constexpr int STAGE_BYTES = 32768;
 constexpr int STAGES = 6;
 
