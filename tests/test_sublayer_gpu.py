@@ -33,14 +33,15 @@ def to_dev_f16(torch, w, dev):
     return torch.from_numpy(w.view(np.uint16).astype(np.int16)).view(torch.float16).to(dev)
 
 
-def sublayer_weights(seed):
-    """Seeded Qwen3-8B attention-sublayer weights (fp16 matrices, fp32 gains)."""
+def sublayer_weights(seed, dim=DIM):
+    """Seeded attention-sublayer weights of a model of width dim (Qwen3-8B:
+    4096; Qwen3-4B: 2560), fp16 matrices and fp32 gains."""
     return dict(
-        att=(1.0 + 0.1 * orc.randn(DIM, seed, 9)).astype(np.float32),
-        wq=orc.proj_weights(seed, HQ * HD, DIM),
-        wk=orc.proj_weights(seed + 1, KV_DIM, DIM),
-        wv=orc.proj_weights(seed + 2, KV_DIM, DIM),
-        wo=orc.proj_weights(seed + 3, DIM, HQ * HD),
+        att=(1.0 + 0.1 * orc.randn(dim, seed, 9)).astype(np.float32),
+        wq=orc.proj_weights(seed, HQ * HD, dim),
+        wk=orc.proj_weights(seed + 1, KV_DIM, dim),
+        wv=orc.proj_weights(seed + 2, KV_DIM, dim),
+        wo=orc.proj_weights(seed + 3, dim, HQ * HD),
         qn=(1.0 + 0.25 * orc.randn(HD, seed, 6)).astype(np.float32),
         kn=(1.0 + 0.25 * orc.randn(HD, seed, 7)).astype(np.float32),
     )
@@ -138,3 +139,32 @@ def test_sharded_wo_needs_peer_set(weights):
         with pytest.raises(q3attn.Q3AError):
             ctx.wo_residual(torch.zeros(DIM, device=dev), torch.zeros(HQ * HD, device=dev),
                             D["wo"])
+
+
+def test_sublayer_at_qwen3_4b_width():
+    """Width 2560 (Qwen3-4B: 32 query heads, 8 KV heads of 128): six rows per
+    projection stage, wo of 2560 rows x 4096 columns; one layer, two tokens."""
+    import torch
+    dev = torch.device("cuda:0")
+    dim = 2560
+    W = sublayer_weights(8600, dim)
+    D = {k: (to_dev_f16(torch, v, dev) if v.dtype == np.float16 else torch.from_numpy(v).to(dev))
+         for k, v in W.items()}
+    pos0, steps = 300, 2
+    max_seq = pos0 + steps
+    kc, vc = orc.make_cache(8700, 0, pos0, HKV, HD, max_seq, kw=W["kn"])[:2]
+    with q3attn.Context(n_layers=1, max_seq=max_seq, ptr_mode=q3attn.PTR_DEVICE) as ctx:
+        ctx.kv_load(0, 0, 0, pos0, torch.from_numpy(kc[:pos0 * KV_DIM]).to(dev),
+                    torch.from_numpy(vc[:pos0 * KV_DIM]).to(dev))
+        x_ref = orc.randn(dim, 8800, 1)
+        xd = torch.from_numpy(x_ref).to(dev)
+        for s in range(steps):
+            x_old = x_ref
+            x_ref = oracle_sublayer(x_old, W, kc, vc, pos0 + s, max_seq, False)
+            ctx.attn_sublayer(xd, D["att"], D["wq"], D["wk"], D["wv"], D["qn"], D["kn"], D["wo"],
+                              0, pos0 + s)
+            ctx.sync()
+            ctx.check_device_error()
+            err = normwise(xd.cpu().numpy() - x_old, x_ref - x_old)
+            assert err <= TOL_SUB_F32, f"step {s}: normwise {err}"
+            xd.copy_(torch.from_numpy(x_ref))
