@@ -123,7 +123,11 @@ int q3a_graph_launch(q3a_ctx *ctx, q3a_graph *graph);
 int q3a_graph_destroy(q3a_graph *graph);
 
 /* Reads and clears the device error flag set by bounded waits in the kernels
- * (Q3A_ERR_TIMEOUT when one expired, else Q3A_OK). */
+ * (Q3A_ERR_TIMEOUT when one expired, else Q3A_OK).  After a timeout the
+ * context's own counters are cleared and its next calls run normally; the
+ * call numbers of a peer set (sequence shards, column gather, wo exchange)
+ * may then disagree between ranks, so a peer set that timed out is
+ * re-created on every rank (new contexts, q3a_peer_export / open). */
 int q3a_check_device_error(q3a_ctx *ctx);
 
 /* The whole attention block of one layer for one new token at `pos`

@@ -509,6 +509,11 @@ extern "C" int q3a_check_device_error(q3a_ctx* c) {
         CUDA_TRY(cudaMemsetAsync(c->words, 0, (size_t)MAX_PIECES * PART_STRIDE * 8, c->stream));
         CUDA_TRY(cudaMemsetAsync(c->group_epoch, 0, (size_t)MAX_PIECES * sizeof(unsigned), c->stream));
         CUDA_TRY(cudaMemsetAsync(c->claims, 0, (size_t)MAX_PIECES * sizeof(int), c->stream));
+        // and the projection's per-head tickets of an unfinished call
+        if (c->qkv_ticket)
+            CUDA_TRY(cudaMemsetAsync(c->qkv_ticket, 0,
+                                     (size_t)(c->cfg.n_heads + 2 * c->cfg.n_kv_heads) * sizeof(int),
+                                     c->stream));
         CUDA_TRY(cudaStreamSynchronize(c->stream));
         return fail(Q3A_ERR_TIMEOUT, "a bounded device wait expired (device error %d)", h);
     }
@@ -978,6 +983,11 @@ static int launch_wo_residual(q3a_ctx* c, float* x, const float* xb, const void*
     // one CTA per SM; every rank uses the same count (its CTA c exchanges
     // with CTA c of the others)
     const int n_ctas = std::min(std::min(dim, c->num_sms), WO_MAX_CTAS);
+    // the sender warp counts at most 64 ring stages per CTA
+    const int stage_rows = 32768 / (wp.ncols * 2), cta_rows = (dim + n_ctas - 1) / n_ctas;
+    if ((cta_rows + stage_rows - 1) / stage_rows > 64)
+        return fail(Q3A_ERR_UNSUPPORTED, "wo of %d rows over %d SMs: too many rows per SM", dim,
+                    n_ctas);
     CUDA_TRY(launch_wo(wp, n_ctas, c->stream));
     c->launches++;
     forget_last(c);
