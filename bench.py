@@ -672,6 +672,80 @@ def cpu_reference_sample(n_calls_max: int, budget_s: float, n_layers_sample: int
                       f"{threads} threads available)"}
 
 
+def cpu_sublayer_sample(n_calls_max: int, budget_s: float):
+    """Times the reference's own CPU attention sublayer (oracle/_ref:
+    rmsnorm, mm_f16 for q, k, v, rmsnorm_head, apply_rope, the KV write,
+    launch_attn, mm_f16 for wo, the residual add) at KV 8192, fp32 cache, on
+    one layer (fp16 weights N(0, 0.02^2)); the oracle port when the
+    reference library is absent."""
+    import ctypes
+    import numpy as np
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import q3a_oracle as orc
+    use_ref = orc.ref_available()
+    rng = np.random.default_rng(1234)
+    f16 = lambda r, c: (rng.standard_normal((r, c), np.float32) * 0.02).astype(np.float16)  # noqa: E731
+    wq, wk, wv, wo = f16(HQ * HD, DIM), f16(KV_DIM, DIM), f16(KV_DIM, DIM), f16(DIM, HQ * HD)
+    kc, vc, _, _ = orc.make_cache(1234, 0, POS, HKV, HD, L_CTX)
+    x = rng.standard_normal(DIM, np.float32)
+    gains = np.ones(DIM, np.float32)
+    w = np.ones(HD, np.float32)
+    att = np.zeros(HQ * L_CTX, np.float32)
+    P = orc._ptr
+    R = orc.ref() if use_ref else None
+    xn = np.zeros(DIM, np.float32)
+    q = np.zeros(HQ * HD, np.float32)
+    k = np.zeros(KV_DIM, np.float32)
+    v = np.zeros(KV_DIM, np.float32)
+    xb = np.zeros(HQ * HD, np.float32)
+    xb2 = np.zeros(DIM, np.float32)
+
+    def mm(o, xin, wm):
+        if use_ref:
+            R.q3ref_mm_f16(P(o), P(xin), P(wm.view(np.uint16)), wm.shape[1], wm.shape[0])
+        else:
+            o[:] = orc.mm_f16(xin, wm)
+
+    def sublayer():
+        if use_ref:
+            R.q3ref_rmsnorm(P(xn), P(x), P(gains), DIM, 1e-6)
+        else:
+            xn[:] = orc.rmsnorm(x, gains)
+        mm(q, xn, wq)
+        mm(k, xn, wk)
+        mm(v, xn, wv)
+        if use_ref:
+            R.q3ref_rmsnorm_head(P(q), P(w), HQ, HD, 1e-6)
+            R.q3ref_rmsnorm_head(P(k), P(w), HKV, HD, 1e-6)
+            R.q3ref_rope(P(q), HQ, HD, POS, 5e6)
+            R.q3ref_rope(P(k), HKV, HD, POS, 5e6)
+            off = POS * KV_DIM * 4
+            R.q3ref_launch_kv_write(P(k), P(v), ctypes.c_void_p(kc.ctypes.data + off),
+                                    ctypes.c_void_p(vc.ctypes.data + off), KV_DIM)
+            R.q3ref_launch_attn(P(xb), P(q), P(kc), P(vc), P(att), 0, POS, HQ, HQ // HKV, HD,
+                                KV_DIM, L_CTX)
+        else:
+            xb[:] = orc.attn_block(q.copy(), k.copy(), v, w, w, kc, vc, 0, POS, HQ, HKV, HD, L_CTX)
+        mm(xb2, xb, wo)
+        x[:] = x + xb2
+
+    sublayer()  # warm
+    calls = 0
+    t0 = time.perf_counter()
+    while calls < n_calls_max and (time.perf_counter() - t0) < budget_s:
+        sublayer()
+        calls += 1
+    dt = time.perf_counter() - t0
+    threads = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
+    us = dt / calls * 1e6
+    bytes_ = proj_bytes(4) + wo_bytes() + 2 * (POS + 1) * KV_DIM * 4
+    return {"value": bytes_ / (us * 1e-6) / 1e9, "unit": "GB/s", "cores": threads,
+            "kind": "reference" if use_ref else "port", "us_per_layer": us,
+            "sample": f"{calls} calls of one fp32 attention sublayer at KV 8192 (the reference's "
+                      f"rmsnorm, mm_f16, rmsnorm_head, apply_rope, KV write, launch_attn; OpenMP, "
+                      f"{threads} threads available)"}
+
+
 def run_reference(args, world, rank):
     if rank != 0:
         return
@@ -1020,6 +1094,8 @@ def main():
             "clocks": sb["sublayer"]["clocks"], "gpu_launches": sb["sublayer"]["launches"]}
         line["gpu_launches"] += (sb["qkv"]["launches"] + sb["wo"]["launches"] +
                                  sb["sublayer"]["launches"])
+        if rank == 0 and world == 1 and not args.no_cpu:
+            line["sublayer"]["cpu_baseline"] = cpu_sublayer_sample(n_calls_max=20, budget_s=5.0)
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = cpu_reference_sample(n_calls_max=400, budget_s=15.0)
         line["cpu_baseline"] = {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")}
