@@ -1153,29 +1153,40 @@ __global__ void __launch_bounds__(DecCfg<KV, TC>::NTHREADS, 1)
                     const int key = row0 + tid;
                     const bool valid = got && tid < nld && key >= vlo && key < vhi;
                     float sc[GQA], mx[GQA];
+                    bool grow = false;  // a score above the running maximum + 8
 #pragma unroll
                     for (int q = 0; q < GQA; q++) {
                         sc[q] = valid ? __uint_as_float(r[q]) + __uint_as_float(r[q + GQA]) : -INFINITY;
                         mx[q] = sc[q];
+                        grow = grow || (sc[q] > mh[q] + 8.0f) || (valid && mh[q] == -INFINITY);
                     }
+                    // Lazy rescaling: while every score of the stage stays
+                    // within 2^8 of the running maximum (weights <= 256),
+                    // the maximum is kept and the stage's cross-warp maximum
+                    // is skipped; one vote, which also carries every thread's
+                    // wait status, picks the path
+                    const bool keep = named_bar_red_and(3, 128, got && !grow);
+                    if (!keep) {
 #pragma unroll
-                    for (int o = 16; o > 0; o >>= 1)
+                        for (int o = 16; o > 0; o >>= 1)
 #pragma unroll
-                        for (int q = 0; q < GQA; q++) mx[q] = fmaxf(mx[q], __shfl_xor_sync(FULL, mx[q], o));
-                    if (lane == 0)
+                            for (int q = 0; q < GQA; q++) mx[q] = fmaxf(mx[q], __shfl_xor_sync(FULL, mx[q], o));
+                        if (lane == 0)
 #pragma unroll
-                        for (int q = 0; q < GQA; q++) red[bf * 16 + warp * 4 + q] = mx[q];
-                    // the stage's maxima of all 4 warps; a failed wait anywhere
-                    // stops all 4 warps together
-                    if (!named_bar_red_and(3, 128, got)) {
-                        ok = false;
-                        break;
+                            for (int q = 0; q < GQA; q++) red[bf * 16 + warp * 4 + q] = mx[q];
+                        // the stage's maxima of all 4 warps; a failed wait
+                        // anywhere stops all 4 warps together
+                        if (!named_bar_red_and(3, 128, got)) {
+                            ok = false;
+                            break;
+                        }
                     }
                     float al[GQA];
 #pragma unroll
                     for (int q = 0; q < GQA; q++) {
-                        const float tmx = fmaxf(fmaxf(red[bf * 16 + q], red[bf * 16 + 4 + q]),
-                                                fmaxf(red[bf * 16 + 8 + q], red[bf * 16 + 12 + q]));
+                        const float tmx = keep ? -INFINITY
+                                               : fmaxf(fmaxf(red[bf * 16 + q], red[bf * 16 + 4 + q]),
+                                                       fmaxf(red[bf * 16 + 8 + q], red[bf * 16 + 12 + q]));
                         const float mn = fmaxf(mh[q], tmx);
                         const bool none = mn == -INFINITY;
                         al[q] = none ? 1.0f : exp2f(mh[q] - mn);
