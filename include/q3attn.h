@@ -189,11 +189,13 @@ int q3a_noalloc_check_error(void *cuda_stream);
  *   x [dim]: the normed layer input (s->xb of the reference);
  *   wq [n_heads*hd][dim], wk, wv [n_kv*hd][dim]: fp16 weights, row-major;
  *   q [n_heads*hd] (out): the normalised, rotated q;
- *   k, v [n_kv*hd] (out, may be NULL): the normalised, rotated k and v;
+ *   k [n_kv*hd] (out, may be NULL): the normalised, rotated k;
+ *   v [n_kv*hd] (out, may be NULL): v;
  *   xb [n_heads*hd] (out): the attention output.
  * Sums are fp32 in a fixed order (per thread, over a warp, then over the
- * consumer warps), not the reference's one sequential sum: results agree to
- * fp32 rounding and repeat bit for bit.  A context holding KV heads
+ * consumer warps), not the reference's one sequential sum: q, k and v agree
+ * with it to fp32 rounding and repeat bit for bit (xb repeats bit for bit in
+ * the deterministic schedule, q3a_set_deterministic).  A context holding KV heads
  * [b, b + n) (kv_head_begin/count) projects only their rows: q heads 4b ..
  * 4(b+n)-1 and KV heads b .. b+n-1, written at their places in the
  * full-width q, k, v (column-parallel), and attends over them (xb: their
